@@ -1,0 +1,397 @@
+#!/usr/bin/env python
+"""Benchmark: Q4_K_M bs=1 decode tok/s + matvec HBM GB/s vs B200 peak.
+
+Workload: Qwen3-0.6B-shaped decoder, Q4_K_M weights
+N(0, 0.02) from seed 0 (synthetic: no model files exist on these machines), a
+512-token uniform-random prompt (seed 1 + rank), 256 greedy tokens.  One
+"step" is the decode of those 256 tokens after the prompt (positions
+512..767); the prompt is prefilled once during setup.
+
+  value   decode tok/s over all ranks, device-timed with CUDA events on the
+          engine's stream, inputs resident in HBM
+  e2e     the same decode through generateLlamaWgsl (the public API): host
+          token in, 256 ids back to the host, wall-clock
+  roofline  bytes the step must read (weights + KV) per token / average
+          per-token kernel time, against MEASURED_PEAKS.json hbm_gbs
+  cpu_baseline  the CPU oracle (a C restatement of the reference's WGSL
+          kernels; the WebGPU runtime itself cannot run here) on a bounded
+          sample of the same model, all host cores
+
+Multi-GPU: independent replicas, one sequence per GPU, no collective on the
+data path (scaling "weak").  `--impl reference` times the CPU restatement of
+the reference on rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CONFIGS = {
+    # name: (synth spec, prompt tokens, generated tokens, sampling)
+    "qwen3-0.6b-q4_k_m": ("qwen3-0.6b", 512, 256, None),
+    "smollm2-135m-q4_k_m": ("smollm2-135m", 32, 128, None),
+    "qwen3-0.6b-q8_0": ("qwen3-0.6b-q8", 1920, 128, None),
+    "gemma3-270m-q4_k_m": ("gemma3-270m", 64, 256, {"temperature": 1.0, "topK": 64, "topP": 0.95, "seed": 0}),
+}
+MAX_CONTEXT = {"qwen3-0.6b": 2048, "qwen3-0.6b-q8": 2048, "smollm2-135m": 512, "gemma3-270m": 512}
+METRIC = "Q4_K_M bs=1 decode tok/s + matvec HBM GB/s vs B200 peak"
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def model_file(spec_name: str, rank: int, world: int, barrier) -> str:
+    from chonklm_b200.synth import SPECS, write_synthetic_gguf
+    d = os.environ.get("CK_BENCH_DIR", "/tmp/chonk_bench")
+    os.makedirs(d, exist_ok=True)
+    path = os.path.join(d, f"{spec_name}.gguf")
+    if rank == 0 and not os.path.exists(path):
+        t = time.time()
+        write_synthetic_gguf(SPECS[spec_name], path + ".tmp", seed=0)
+        os.replace(path + ".tmp", path)
+        log(f"[bench] wrote {path} in {time.time() - t:.1f}s")
+    barrier()
+    return path
+
+
+class Clocks:
+    """nvidia-smi samples during the timed region."""
+
+    def __init__(self, index: int):
+        self.index = index
+        self.rows = []
+        self.proc = None
+
+    def __enter__(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thr = threading.Thread(target=self._read, daemon=True)
+            self.thr.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([c.strip() for c in line.split(",")])
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in self.rows if len(r) > 2 and r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if len(r) > 2 and r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = set()
+        for r in self.rows:
+            for i, n in enumerate(names):
+                if len(r) > 5 + i and r[5 + i].lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(self.rows)}
+
+
+def cpu_baseline_sample(path: str, vocab: int, max_context: int, seconds: float = 12.0):
+    """Oracle (fp32, WGSL operation order, OpenMP over output rows) decode
+    tok/s on the host cores: a bounded sample of the same model."""
+    cores = os.cpu_count() or 1
+    os.environ.setdefault("OMP_NUM_THREADS", str(cores))
+    cores = int(os.environ["OMP_NUM_THREADS"])
+    from oracle import oracle
+    import numpy as np
+    m = oracle.OracleModel(path, vocab=vocab, max_context=max_context)
+    rng = np.random.default_rng(1)
+    for t in rng.integers(0, vocab, size=4).tolist():
+        m.run_token(t, False)
+    nid = int(rng.integers(0, vocab))
+    n = 0
+    t0 = time.perf_counter()
+    while n < 64:
+        nid = m.run_token(nid, True)
+        n += 1
+        if time.perf_counter() - t0 > seconds:
+            break
+    dt = time.perf_counter() - t0
+    m.close()
+    return {"value": n / dt, "unit": "tok/s", "cores": cores, "kind": "port",
+            "sample": f"{n} greedy decode steps of the same synthetic model at positions 4..{4 + n} "
+                      f"(C oracle, fp32, OpenMP over rows, {cores} threads)"}
+
+
+def run_reference(args, cfg_name, rank, world, barrier):
+    if rank != 0:
+        return
+    spec, prompt_len, gen, sampling = CONFIGS[cfg_name]
+    from chonklm_b200.synth import SPECS
+    path = model_file(spec, 0, 1, lambda: None)
+    vocab = SPECS[spec].vocab
+    cores = os.cpu_count() or 1
+    os.environ.setdefault("OMP_NUM_THREADS", str(cores))
+    cores = int(os.environ["OMP_NUM_THREADS"])
+    from oracle import oracle
+    import numpy as np
+    m = oracle.OracleModel(path, vocab=vocab, max_context=MAX_CONTEXT[spec])
+    rng = np.random.default_rng(1)
+    for t in rng.integers(0, vocab, size=4).tolist():
+        m.run_token(t, False)
+    nid = int(rng.integers(0, vocab))
+    per_step = 2   # tokens decoded per step: a bounded sample of the 256-token step
+    for _ in range(args.warmup):
+        for _ in range(per_step):
+            nid = m.run_token(nid, True)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        for _ in range(per_step):
+            nid = m.run_token(nid, True)
+        times.append(time.perf_counter() - t0)
+    tot = sum(times)
+    value = per_step * args.steps / tot
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * tot / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": cfg_name, "prompt": prompt_len, "generated": gen,
+                       "note": "reference WebGPU runtime unavailable on this box (no Node/Chromium/WebGPU "
+                               "adapter); CPU restatement of its WGSL kernels timed instead"},
+            "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": "port",
+                             "sample": f"{per_step} greedy decode steps per step at positions >= 4, "
+                                       f"C oracle fp32, {cores} OpenMP threads"},
+            "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    m.close()
+
+
+def matvec_report(path, peak):
+    """Per-shape matvec GB/s (algorithmic bytes: weights + x + y) for the
+    Q4_K / Q6_K tensors of the model, each launch streaming from HBM."""
+    from chonklm_b200 import _lib
+    from chonklm_b200.gguf import ByteSource, fetch_gguf_header
+    src = ByteSource(path)
+    g = fetch_gguf_header(src)
+    out = {}
+    for name in ["blk.1.attn_q.weight", "blk.1.ffn_up.weight", "blk.1.ffn_down.weight", "blk.0.ffn_down.weight",
+                 "token_embd.weight"]:
+        t = g.tensor_map.get(name)
+        if t is None:
+            continue
+        data = src.read(g.data_offset + t.offset, t.n_bytes)
+        k, n = t.shape[0], t.shape[1]
+        us = _lib.bench_matvec(t.type, data, k, n, reps=100 if n > 100000 else 400)
+        byts = t.n_bytes + 4 * k + 4 * n
+        gbs = byts / (us * 1e-6) / 1e9
+        out[name] = {"type": t.type, "k": k, "n": n, "us": round(us, 2), "GBps": round(gbs, 1),
+                     "frac": round(gbs / peak, 3)}
+    return out
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="qwen3-0.6b-q4_k_m", choices=list(CONFIGS))
+    ap.add_argument("--mode", type=int, default=0, help="0 megakernel, 1 per-phase CUDA graph")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-matvec", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    import torch
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        backend = "nccl" if torch.cuda.is_available() else "gloo"
+        if backend == "nccl":
+            torch.cuda.set_device(local)
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=600))
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    if args.impl == "reference":
+        run_reference(args, args.config, rank, world, barrier)
+        if dist is not None:
+            dist.destroy_process_group()
+        return
+
+    torch.cuda.set_device(local)
+    spec, prompt_len, gen, sampling = CONFIGS[args.config]
+    from chonklm_b200 import _lib
+    from chonklm_b200.registry import ModelDef
+    from chonklm_b200.runtime import generateLlamaWgsl, loadLlamaWgslModel
+    from chonklm_b200.synth import SPECS
+    import numpy as np
+
+    path = model_file(spec, rank, world, barrier)
+    S = SPECS[spec]
+    mdef = ModelDef(id=args.config, label=args.config, vocab=S.vocab, layers=S.layers, kvHeads=S.kv_heads,
+                    headDim=S.head_dim, maxContext=MAX_CONTEXT[spec], gguf=path, eosIds=[])
+    t = time.time()
+    loaded = loadLlamaWgslModel(mdef, device=local)
+    log(f"[bench r{rank}] loaded in {time.time() - t:.1f}s")
+    eng = loaded.engine.dev
+    eng.set_mode(args.mode)
+    stream = torch.cuda.current_stream()
+    eng.set_stream(stream.cuda_stream)
+    prompt = np.random.default_rng(1 + rank).integers(0, S.vocab, size=prompt_len).tolist()
+    samp = None
+    if sampling:
+        samp, _ = _lib.make_sampling(sampling["temperature"], sampling["topP"], sampling["topK"], 1.0,
+                                     sampling["seed"], 0)
+    nid = eng.prefill(prompt, True, samp)
+    ids0 = eng.decode(nid, 2, samp)           # stores the first id at the prompt end
+    eng.truncate(prompt_len)
+    w0, kv0 = eng.step_bytes()
+    eng.truncate(prompt_len)
+
+    def one_step():
+        eng.truncate(prompt_len)
+        ev0 = torch.cuda.Event(enable_timing=True)
+        ev1 = torch.cuda.Event(enable_timing=True)
+        ev0.record(stream)
+        eng.enqueue_decode_steps(gen)
+        ev1.record(stream)
+        return ev0, ev1
+
+    for _ in range(args.warmup):
+        one_step()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    evs = []
+    with Clocks(local) as clk:
+        for _ in range(args.steps):
+            evs.append(one_step())
+        torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    eng.sync()
+    step_ms = [a.elapsed_time(b) for a, b in evs]
+    tot_ms = sum(step_ms)
+    # KV bytes per token averaged over the step's positions
+    eng.truncate(prompt_len + gen - 1)
+    w1, kv1 = eng.step_bytes()
+    bytes_per_token = w0 + 0.5 * (kv0 + kv1)
+
+    # ---- e2e through generateLlamaWgsl -------------------------------------
+    e2e_times = []
+    e2e_io = []
+    opts = {"maxNewTokens": gen}
+    if sampling:
+        opts.update(sampling)
+    for i in range(args.warmup + args.steps):
+        loaded.cachedTokenIds = list(prompt)
+        loaded.cachedNextId = nid
+        eng.truncate(prompt_len)
+        io0 = eng.io_bytes()
+        t0 = time.perf_counter()
+        res = generateLlamaWgsl(loaded, prompt, opts)
+        dt = time.perf_counter() - t0
+        io1 = eng.io_bytes()
+        if i >= args.warmup:
+            e2e_times.append(dt)
+            e2e_io.append((io1[0] - io0[0], io1[1] - io0[1]))
+        assert len(res["ids"]) == gen, len(res["ids"])
+
+    # ---- reduce over ranks ------------------------------------------------------
+    vals = torch.tensor([tot_ms, sum(e2e_times)], dtype=torch.float64, device="cuda")
+    if dist is not None:
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    max_ms, max_e2e = float(vals[0]), float(vals[1])
+    tokens = gen * args.steps * world
+    value = tokens / (max_ms / 1000.0)
+    e2e_value = tokens / max_e2e
+
+    out = None
+    if rank == 0:
+        peak, peak_kind = peaks()
+        per_tok_s = (tot_ms / 1000.0) / (gen * args.steps)
+        achieved = bytes_per_token / per_tok_s / 1e9
+        traffic = None
+        try:
+            with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+                traffic = json.load(f).get(args.config)
+        except Exception:
+            traffic = None
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            try:
+                cpu = cpu_baseline_sample(path, S.vocab, MAX_CONTEXT[spec])
+            except Exception as e:  # reported, not fatal
+                cpu = {"value": None, "error": str(e)}
+        mv = None
+        if not args.no_matvec:
+            try:
+                mv = matvec_report(path, peak)
+            except Exception as e:
+                mv = {"error": str(e)}
+        # megakernel: one cooperative launch per token; graph mode: one per phase
+        launches_per_token = 1 if args.mode == 0 else 1 + 5 * S.layers + 4 + 1
+        out = {
+            "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(tot_ms / args.steps, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8-dp4a/fp32", "data": "synthetic",
+            "config": {"workload": args.config, "prompt": prompt_len, "generated": gen,
+                       "weights": "N(0,0.02) seed 0, Q4_K_M mixture", "kv_cache": "fp16",
+                       "mode": "megakernel" if args.mode == 0 else "graph",
+                       "l2": "inputs larger than L2 (weights %.0f MB per token > 126 MB L2)" % (w0 / 1e6),
+                       "parallelism": f"replicas x{world}"},
+            "e2e": {"value": round(e2e_value, 2), "unit": "tok/s",
+                    "h2d_bytes_per_step": int(statistics.mean(x[0] for x in e2e_io)),
+                    "d2h_bytes_per_step": int(statistics.mean(x[1] for x in e2e_io))},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": traffic,
+                         "peak_source": peak_kind,
+                         "bytes_per_token": round(bytes_per_token), "us_per_token": round(per_tok_s * 1e6, 2)},
+            "cpu_baseline": cpu,
+            "matvec": mv,
+            "clocks": clk.summary(),
+            "gpu_launches": int(launches_per_token * gen * args.steps),
+            "decode_ids_head": ids0[:2],
+        }
+        print(json.dumps(out), flush=True)
+    loaded.engine.dispose()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

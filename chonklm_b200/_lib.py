@@ -1,0 +1,270 @@
+"""ctypes binding of libchonk_b200.so (the C ABI in include/chonk_b200.h).
+
+There is no CPU fallback: if the library cannot be loaded, or the CUDA call
+fails, every entry point raises.  The library is built in-tree by
+`chonklm_b200.build` (nvcc, sm_100a).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from typing import Optional, Sequence, Tuple
+
+import numpy as np
+
+from . import build as _build
+
+CK_OK = 0
+CK_EINVAL = -1
+CK_ECUDA = -2
+CK_ESTATE = -3
+CK_ECONTEXT = -4
+CK_EDEVICE = -5
+CK_ENOMEM = -6
+
+CK_ARCH_LLAMA = 0
+CK_ARCH_GEMMA3 = 1
+CK_KV_F16 = 0
+CK_KV_F32 = 1
+CK_MAX_LAYERS = 128
+
+MODE_MEGAKERNEL = 0
+MODE_GRAPH = 1
+
+
+class CkError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"{msg} (ck code {code})")
+        self.code = code
+
+
+class ContextExhausted(CkError):
+    pass
+
+
+class ck_model_cfg(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int32) for n in ("hidden", "intermediate", "vocab", "layers", "heads", "kv_heads",
+                                              "head_dim", "context_length")] + \
+               [("norm_eps", ctypes.c_float), ("qk_norm_eps", ctypes.c_float), ("embedding_scale", ctypes.c_float)] + \
+               [(n, ctypes.c_int32) for n in ("arch", "rope_interleaved", "qk_norm", "kv_dtype")] + \
+               [("layer_rope_theta", ctypes.c_uint32 * CK_MAX_LAYERS),
+                ("layer_window", ctypes.c_uint32 * CK_MAX_LAYERS)]
+
+
+class ck_sampling(ctypes.Structure):
+    _fields_ = [("temperature", ctypes.c_double), ("top_p", ctypes.c_double), ("top_k", ctypes.c_int32),
+                ("repetition_penalty", ctypes.c_double), ("penalized_ids", ctypes.POINTER(ctypes.c_uint32)),
+                ("n_penalized", ctypes.c_int32), ("philox_seed", ctypes.c_uint64),
+                ("philox_offset", ctypes.c_uint64)]
+
+
+_lock = threading.Lock()
+_lib = None
+
+
+def lib():
+    """Load (building first if sources changed) libchonk_b200.so."""
+    global _lib
+    with _lock:
+        if _lib is None:
+            path = _build.LIB
+            if _build.needs_build():
+                try:
+                    path = _build.build()
+                except Exception as e:  # no nvcc / compile error: fail loudly
+                    if not os.path.exists(path):
+                        raise RuntimeError(f"libchonk_b200.so is missing and could not be built: {e}") from e
+            L = ctypes.CDLL(path)
+            P, I, U, S, D = ctypes.c_void_p, ctypes.c_int, ctypes.c_uint32, ctypes.c_size_t, ctypes.c_double
+            pp = ctypes.POINTER
+            L.ck_create.argtypes = [pp(ck_model_cfg), I, pp(P)]
+            L.ck_upload_tensor.argtypes = [P, ctypes.c_char_p, I, pp(ctypes.c_int64), I, P, S]
+            L.ck_finalize.argtypes = [P]
+            L.ck_destroy.argtypes = [P]
+            L.ck_run_token.argtypes = [P, U, I, pp(ck_sampling), pp(U)]
+            L.ck_prefill.argtypes = [P, pp(U), I, I, pp(ck_sampling), pp(U)]
+            L.ck_decode.argtypes = [P, U, I, pp(ck_sampling), pp(U), I, pp(U), pp(I)]
+            L.ck_get_logits.argtypes = [P, P, S]
+            L.ck_get_candidates.argtypes = [P, P, P, S]
+            L.ck_reset.argtypes = [P]
+            L.ck_position.argtypes = [P, pp(I)]
+            L.ck_truncate.argtypes = [P, I]
+            L.ck_last_error.argtypes = [P]
+            L.ck_last_error.restype = ctypes.c_char_p
+            L.ck_global_error.argtypes = []
+            L.ck_global_error.restype = ctypes.c_char_p
+            L.ck_set_stream.argtypes = [P, P]
+            L.ck_set_mode.argtypes = [P, I]
+            L.ck_enqueue_decode_steps.argtypes = [P, I]
+            L.ck_sync.argtypes = [P]
+            L.ck_step_bytes.argtypes = [P, pp(D), pp(D)]
+            L.ck_dequant.argtypes = [I, P, S, I, I, P, I]
+            L.ck_matvec.argtypes = [I, P, S, I, I, P, P, I]
+            L.ck_bench_matvec.argtypes = [I, P, S, I, I, I, pp(D), I]
+            L.ck_abi_info.argtypes = [pp(I), pp(I)]
+            L.ck_io_bytes.argtypes = [P, pp(ctypes.c_uint64), pp(ctypes.c_uint64)]
+            _lib = L
+    return _lib
+
+
+def _check(rc: int, h=None) -> None:
+    if rc == CK_OK:
+        return
+    L = lib()
+    msg = (L.ck_last_error(h) if h else L.ck_global_error()) or b""
+    msg = msg.decode("utf-8", "replace")
+    if rc == CK_ECONTEXT:
+        raise ContextExhausted(rc, msg)
+    raise CkError(rc, msg)
+
+
+def _u32p(a: np.ndarray):
+    return a.ctypes.data_as(ctypes.POINTER(ctypes.c_uint32))
+
+
+def make_sampling(temperature: float = 0.0, top_p: float = 1.0, top_k: int = 0, repetition_penalty: float = 1.0,
+                  seed: int = 0, offset: int = 0, penalized_ids: Optional[Sequence[int]] = None):
+    s = ck_sampling()
+    s.temperature = float(temperature or 0.0)
+    s.top_p = float(1.0 if top_p is None else top_p)
+    s.top_k = int(top_k or 0)
+    s.repetition_penalty = float(1.0 if repetition_penalty is None else repetition_penalty)
+    s.philox_seed = int(seed) & (2 ** 64 - 1)
+    s.philox_offset = int(offset)
+    keep = None
+    if penalized_ids is not None:
+        keep = np.ascontiguousarray(np.asarray(list(penalized_ids), dtype=np.uint32))
+        s.penalized_ids = _u32p(keep) if keep.size else ctypes.cast(ctypes.c_void_p(0), ctypes.POINTER(ctypes.c_uint32))
+        s.n_penalized = int(keep.size)
+    return s, keep
+
+
+class Engine:
+    """One device engine (LlamaWgslEngine's device side)."""
+
+    def __init__(self, cfg: ck_model_cfg, device: int = 0):
+        self._L = lib()
+        h = ctypes.c_void_p()
+        _check(self._L.ck_create(ctypes.byref(cfg), device, ctypes.byref(h)))
+        self.h = h
+        self.cfg = cfg
+
+    def upload(self, name: str, ggml_type: int, shape: Sequence[int], data: bytes) -> None:
+        shp = (ctypes.c_int64 * len(shape))(*shape)
+        buf = np.frombuffer(data, dtype=np.uint8) if not isinstance(data, np.ndarray) else data
+        buf = np.ascontiguousarray(buf)
+        _check(self._L.ck_upload_tensor(self.h, name.encode(), ggml_type, shp, len(shape), buf.ctypes.data,
+                                        buf.nbytes), self.h)
+
+    def finalize(self) -> None:
+        _check(self._L.ck_finalize(self.h), self.h)
+
+    def run_token(self, token: int, need_logits: bool, sampling=None) -> int:
+        out = ctypes.c_uint32(0)
+        _check(self._L.ck_run_token(self.h, int(token), 1 if need_logits else 0,
+                                    ctypes.byref(sampling) if sampling is not None else None, ctypes.byref(out)),
+               self.h)
+        return int(out.value)
+
+    def prefill(self, tokens: Sequence[int], need_logits_last: bool = True, sampling=None) -> int:
+        arr = np.ascontiguousarray(np.asarray(list(tokens), dtype=np.uint32))
+        out = ctypes.c_uint32(0)
+        _check(self._L.ck_prefill(self.h, _u32p(arr), int(arr.size), 1 if need_logits_last else 0,
+                                  ctypes.byref(sampling) if sampling is not None else None, ctypes.byref(out)),
+               self.h)
+        return int(out.value)
+
+    def decode(self, first: int, max_new: int, sampling=None, eos_ids: Sequence[int] = ()) -> list:
+        eos = np.ascontiguousarray(np.asarray(list(eos_ids) or [0], dtype=np.uint32))
+        out = np.zeros(max(1, max_new), dtype=np.uint32)
+        n = ctypes.c_int(0)
+        _check(self._L.ck_decode(self.h, int(first), int(max_new),
+                                 ctypes.byref(sampling) if sampling is not None else None, _u32p(eos),
+                                 len(eos_ids), _u32p(out), ctypes.byref(n)), self.h)
+        return out[:n.value].tolist()
+
+    def logits(self) -> np.ndarray:
+        out = np.empty(self.cfg.vocab, dtype=np.float32)
+        _check(self._L.ck_get_logits(self.h, out.ctypes.data, out.size), self.h)
+        return out
+
+    def candidates(self) -> Tuple[np.ndarray, np.ndarray]:
+        g = (self.cfg.vocab + 255) // 256
+        v = np.empty(g, dtype=np.float32)
+        i = np.empty(g, dtype=np.uint32)
+        _check(self._L.ck_get_candidates(self.h, v.ctypes.data, i.ctypes.data, g), self.h)
+        return v, i
+
+    def reset(self) -> None:
+        _check(self._L.ck_reset(self.h), self.h)
+
+    @property
+    def position(self) -> int:
+        p = ctypes.c_int(0)
+        _check(self._L.ck_position(self.h, ctypes.byref(p)), self.h)
+        return p.value
+
+    def truncate(self, pos: int) -> None:
+        _check(self._L.ck_truncate(self.h, int(pos)), self.h)
+
+    def set_stream(self, stream_handle: int) -> None:
+        _check(self._L.ck_set_stream(self.h, ctypes.c_void_p(stream_handle)), self.h)
+
+    def set_mode(self, mode: int) -> None:
+        _check(self._L.ck_set_mode(self.h, int(mode)), self.h)
+
+    def enqueue_decode_steps(self, n: int) -> None:
+        _check(self._L.ck_enqueue_decode_steps(self.h, int(n)), self.h)
+
+    def sync(self) -> None:
+        _check(self._L.ck_sync(self.h), self.h)
+
+    def step_bytes(self) -> Tuple[float, float]:
+        w, k = ctypes.c_double(), ctypes.c_double()
+        _check(self._L.ck_step_bytes(self.h, ctypes.byref(w), ctypes.byref(k)), self.h)
+        return w.value, k.value
+
+    def io_bytes(self) -> Tuple[int, int]:
+        a, b = ctypes.c_uint64(0), ctypes.c_uint64(0)
+        _check(self._L.ck_io_bytes(self.h, ctypes.byref(a), ctypes.byref(b)), self.h)
+        return a.value, b.value
+
+    def close(self) -> None:
+        if getattr(self, "h", None):
+            self._L.ck_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def dequant(ggml_type: int, data: bytes, k: int, n: int, device: int = 0) -> np.ndarray:
+    buf = np.ascontiguousarray(np.frombuffer(data, dtype=np.uint8))
+    out = np.empty((n, k), dtype=np.float32)
+    _check(lib().ck_dequant(ggml_type, buf.ctypes.data, buf.nbytes, k, n, out.ctypes.data, device))
+    return out
+
+
+def matvec(ggml_type: int, data: bytes, k: int, n: int, x: np.ndarray, device: int = 0) -> np.ndarray:
+    buf = np.ascontiguousarray(np.frombuffer(data, dtype=np.uint8))
+    xx = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.empty(n, dtype=np.float32)
+    _check(lib().ck_matvec(ggml_type, buf.ctypes.data, buf.nbytes, k, n, xx.ctypes.data, y.ctypes.data, device))
+    return y
+
+
+def bench_matvec(ggml_type: int, data: bytes, k: int, n: int, reps: int = 200, device: int = 0) -> float:
+    buf = np.ascontiguousarray(np.frombuffer(data, dtype=np.uint8))
+    us = ctypes.c_double(0)
+    _check(lib().ck_bench_matvec(ggml_type, buf.ctypes.data, buf.nbytes, k, n, reps, ctypes.byref(us), device))
+    return us.value
+
+
+def abi_info() -> Tuple[int, int]:
+    a, b = ctypes.c_int(0), ctypes.c_int(0)
+    lib().ck_abi_info(ctypes.byref(a), ctypes.byref(b))
+    return a.value, b.value

@@ -1,0 +1,988 @@
+// chonk_b200 engine: device buffers, phase schedule, CUDA graphs and the C ABI.
+//
+// Host-side twin of LlamaWgslEngine (llama-wgsl-runtime.ts:619-1220): it owns
+// every device buffer (weights, KV cache, scratch) and frees them in
+// ck_destroy, as `dispose` does (:1152-1215).
+#include <cuda_runtime.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <map>
+#include <string>
+#include <vector>
+
+#include "../../include/chonk_b200.h"
+#include "ck_ops.cuh"
+
+namespace {
+
+thread_local std::string g_err;
+
+int set_global(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return code;
+}
+
+struct Weight {
+  Lay L;
+  int n = 0;
+  uint8_t* dev = nullptr;
+  bool present = false;
+};
+
+struct LayerW {
+  Weight q, k, v, o, gate, up, down;
+  float *attn_norm = nullptr, *post_norm = nullptr, *pre_ffn = nullptr, *post_ffn = nullptr;
+  float *q_norm = nullptr, *k_norm = nullptr;
+};
+
+size_t elem_kv(const ck_model_cfg& c) { return c.kv_dtype == CK_KV_F32 ? 4 : 2; }
+
+}  // namespace
+
+struct ck_engine {
+  ck_model_cfg cfg;
+  int device = 0;
+  int sms = 0;
+  cudaStream_t own = nullptr, stream = nullptr;
+  std::string err;
+  bool finalized = false;
+  int mode = 0;  // 0 megakernel, 1 graph of per-phase kernels
+
+  std::vector<LayerW> L;
+  Weight emb, head;
+  float* final_norm = nullptr;
+  std::vector<void*> allocs;
+
+  // device state
+  CkState* st = nullptr;
+  CkDev D;
+  float *resA = nullptr, *resB = nullptr, *tmp = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *attn = nullptr,
+        *g = nullptr, *u = nullptr, *part = nullptr;
+  unsigned* counters = nullptr;
+  uint8_t* kv = nullptr;
+  size_t kv_bytes = 0;
+  int smax = 1;
+
+  // schedules
+  std::vector<Phase> ph_logits, ph_prefill;
+  Phase *d_logits = nullptr, *d_prefill = nullptr;
+  int mega_grid = 0;
+  cudaGraphExec_t gx_logits[2] = {nullptr, nullptr}, gx_prefill[2] = {nullptr, nullptr};
+
+  // host mirrors
+  int pos = 0;
+  unsigned long long io_h2d = 0, io_d2h = 0;  // bytes copied by step calls
+  CkState shadow;
+  uint8_t* pinned = nullptr;  // staging for small copies
+
+  int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    err = buf;
+    return code;
+  }
+};
+
+#define CKC(h, call)                                                                                    \
+  do {                                                                                                  \
+    cudaError_t e_ = (call);                                                                            \
+    if (e_ != cudaSuccess) return (h)->fail(CK_ECUDA, "%s: %s (%s:%d)", #call, cudaGetErrorString(e_), \
+                                           __FILE__, __LINE__);                                          \
+  } while (0)
+
+#define CKG(call)                                                                                       \
+  do {                                                                                                  \
+    cudaError_t e_ = (call);                                                                            \
+    if (e_ != cudaSuccess) return set_global(CK_ECUDA, "%s: %s", #call, cudaGetErrorString(e_));       \
+  } while (0)
+
+namespace {
+
+// Host<->device copies of the step calls, counted for the e2e report.
+cudaError_t h2d(ck_engine* h, void* dst, const void* src, size_t n) {
+  h->io_h2d += n;
+  return cudaMemcpyAsync(dst, src, n, cudaMemcpyHostToDevice, h->stream);
+}
+cudaError_t d2h(ck_engine* h, void* dst, const void* src, size_t n) {
+  h->io_d2h += n;
+  return cudaMemcpyAsync(dst, src, n, cudaMemcpyDeviceToHost, h->stream);
+}
+
+template <class T>
+int dalloc(ck_engine* h, T** p, size_t bytes) {
+  void* q = nullptr;
+  cudaError_t e = cudaMalloc(&q, bytes ? bytes : 16);
+  if (e != cudaSuccess) return h->fail(CK_ENOMEM, "cudaMalloc(%zu): %s", bytes, cudaGetErrorString(e));
+  h->allocs.push_back(q);
+  *p = (T*)q;
+  return CK_OK;
+}
+
+// Raw GGUF blocks (host) -> device streaming layout.
+int upload_quant(ck_engine* h, Weight& w, int type, int k, int n, const void* bytes, size_t nbytes,
+                 const char* name) {
+  if (!ck_type_ok(type))
+    return h->fail(CK_EINVAL, "Llama WGSL tensor %s is not a supported GGUF quantized tensor (type %d)", name, type);
+  if (k % ck_block_weights(type) != 0)
+    return h->fail(CK_EINVAL, "GGML tensor type %d requires %d-element rows, %s has %d", type,
+                   ck_block_weights(type), name, k);
+  size_t raw = (size_t)n * (k / ck_block_weights(type)) * ck_block_bytes(type);
+  if (nbytes != raw) return h->fail(CK_EINVAL, "%s: %zu bytes, expected %zu", name, nbytes, raw);
+  Lay L = make_lay(type, k);
+  uint8_t* tmp = nullptr;
+  CKC(h, cudaMalloc(&tmp, raw));
+  cudaError_t e = cudaMemcpyAsync(tmp, bytes, raw, cudaMemcpyHostToDevice, h->own);
+  if (e != cudaSuccess) { cudaFree(tmp); return h->fail(CK_ECUDA, "upload %s: %s", name, cudaGetErrorString(e)); }
+  uint8_t* dst = nullptr;
+  int rc = dalloc(h, &dst, (size_t)L.row_bytes * n);
+  if (rc) { cudaFree(tmp); return rc; }
+  cudaMemsetAsync(dst, 0, (size_t)L.row_bytes * n, h->own);
+  long long total = (long long)n * L.nb;
+  k_relayout<<<(unsigned)((total + 255) / 256), 256, 0, h->own>>>(tmp, dst, L, n);
+  e = cudaStreamSynchronize(h->own);
+  cudaFree(tmp);
+  if (e != cudaSuccess) return h->fail(CK_ECUDA, "relayout %s: %s", name, cudaGetErrorString(e));
+  w.L = L;
+  w.n = n;
+  w.dev = dst;
+  w.present = true;
+  return CK_OK;
+}
+
+float f16_bits_to_f32(uint16_t b) {
+  // exact, subnormals kept (f16ToF32, llama-wgsl-runtime.ts:1837-1844)
+  int s = (b >> 15) & 1, e = (b >> 10) & 0x1f, f = b & 0x3ff;
+  float v;
+  if (e == 0) v = ldexpf((float)f, -24);
+  else if (e == 31) v = f ? NAN : INFINITY;
+  else v = ldexpf((float)(1024 + f), e - 25);
+  return s ? -v : v;
+}
+
+int upload_norm(ck_engine* h, float** dst, int type, int n_expected, int64_t ne, const void* bytes, size_t nbytes,
+                const char* name) {
+  if (type != CK_GGML_F32 && type != CK_GGML_F16)
+    return h->fail(CK_EINVAL, "Llama WGSL tensor %s is %d, expected float32/float16", name, type);
+  if (ne != n_expected) return h->fail(CK_EINVAL, "%s: %lld elements, expected %d", name, (long long)ne, n_expected);
+  if (nbytes != (size_t)ne * (type == CK_GGML_F32 ? 4 : 2))
+    return h->fail(CK_EINVAL, "%s: %zu bytes for %lld elements", name, nbytes, (long long)ne);
+  std::vector<float> f(ne);
+  if (type == CK_GGML_F32) memcpy(f.data(), bytes, nbytes);
+  else {
+    const uint16_t* p = (const uint16_t*)bytes;
+    for (int64_t i = 0; i < ne; i++) f[i] = f16_bits_to_f32(p[i]);
+  }
+  if (!*dst) {
+    int rc = dalloc(h, dst, (size_t)ne * 4);
+    if (rc) return rc;
+  }
+  CKC(h, cudaMemcpy(*dst, f.data(), (size_t)ne * 4, cudaMemcpyHostToDevice));
+  return CK_OK;
+}
+
+Pro pro_norm(const float* a, const float* w, float eps) {
+  Pro p{};
+  p.kind = PRO_NORM; p.a = a; p.w0 = w; p.eps = eps;
+  return p;
+}
+Pro pro_gemma(const float* sub, const float* wpost, const float* rin, float* rout, const float* wpre, float eps) {
+  Pro p{};
+  p.kind = PRO_GEMMA; p.a = sub; p.w1 = wpost; p.rin = rin; p.rout = rout; p.w0 = wpre; p.eps = eps;
+  return p;
+}
+MvSeg seg(const Weight& w, float* out, const float* add) {
+  MvSeg s{};
+  s.w = w.dev; s.out = out; s.add = add; s.L = w.L; s.n = w.n;
+  return s;
+}
+
+int mv_groups(const MvPhase& m) {
+  int upl = (m.k + 1023) >> 10;
+  int R = upl <= 1 ? 4 : (upl == 2 ? 2 : 1);
+  int g = 0;
+  for (int i = 0; i < m.nseg; i++) g += (m.seg[i].n + R - 1) / R;
+  return g;
+}
+
+Phase mk_mv(ck_engine* h, const Pro& pro, int k, std::initializer_list<MvSeg> segs) {
+  Phase p;
+  memset(&p, 0, sizeof p);
+  p.kind = PH_MATVEC;
+  p.mv.pro = pro;
+  p.mv.k = k;
+  p.mv.nseg = 0;
+  for (const MvSeg& s : segs) p.mv.seg[p.mv.nseg++] = s;
+  int groups = mv_groups(p.mv);
+  int grid = (groups + CK_WARPS - 1) / CK_WARPS;
+  int cap = h->sms * 4;
+  p.grid = grid < 1 ? 1 : (grid > cap ? cap : grid);
+  return p;
+}
+
+void build_schedule(ck_engine* h, bool logits, std::vector<Phase>& out) {
+  const ck_model_cfg& c = h->cfg;
+  const int H = c.hidden, hd = c.head_dim, qd = c.heads * hd;
+  const bool gemma = c.arch == CK_ARCH_GEMMA3;
+  out.clear();
+  Phase p;
+  memset(&p, 0, sizeof p);
+  p.kind = PH_EMBED;
+  p.grid = (H + CK_THREADS - 1) / CK_THREADS;
+  if (p.grid < 8) p.grid = 8;
+  p.em.w = h->emb.dev;
+  p.em.L = h->emb.L;
+  p.em.out = h->resA;
+  p.em.scale = c.embedding_scale;
+  p.em.need_logits = logits ? 1 : 0;
+  out.push_back(p);
+
+  float* cur = h->resA;    // residual before the layer's first add
+  float* other = h->resB;
+  for (int i = 0; i < c.layers; i++) {
+    const LayerW& W = h->L[i];
+    Pro pq = (!gemma || i == 0) ? pro_norm(cur, W.attn_norm, c.norm_eps)
+                                : pro_gemma(h->tmp, h->L[i - 1].post_ffn, cur, other, W.attn_norm, c.norm_eps);
+    if (gemma && i > 0) std::swap(cur, other);
+    out.push_back(mk_mv(h, pq, H, {seg(W.q, h->q, nullptr), seg(W.k, h->k, nullptr), seg(W.v, h->v, nullptr)}));
+
+    Phase a;
+    memset(&a, 0, sizeof a);
+    a.kind = PH_ATTN;
+    a.at.q = h->q; a.at.k = h->k; a.at.v = h->v;
+    a.at.qw = c.qk_norm ? W.q_norm : nullptr;
+    a.at.kw = c.qk_norm ? W.k_norm : nullptr;
+    size_t per = (size_t)c.kv_heads * c.context_length * hd * elem_kv(c);
+    a.at.kc = h->kv + (size_t)(2 * i) * per;
+    a.at.vc = h->kv + (size_t)(2 * i + 1) * per;
+    a.at.out = h->attn;
+    a.at.part = h->part;
+    a.at.counter = h->counters;
+    a.at.heads = c.heads; a.at.kvh = c.kv_heads; a.at.hd = hd; a.at.ctx = c.context_length;
+    a.at.window = (int)c.layer_window[i];
+    a.at.interleaved = c.rope_interleaved;
+    a.at.kv_f32 = c.kv_dtype == CK_KV_F32;
+    a.at.smax = h->smax;
+    a.at.theta = c.layer_rope_theta[i];
+    a.at.eps = c.qk_norm_eps;
+    a.at.scale = (float)(1.0 / sqrt((double)hd));  // ATTN_SCALE constant (:1711)
+    a.grid = c.kv_heads * h->smax;
+    out.push_back(a);
+
+    Pro pc{};
+    pc.kind = PRO_COPY;
+    pc.a = h->attn;
+    if (!gemma) {
+      // o_proj + residual add; addRmsNorm's norm moves into the gate/up prologue
+      out.push_back(mk_mv(h, pc, qd, {seg(W.o, cur, cur)}));
+      out.push_back(mk_mv(h, pro_norm(cur, W.post_norm, c.norm_eps), H,
+                          {seg(W.gate, h->g, nullptr), seg(W.up, h->u, nullptr)}));
+      Pro ps{};
+      ps.kind = PRO_SILU; ps.a = h->g; ps.b = h->u;
+      out.push_back(mk_mv(h, ps, c.intermediate, {seg(W.down, cur, cur)}));
+    } else {
+      out.push_back(mk_mv(h, pc, qd, {seg(W.o, h->tmp, nullptr)}));
+      out.push_back(mk_mv(h, pro_gemma(h->tmp, W.post_norm, cur, other, W.pre_ffn, c.norm_eps), H,
+                          {seg(W.gate, h->g, nullptr), seg(W.up, h->u, nullptr)}));
+      std::swap(cur, other);
+      Pro pg{};
+      pg.kind = PRO_GELU; pg.a = h->g; pg.b = h->u;
+      out.push_back(mk_mv(h, pg, c.intermediate, {seg(W.down, h->tmp, nullptr)}));
+    }
+  }
+  if (logits) {
+    Pro pf = !gemma ? pro_norm(cur, h->final_norm, c.norm_eps)
+                    : pro_gemma(h->tmp, h->L[c.layers - 1].post_ffn, cur, other, h->final_norm, c.norm_eps);
+    out.push_back(mk_mv(h, pf, H, {seg(h->head, h->D.logits, nullptr)}));
+    Phase a1;
+    memset(&a1, 0, sizeof a1);
+    a1.kind = PH_ARGMAX1;
+    a1.grid = (c.vocab + 255) / 256;
+    if (a1.grid > h->sms * 4) a1.grid = h->sms * 4;
+    out.push_back(a1);
+    Phase a2;
+    memset(&a2, 0, sizeof a2);
+    a2.kind = PH_ARGMAX2;
+    a2.grid = 1;
+    out.push_back(a2);
+    Phase s;
+    memset(&s, 0, sizeof s);
+    s.kind = PH_SAMPLE;
+    s.grid = 1;
+    out.push_back(s);
+  }
+  Phase f;
+  memset(&f, 0, sizeof f);
+  f.kind = PH_FINISH;
+  f.grid = 1;
+  f.need_logits = logits ? 1 : 0;
+  out.push_back(f);
+}
+
+int enqueue_phases(ck_engine* h, const std::vector<Phase>& ph, const Phase* dph, int mode, cudaStream_t s) {
+  if (mode == 1) {
+    for (size_t i = 0; i < ph.size(); i++) {
+      if (ph[i].kind == PH_MATVEC) k_mv<<<ph[i].grid, CK_THREADS, 0, s>>>(dph + i, h->D);
+      else if (ph[i].kind == PH_ATTN) k_attn<<<ph[i].grid, CK_THREADS, 0, s>>>(dph + i, h->D);
+      else k_misc<<<ph[i].grid, CK_THREADS, 0, s>>>(dph + i, h->D);
+    }
+    CKC(h, cudaGetLastError());
+    return CK_OK;
+  }
+  CKC(h, cudaMemsetAsync(&h->st->bar, 0, sizeof(uint32_t), s));
+  int nph = (int)ph.size();
+  void* args[] = {(void*)&dph, (void*)&nph, (void*)&h->D};
+  CKC(h, cudaLaunchCooperativeKernel((const void*)k_mega, dim3(h->mega_grid), dim3(CK_THREADS), args, 0, s));
+  return CK_OK;
+}
+
+int capture(ck_engine* h, const std::vector<Phase>& ph, const Phase* dph, int mode, cudaGraphExec_t* out) {
+  cudaStream_t s = h->own;
+  cudaGraph_t g = nullptr;
+  CKC(h, cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+  int rc = enqueue_phases(h, ph, dph, mode, s);
+  cudaError_t e = cudaStreamEndCapture(s, &g);
+  if (rc) { if (g) cudaGraphDestroy(g); return rc; }
+  if (e != cudaSuccess) return h->fail(CK_ECUDA, "graph capture: %s", cudaGetErrorString(e));
+  e = cudaGraphInstantiate(out, g, 0);
+  cudaGraphDestroy(g);
+  if (e != cudaSuccess) return h->fail(CK_ECUDA, "graph instantiate: %s", cudaGetErrorString(e));
+  return CK_OK;
+}
+
+int launch_step(ck_engine* h, bool logits) {
+  cudaGraphExec_t gx = logits ? h->gx_logits[h->mode] : h->gx_prefill[h->mode];
+  if (gx) {
+    CKC(h, cudaGraphLaunch(gx, h->stream));
+    return CK_OK;
+  }
+  return enqueue_phases(h, logits ? h->ph_logits : h->ph_prefill, logits ? h->d_logits : h->d_prefill, h->mode,
+                        h->stream);
+}
+
+// Host option block -> device (sampling.ts SamplingOptions + penalty plumbing
+// of LlamaWgslEngine.argmax, llama-wgsl-runtime.ts:1647-1665).
+int set_params(ck_engine* h, const ck_sampling* s, int chain, uint64_t draw_override, bool use_override) {
+  CkState& p = h->shadow;
+  double temp = s ? s->temperature : 0.0, top_p = s ? s->top_p : 1.0, pen = s ? s->repetition_penalty : 1.0;
+  int top_k = s ? s->top_k : 0;
+  p.temperature = temp;
+  p.top_p = top_p;
+  p.top_k = top_k < 0 ? 0 : top_k;
+  p.pen_d = pen;
+  p.pen_milli = (uint32_t)floor(pen * 1000.0 + 0.5);
+  p.sampling = (temp > 0.0 || top_p < 1.0 || p.top_k > 0) ? 1 : 0;
+  p.chain = chain;
+  p.seed = s ? s->philox_seed : 0ull;
+  p.draw = use_override ? (uint32_t)draw_override : (s ? (uint32_t)s->philox_offset : 0u);
+  p.abort_flag = 0;
+  p.bar = 0;
+  p.pen_src = 0;
+  p.pen_count = 0;
+  if (s && s->penalized_ids) {
+    int n = s->n_penalized;
+    if (n < 0) n = 0;
+    // penalizedTokenIds.slice(-contextLength) (:1651-1653)
+    int keep = n > h->cfg.context_length ? h->cfg.context_length : n;
+    const uint32_t* ids = s->penalized_ids + (n - keep);
+    p.pen_src = 1;
+    p.pen_count = keep;
+    if (keep > 0) CKC(h, h2d(h, h->D.pen_list, ids, (size_t)keep * 4));
+  }
+  size_t off = offsetof(CkState, draw);
+  memcpy(h->pinned, (const uint8_t*)&p + off, sizeof(CkState) - off);
+  CKC(h, h2d(h, (uint8_t*)h->st + off, h->pinned, sizeof(CkState) - off));
+  return CK_OK;
+}
+
+int check_device(ck_engine* h) {
+  int* e = (int*)(h->pinned + 256);
+  CKC(h, d2h(h, e, &h->st->err, 4));
+  CKC(h, cudaStreamSynchronize(h->stream));
+  if (*e) {
+    int bits = *e;
+    cudaMemsetAsync(&h->st->err, 0, 4, h->stream);
+    cudaMemsetAsync(&h->st->abort_flag, 0, 4, h->stream);
+    cudaStreamSynchronize(h->stream);
+    if (bits & CK_DERR_TOKEN) return h->fail(CK_EDEVICE, "token id outside embedding table");
+    if (bits & CK_DERR_BARRIER) return h->fail(CK_EDEVICE, "device grid barrier timed out");
+    return h->fail(CK_EDEVICE, "device error bits 0x%x", bits);
+  }
+  return CK_OK;
+}
+
+int set_pos_dev(ck_engine* h, int pos) {
+  int* p = (int*)(h->pinned + 320);
+  *p = pos;
+  CKC(h, h2d(h, &h->st->pos, p, 4));
+  CKC(h, cudaStreamSynchronize(h->stream));
+  h->pos = pos;
+  return CK_OK;
+}
+
+}  // namespace
+
+// ============================================================================
+extern "C" {
+
+const char* ck_global_error(void) { return g_err.c_str(); }
+
+void ck_abi_info(int* sizeof_cfg, int* sizeof_sampling) {
+  if (sizeof_cfg) *sizeof_cfg = (int)sizeof(ck_model_cfg);
+  if (sizeof_sampling) *sizeof_sampling = (int)sizeof(ck_sampling);
+}
+const char* ck_last_error(ck_engine* h) { return h ? h->err.c_str() : g_err.c_str(); }
+
+int ck_create(const ck_model_cfg* cfg, int device, ck_engine** out) {
+  if (!cfg || !out) return set_global(CK_EINVAL, "ck_create: null argument");
+  const ck_model_cfg& c = *cfg;
+  if (c.arch != CK_ARCH_LLAMA && c.arch != CK_ARCH_GEMMA3) return set_global(CK_EINVAL, "unsupported arch %d", c.arch);
+  if (c.layers <= 0 || c.layers > CK_MAX_LAYERS) return set_global(CK_EINVAL, "layers %d out of range", c.layers);
+  if (c.hidden <= 0 || c.hidden % 32 || c.hidden > CK_KMAX) return set_global(CK_EINVAL, "hidden %d unsupported", c.hidden);
+  if (c.intermediate <= 0 || c.intermediate % 32 || c.intermediate > CK_KMAX)
+    return set_global(CK_EINVAL, "intermediate %d unsupported", c.intermediate);
+  if (c.head_dim != 64 && c.head_dim != 128 && c.head_dim != 256)
+    return set_global(CK_EINVAL, "head_dim %d unsupported (64/128/256)", c.head_dim);
+  if (c.heads <= 0 || c.kv_heads <= 0 || c.heads % c.kv_heads)
+    return set_global(CK_EINVAL, "heads %d / kv_heads %d invalid", c.heads, c.kv_heads);
+  int G = c.heads / c.kv_heads;
+  if (G > CK_GMAX || G * c.head_dim > 1024)
+    return set_global(CK_EINVAL, "GQA group %d x head_dim %d unsupported", G, c.head_dim);
+  if (c.heads * c.head_dim > CK_KMAX) return set_global(CK_EINVAL, "q dim too large");
+  if (c.vocab <= 0 || (c.vocab + 255) / 256 > CK_SAMPLE_MAX) return set_global(CK_EINVAL, "vocab %d unsupported", c.vocab);
+  if (c.context_length <= 0) return set_global(CK_EINVAL, "context_length %d", c.context_length);
+  CKG(cudaSetDevice(device));
+  ck_engine* h = new ck_engine();
+  h->cfg = c;
+  h->device = device;
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) { delete h; return set_global(CK_ECUDA, "no device"); }
+  h->sms = prop.multiProcessorCount;
+  if (cudaStreamCreateWithFlags(&h->own, cudaStreamNonBlocking) != cudaSuccess) {
+    delete h;
+    return set_global(CK_ECUDA, "stream create failed");
+  }
+  h->stream = h->own;
+  h->L.resize(c.layers);
+  memset(&h->shadow, 0, sizeof h->shadow);
+  if (cudaHostAlloc((void**)&h->pinned, 4096, cudaHostAllocDefault) != cudaSuccess) {
+    cudaStreamDestroy(h->own);
+    delete h;
+    return set_global(CK_ECUDA, "pinned alloc failed");
+  }
+  const char* m = getenv("CK_MODE");
+  if (m && atoi(m) == 1) h->mode = 1;
+  *out = h;
+  return CK_OK;
+}
+
+int ck_upload_tensor(ck_engine* h, const char* name, int ggml_type, const int64_t* shape, int ndim, const void* bytes,
+                     size_t nbytes) {
+  if (!h || !name || !shape || ndim < 1 || !bytes) return set_global(CK_EINVAL, "ck_upload_tensor: bad argument");
+  if (h->finalized) return h->fail(CK_ESTATE, "ck_upload_tensor after ck_finalize");
+  CKC(h, cudaSetDevice(h->device));
+  const ck_model_cfg& c = h->cfg;
+  int64_t ne0 = shape[0], ne1 = ndim > 1 ? shape[1] : 1;
+  for (int i = 2; i < ndim; i++) ne1 *= shape[i];
+  std::string s(name);
+  const int H = c.hidden, qd = c.heads * c.head_dim, kvd = c.kv_heads * c.head_dim, I = c.intermediate;
+  auto quant = [&](Weight& w, int k, int n) -> int {
+    if (ne0 != k || ne1 != n)
+      return h->fail(CK_EINVAL, "%s: shape [%lld, %lld], expected [%d, %d]", name, (long long)ne0, (long long)ne1, k, n);
+    return upload_quant(h, w, ggml_type, k, n, bytes, nbytes, name);
+  };
+  if (s == "token_embd.weight") return quant(h->emb, H, c.vocab);
+  if (s == "output.weight") return quant(h->head, H, c.vocab);
+  if (s == "output_norm.weight") return upload_norm(h, &h->final_norm, ggml_type, H, ne0 * ne1, bytes, nbytes, name);
+  int layer = -1, used = 0;
+  char rest[128];
+  if (sscanf(name, "blk.%d.%127s%n", &layer, rest, &used) == 2 && layer >= 0 && layer < c.layers) {
+    LayerW& W = h->L[layer];
+    std::string r(rest);
+    bool gemma = c.arch == CK_ARCH_GEMMA3;
+    if (r == "attn_q.weight") return quant(W.q, H, qd);
+    if (r == "attn_k.weight") return quant(W.k, H, kvd);
+    if (r == "attn_v.weight") return quant(W.v, H, kvd);
+    if (r == "attn_output.weight") return quant(W.o, qd, H);
+    if (r == "ffn_gate.weight") return quant(W.gate, H, I);
+    if (r == "ffn_up.weight") return quant(W.up, H, I);
+    if (r == "ffn_down.weight") return quant(W.down, I, H);
+    if (r == "attn_norm.weight") return upload_norm(h, &W.attn_norm, ggml_type, H, ne0 * ne1, bytes, nbytes, name);
+    if (r == "attn_q_norm.weight")
+      return upload_norm(h, &W.q_norm, ggml_type, c.head_dim, ne0 * ne1, bytes, nbytes, name);
+    if (r == "attn_k_norm.weight")
+      return upload_norm(h, &W.k_norm, ggml_type, c.head_dim, ne0 * ne1, bytes, nbytes, name);
+    // post_attention_layernorm alias: ffn_norm (llama) / post_attention_norm (gemma3), :346-352
+    if (!gemma && r == "ffn_norm.weight")
+      return upload_norm(h, &W.post_norm, ggml_type, H, ne0 * ne1, bytes, nbytes, name);
+    if (gemma && r == "post_attention_norm.weight")
+      return upload_norm(h, &W.post_norm, ggml_type, H, ne0 * ne1, bytes, nbytes, name);
+    if (gemma && r == "ffn_norm.weight")
+      return upload_norm(h, &W.pre_ffn, ggml_type, H, ne0 * ne1, bytes, nbytes, name);
+    if (gemma && r == "post_ffw_norm.weight")
+      return upload_norm(h, &W.post_ffn, ggml_type, H, ne0 * ne1, bytes, nbytes, name);
+  }
+  return CK_OK;  // tensors the decode step does not read are ignored
+}
+
+int ck_finalize(ck_engine* h) {
+  if (!h) return set_global(CK_EINVAL, "null engine");
+  if (h->finalized) return CK_OK;
+  CKC(h, cudaSetDevice(h->device));
+  const ck_model_cfg& c = h->cfg;
+  bool gemma = c.arch == CK_ARCH_GEMMA3;
+  if (!h->emb.present) return h->fail(CK_EINVAL, "Llama WGSL manifest missing tensor token_embd.weight");
+  if (!h->final_norm) return h->fail(CK_EINVAL, "Llama WGSL manifest missing tensor output_norm.weight");
+  if (!h->head.present) h->head = h->emb;  // tied LM head (:345)
+  for (int i = 0; i < c.layers; i++) {
+    LayerW& W = h->L[i];
+    if (!W.q.present || !W.k.present || !W.v.present)
+      return h->fail(CK_EINVAL, "Llama WGSL layer %d is missing attention projection weights", i);
+    if (!W.o.present) return h->fail(CK_EINVAL, "layer %d is missing attn_output.weight", i);
+    if (!W.gate.present || !W.up.present || !W.down.present)
+      return h->fail(CK_EINVAL, "Llama WGSL layer %d is missing MLP projection weights", i);
+    if (!W.attn_norm || !W.post_norm) return h->fail(CK_EINVAL, "layer %d is missing norm weights", i);
+    if (gemma && (!W.pre_ffn || !W.post_ffn || !W.q_norm || !W.k_norm))
+      return h->fail(CK_EINVAL, "Gemma WGSL layer is missing required weights");
+    if (c.qk_norm && (!W.q_norm || !W.k_norm)) return h->fail(CK_EINVAL, "layer %d is missing q/k norm", i);
+  }
+  int rc;
+  const int H = c.hidden, hd = c.head_dim;
+  int G = c.heads / c.kv_heads;
+  h->smax = (2 * h->sms + c.kv_heads - 1) / c.kv_heads;
+  if (h->smax > 64) h->smax = 64;
+  if (h->smax < 1) h->smax = 1;
+  if ((rc = dalloc(h, &h->st, sizeof(CkState)))) return rc;
+  CKC(h, cudaMemset(h->st, 0, sizeof(CkState)));
+  h->D.st = h->st;
+  h->D.vocab = c.vocab;
+  h->D.ctx = c.context_length;
+  if ((rc = dalloc(h, &h->D.tokens, (size_t)c.context_length * 4))) return rc;
+  if ((rc = dalloc(h, &h->D.pen_list, (size_t)c.context_length * 4))) return rc;
+  if ((rc = dalloc(h, &h->D.pen_mask, (size_t)((c.vocab + 31) / 32) * 4))) return rc;
+  if ((rc = dalloc(h, &h->D.logits, (size_t)c.vocab * 4))) return rc;
+  int groups = (c.vocab + 255) / 256;
+  if ((rc = dalloc(h, &h->D.cand_val, (size_t)groups * 4))) return rc;
+  if ((rc = dalloc(h, &h->D.cand_idx, (size_t)groups * 4))) return rc;
+  CKC(h, cudaMemset(h->D.tokens, 0, (size_t)c.context_length * 4));
+  CKC(h, cudaMemset(h->D.pen_mask, 0, (size_t)((c.vocab + 31) / 32) * 4));
+  if ((rc = dalloc(h, &h->resA, (size_t)H * 4))) return rc;
+  if ((rc = dalloc(h, &h->resB, (size_t)H * 4))) return rc;
+  if ((rc = dalloc(h, &h->tmp, (size_t)H * 4))) return rc;
+  if ((rc = dalloc(h, &h->q, (size_t)c.heads * hd * 4))) return rc;
+  if ((rc = dalloc(h, &h->k, (size_t)c.kv_heads * hd * 4))) return rc;
+  if ((rc = dalloc(h, &h->v, (size_t)c.kv_heads * hd * 4))) return rc;
+  if ((rc = dalloc(h, &h->attn, (size_t)c.heads * hd * 4))) return rc;
+  if ((rc = dalloc(h, &h->g, (size_t)c.intermediate * 4))) return rc;
+  if ((rc = dalloc(h, &h->u, (size_t)c.intermediate * 4))) return rc;
+  if ((rc = dalloc(h, &h->part, (size_t)c.kv_heads * h->smax * G * (hd + 2) * 4))) return rc;
+  if ((rc = dalloc(h, &h->counters, (size_t)c.kv_heads * 4))) return rc;
+  CKC(h, cudaMemset(h->counters, 0, (size_t)c.kv_heads * 4));
+  h->kv_bytes = (size_t)c.layers * 2 * c.kv_heads * c.context_length * hd * elem_kv(c);
+  if ((rc = dalloc(h, &h->kv, h->kv_bytes))) return rc;
+  CKC(h, cudaMemset(h->kv, 0, h->kv_bytes));
+
+  build_schedule(h, true, h->ph_logits);
+  build_schedule(h, false, h->ph_prefill);
+  if ((rc = dalloc(h, &h->d_logits, h->ph_logits.size() * sizeof(Phase)))) return rc;
+  if ((rc = dalloc(h, &h->d_prefill, h->ph_prefill.size() * sizeof(Phase)))) return rc;
+  CKC(h, cudaMemcpy(h->d_logits, h->ph_logits.data(), h->ph_logits.size() * sizeof(Phase), cudaMemcpyHostToDevice));
+  CKC(h, cudaMemcpy(h->d_prefill, h->ph_prefill.data(), h->ph_prefill.size() * sizeof(Phase),
+                    cudaMemcpyHostToDevice));
+  int per_sm = 0;
+  CKC(h, cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_mega, CK_THREADS, 0));
+  int want = 1;
+  const char* w = getenv("CK_MEGA_CTAS_PER_SM");
+  if (w) want = atoi(w);
+  if (want < 1) want = 1;
+  if (per_sm < 1) return h->fail(CK_ECUDA, "megakernel does not fit on an SM");
+  h->mega_grid = h->sms * (want < per_sm ? want : per_sm);
+  for (int m = 0; m < 2; m++) {
+    if ((rc = capture(h, h->ph_logits, h->d_logits, m, &h->gx_logits[m]))) {
+      cudaGetLastError();
+      h->gx_logits[m] = nullptr;  // fall back to direct launches
+    }
+    if ((rc = capture(h, h->ph_prefill, h->d_prefill, m, &h->gx_prefill[m]))) {
+      cudaGetLastError();
+      h->gx_prefill[m] = nullptr;
+    }
+  }
+  h->err.clear();
+  CKC(h, cudaDeviceSynchronize());
+  h->finalized = true;
+  h->pos = 0;
+  return CK_OK;
+}
+
+int ck_set_stream(ck_engine* h, void* stream) {
+  if (!h) return set_global(CK_EINVAL, "null engine");
+  h->stream = stream ? (cudaStream_t)stream : h->own;
+  return CK_OK;
+}
+
+int ck_set_mode(ck_engine* h, int mode) {
+  if (!h) return set_global(CK_EINVAL, "null engine");
+  if (mode != 0 && mode != 1) return h->fail(CK_EINVAL, "mode %d", mode);
+  h->mode = mode;
+  return CK_OK;
+}
+
+static int pre_step(ck_engine* h) {
+  if (!h) return set_global(CK_EINVAL, "null engine");
+  if (!h->finalized) return h->fail(CK_ESTATE, "engine not finalized");
+  if (h->pos >= h->cfg.context_length)
+    return h->fail(CK_ECONTEXT, "Llama WGSL context exhausted at %d tokens", h->cfg.context_length);
+  CKC(h, cudaSetDevice(h->device));
+  return CK_OK;
+}
+
+int ck_run_token(ck_engine* h, uint32_t token, int need_logits, const ck_sampling* s, uint32_t* out_id) {
+  int rc = pre_step(h);
+  if (rc) return rc;
+  if (token >= (uint32_t)h->cfg.vocab) return h->fail(CK_EINVAL, "token id %u outside embedding table", token);
+  if ((rc = set_params(h, s, 0, 0, false))) return rc;
+  uint32_t* tk = (uint32_t*)(h->pinned + 384);
+  *tk = token;
+  CKC(h, h2d(h, h->D.tokens + h->pos, tk, 4));
+  if ((rc = launch_step(h, need_logits != 0))) return rc;
+  uint32_t* res = (uint32_t*)(h->pinned + 448);
+  if (need_logits) CKC(h, d2h(h, res, &h->st->next_token, 4));
+  if ((rc = check_device(h))) return rc;
+  h->pos += 1;
+  if (out_id) *out_id = need_logits ? *res : 0u;
+  return CK_OK;
+}
+
+int ck_prefill(ck_engine* h, const uint32_t* tokens, int n, int need_logits_last, const ck_sampling* s,
+               uint32_t* out_id) {
+  int rc = pre_step(h);
+  if (rc) return rc;
+  if (n <= 0 || !tokens) return h->fail(CK_EINVAL, "ck_prefill: empty prompt");
+  if (h->pos + n > h->cfg.context_length)
+    return h->fail(CK_ECONTEXT, "Llama WGSL context exhausted at %d tokens", h->cfg.context_length);
+  for (int i = 0; i < n; i++)
+    if (tokens[i] >= (uint32_t)h->cfg.vocab) return h->fail(CK_EINVAL, "token id %u outside embedding table", tokens[i]);
+  if ((rc = set_params(h, s, 0, 0, false))) return rc;
+  CKC(h, h2d(h, h->D.tokens + h->pos, tokens, (size_t)n * 4));
+  for (int i = 0; i < n; i++)
+    if ((rc = launch_step(h, need_logits_last && i == n - 1))) return rc;
+  uint32_t* res = (uint32_t*)(h->pinned + 448);
+  if (need_logits_last) CKC(h, d2h(h, res, &h->st->next_token, 4));
+  if ((rc = check_device(h))) return rc;
+  h->pos += n;
+  if (out_id) *out_id = need_logits_last ? *res : 0u;
+  return CK_OK;
+}
+
+int ck_decode(ck_engine* h, uint32_t first, int max_new, const ck_sampling* s, const uint32_t* eos_ids, int n_eos,
+              uint32_t* out_ids, int* n_out) {
+  if (!h) return set_global(CK_EINVAL, "null engine");
+  if (!h->finalized) return h->fail(CK_ESTATE, "engine not finalized");
+  if (!out_ids || !n_out) return h->fail(CK_EINVAL, "ck_decode: null output");
+  *n_out = 0;
+  if (max_new <= 0) return CK_OK;
+  auto is_eos = [&](uint32_t id) {
+    for (int i = 0; i < n_eos; i++) if (eos_ids[i] == id) return true;
+    return false;
+  };
+  out_ids[0] = first;
+  int produced = 1;
+  if (is_eos(first) || max_new == 1) { *n_out = 1; return CK_OK; }
+  int rc = pre_step(h);
+  if (rc) return rc;
+  if (first >= (uint32_t)h->cfg.vocab) return h->fail(CK_EINVAL, "token id %u outside embedding table", first);
+  uint64_t draw0 = s ? s->philox_offset : 0;
+  if ((rc = set_params(h, s, 1, draw0, true))) return rc;
+  uint32_t* tk = (uint32_t*)(h->pinned + 384);
+  *tk = first;
+  CKC(h, h2d(h, h->D.tokens + h->pos, tk, 4));
+  const int CH = 16;
+  uint32_t* back = (uint32_t*)(h->pinned + 1024);
+  bool done = false;
+  while (!done) {
+    int remaining = max_new - produced;
+    int room = h->cfg.context_length - h->pos;
+    int steps = remaining < CH ? remaining : CH;
+    if (steps > room) steps = room;
+    if (steps <= 0) break;
+    for (int i = 0; i < steps; i++)
+      if ((rc = launch_step(h, true))) return rc;
+    // ids produced by these steps: tokens[pos+1 .. pos+steps] (the last one
+    // may sit at ctx, which is not stored: read it from next_token instead)
+    int stored = steps;
+    if (h->pos + steps >= h->cfg.context_length) stored = h->cfg.context_length - 1 - h->pos;
+    if (stored > 0)
+      CKC(h, d2h(h, back, h->D.tokens + h->pos + 1, (size_t)stored * 4));
+    CKC(h, d2h(h, back + stored, &h->st->next_token, 4));
+    if ((rc = check_device(h))) return rc;
+    if (stored < steps) back[steps - 1] = back[stored];
+    int used = steps;
+    for (int i = 0; i < steps; i++) {
+      out_ids[produced++] = back[i];
+      if (is_eos(back[i]) || produced >= max_new) { used = i + 1; done = true; break; }
+    }
+    if (used < steps) {  // ran past an EOS: rewind the position (KV beyond is dead)
+      if ((rc = set_pos_dev(h, h->pos + used))) return rc;
+    } else {
+      h->pos += steps;
+    }
+    if (h->pos >= h->cfg.context_length) break;
+  }
+  *n_out = produced;
+  return CK_OK;
+}
+
+int ck_enqueue_decode_steps(ck_engine* h, int n) {
+  int rc = pre_step(h);
+  if (rc) return rc;
+  if (h->pos + n > h->cfg.context_length) return h->fail(CK_ECONTEXT, "context exhausted");
+  // greedy, chained: each step's id becomes the next step's input
+  if ((rc = set_params(h, nullptr, 1, 0, true))) return rc;
+  for (int i = 0; i < n; i++)
+    if ((rc = launch_step(h, true))) return rc;
+  h->pos += n;
+  return CK_OK;
+}
+
+int ck_sync(ck_engine* h) {
+  if (!h) return set_global(CK_EINVAL, "null engine");
+  return check_device(h);
+}
+
+int ck_get_logits(ck_engine* h, float* out, size_t n) {
+  if (!h || !out) return set_global(CK_EINVAL, "bad argument");
+  if (n > (size_t)h->cfg.vocab) n = h->cfg.vocab;
+  CKC(h, cudaStreamSynchronize(h->stream));
+  CKC(h, cudaMemcpy(out, h->D.logits, n * 4, cudaMemcpyDeviceToHost));
+  return CK_OK;
+}
+
+int ck_get_candidates(ck_engine* h, float* val, uint32_t* idx, size_t n) {
+  if (!h || !val || !idx) return set_global(CK_EINVAL, "bad argument");
+  size_t g = (size_t)(h->cfg.vocab + 255) / 256;
+  if (n > g) n = g;
+  CKC(h, cudaStreamSynchronize(h->stream));
+  CKC(h, cudaMemcpy(val, h->D.cand_val, n * 4, cudaMemcpyDeviceToHost));
+  CKC(h, cudaMemcpy(idx, h->D.cand_idx, n * 4, cudaMemcpyDeviceToHost));
+  return CK_OK;
+}
+
+int ck_reset(ck_engine* h) {
+  if (!h) return set_global(CK_EINVAL, "null engine");
+  if (!h->finalized) return h->fail(CK_ESTATE, "engine not finalized");
+  CKC(h, cudaSetDevice(h->device));
+  CKC(h, cudaMemsetAsync(h->kv, 0, h->kv_bytes, h->stream));  // clearBuffer (:1014-1017)
+  return set_pos_dev(h, 0);
+}
+
+int ck_position(ck_engine* h, int* pos) {
+  if (!h || !pos) return set_global(CK_EINVAL, "bad argument");
+  *pos = h->pos;
+  return CK_OK;
+}
+
+int ck_truncate(ck_engine* h, int pos) {
+  if (!h) return set_global(CK_EINVAL, "null engine");
+  if (pos < 0 || pos > h->pos) return h->fail(CK_EINVAL, "truncate to %d outside [0, %d]", pos, h->pos);
+  return set_pos_dev(h, pos);
+}
+
+int ck_step_bytes(ck_engine* h, double* weight_bytes, double* kv_bytes) {
+  if (!h || !weight_bytes || !kv_bytes) return set_global(CK_EINVAL, "bad argument");
+  const ck_model_cfg& c = h->cfg;
+  double wb = 0;
+  auto add = [&](const Weight& w) { wb += (double)w.L.row_bytes * w.n; };
+  for (const LayerW& W : h->L) {
+    add(W.q); add(W.k); add(W.v); add(W.o); add(W.gate); add(W.up); add(W.down);
+  }
+  add(h->head);
+  double kb = 0;
+  for (int i = 0; i < c.layers; i++) {
+    int p = h->pos;
+    int start = (c.layer_window[i] && p + 1 > (int)c.layer_window[i]) ? p + 1 - (int)c.layer_window[i] : 0;
+    kb += 2.0 * c.kv_heads * (double)(p - start + 1) * c.head_dim * elem_kv(c);
+  }
+  *weight_bytes = wb;
+  *kv_bytes = kb;
+  return CK_OK;
+}
+
+int ck_io_bytes(ck_engine* h, uint64_t* h2d_bytes, uint64_t* d2h_bytes) {
+  if (!h || !h2d_bytes || !d2h_bytes) return set_global(CK_EINVAL, "bad argument");
+  *h2d_bytes = h->io_h2d;
+  *d2h_bytes = h->io_d2h;
+  return CK_OK;
+}
+
+int ck_destroy(ck_engine* h) {
+  if (!h) return CK_OK;
+  cudaSetDevice(h->device);
+  cudaStreamSynchronize(h->own);
+  for (int m = 0; m < 2; m++) {
+    if (h->gx_logits[m]) cudaGraphExecDestroy(h->gx_logits[m]);
+    if (h->gx_prefill[m]) cudaGraphExecDestroy(h->gx_prefill[m]);
+  }
+  for (void* p : h->allocs) cudaFree(p);
+  if (h->pinned) cudaFreeHost(h->pinned);
+  if (h->own) cudaStreamDestroy(h->own);
+  delete h;
+  return CK_OK;
+}
+
+// ---- parity / measurement helpers --------------------------------------------
+namespace {
+int prep_weight(ck_engine* h, int type, const void* bytes, size_t nbytes, int k, int n, Weight& w) {
+  return upload_quant(h, w, type, k, n, bytes, nbytes, "tensor");
+}
+
+int make_tmp(int device, ck_engine** out) {
+  CKG(cudaSetDevice(device));
+  ck_engine* h = new ck_engine();
+  h->device = device;
+  cudaDeviceProp prop;
+  CKG(cudaGetDeviceProperties(&prop, device));
+  h->sms = prop.multiProcessorCount;
+  CKG(cudaStreamCreateWithFlags(&h->own, cudaStreamNonBlocking));
+  h->stream = h->own;
+  *out = h;
+  return CK_OK;
+}
+
+void free_tmp(ck_engine* h) {
+  cudaStreamSynchronize(h->own);
+  for (void* p : h->allocs) cudaFree(p);
+  cudaStreamDestroy(h->own);
+  delete h;
+}
+}  // namespace
+
+int ck_dequant(int ggml_type, const void* bytes, size_t nbytes, int k, int n, float* out, int device) {
+  if (!bytes || !out || k <= 0 || n <= 0) return set_global(CK_EINVAL, "ck_dequant: bad argument");
+  ck_engine* h;
+  int rc = make_tmp(device, &h);
+  if (rc) return rc;
+  Weight w;
+  if ((rc = prep_weight(h, ggml_type, bytes, nbytes, k, n, w))) {
+    std::string m = h->err;
+    free_tmp(h);
+    return set_global(rc, "%s", m.c_str());
+  }
+  float* d = nullptr;
+  if ((rc = dalloc(h, &d, (size_t)k * n * 4))) { free_tmp(h); return set_global(rc, "alloc"); }
+  long long total = (long long)k * n;
+  k_dequant<<<(unsigned)((total + 255) / 256), 256, 0, h->own>>>(w.dev, w.L, n, d);
+  cudaError_t e = cudaMemcpyAsync(out, d, (size_t)total * 4, cudaMemcpyDeviceToHost, h->own);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(h->own);
+  free_tmp(h);
+  if (e != cudaSuccess) return set_global(CK_ECUDA, "ck_dequant: %s", cudaGetErrorString(e));
+  return CK_OK;
+}
+
+static int matvec_setup(ck_engine* h, int type, const void* bytes, size_t nbytes, int k, int n, Weight& w, float** x,
+                        float** y, Phase** dph, Phase& ph) {
+  int rc;
+  if (k > CK_KMAX || k % 32) return h->fail(CK_EINVAL, "k %d unsupported", k);
+  if ((rc = prep_weight(h, type, bytes, nbytes, k, n, w))) return rc;
+  if ((rc = dalloc(h, x, (size_t)k * 4))) return rc;
+  if ((rc = dalloc(h, y, (size_t)n * 4))) return rc;
+  Pro p{};
+  p.kind = PRO_COPY;
+  p.a = *x;
+  ph = mk_mv(h, p, k, {seg(w, *y, nullptr)});
+  if ((rc = dalloc(h, dph, sizeof(Phase)))) return rc;
+  CKC(h, cudaMemcpy(*dph, &ph, sizeof(Phase), cudaMemcpyHostToDevice));
+  return CK_OK;
+}
+
+int ck_matvec(int ggml_type, const void* bytes, size_t nbytes, int k, int n, const float* x, float* y, int device) {
+  if (!bytes || !x || !y) return set_global(CK_EINVAL, "ck_matvec: bad argument");
+  ck_engine* h;
+  int rc = make_tmp(device, &h);
+  if (rc) return rc;
+  Weight w;
+  float *dx, *dy;
+  Phase* dph;
+  Phase ph;
+  if ((rc = matvec_setup(h, ggml_type, bytes, nbytes, k, n, w, &dx, &dy, &dph, ph))) {
+    std::string m = h->err;
+    free_tmp(h);
+    return set_global(rc, "%s", m.c_str());
+  }
+  CkDev D;
+  memset(&D, 0, sizeof D);
+  cudaMemcpyAsync(dx, x, (size_t)k * 4, cudaMemcpyHostToDevice, h->own);
+  k_mv<<<ph.grid, CK_THREADS, 0, h->own>>>(dph, D);
+  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) e = cudaMemcpyAsync(y, dy, (size_t)n * 4, cudaMemcpyDeviceToHost, h->own);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(h->own);
+  free_tmp(h);
+  if (e != cudaSuccess) return set_global(CK_ECUDA, "ck_matvec: %s", cudaGetErrorString(e));
+  return CK_OK;
+}
+
+int ck_bench_matvec(int ggml_type, const void* bytes, size_t nbytes, int k, int n, int reps, double* us_per,
+                    int device) {
+  if (!bytes || !us_per || reps <= 0) return set_global(CK_EINVAL, "ck_bench_matvec: bad argument");
+  ck_engine* h;
+  int rc = make_tmp(device, &h);
+  if (rc) return rc;
+  Weight w;
+  float *dx, *dy;
+  Phase* dph;
+  Phase ph;
+  if ((rc = matvec_setup(h, ggml_type, bytes, nbytes, k, n, w, &dx, &dy, &dph, ph))) {
+    std::string m = h->err;
+    free_tmp(h);
+    return set_global(rc, "%s", m.c_str());
+  }
+  CkDev D;
+  memset(&D, 0, sizeof D);
+  cudaMemsetAsync(dx, 0, (size_t)k * 4, h->own);
+  // Rotate over enough weight copies to exceed L2 so every launch streams
+  // from HBM.
+  size_t wbytes = (size_t)w.L.row_bytes * n;
+  int copies = (int)((256ull << 20) / (wbytes ? wbytes : 1)) + 1;
+  if (copies > 64) copies = 64;
+  std::vector<Phase*> phs;
+  std::vector<uint8_t*> ws;
+  phs.push_back(dph);
+  for (int c = 1; c < copies; c++) {
+    uint8_t* wc = nullptr;
+    if (dalloc(h, &wc, wbytes)) break;
+    cudaMemcpyAsync(wc, w.dev, wbytes, cudaMemcpyDeviceToDevice, h->own);
+    Phase pc = ph;
+    pc.mv.seg[0].w = wc;
+    Phase* dpc = nullptr;
+    if (dalloc(h, &dpc, sizeof(Phase))) break;
+    cudaMemcpyAsync(dpc, &pc, sizeof(Phase), cudaMemcpyHostToDevice, h->own);
+    phs.push_back(dpc);
+  }
+  for (int i = 0; i < 3; i++) k_mv<<<ph.grid, CK_THREADS, 0, h->own>>>(phs[i % phs.size()], D);
+  cudaEvent_t a, b;
+  cudaEventCreate(&a);
+  cudaEventCreate(&b);
+  cudaEventRecord(a, h->own);
+  for (int i = 0; i < reps; i++) k_mv<<<ph.grid, CK_THREADS, 0, h->own>>>(phs[i % phs.size()], D);
+  cudaEventRecord(b, h->own);
+  cudaError_t e = cudaEventSynchronize(b);
+  float ms = 0.f;
+  if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, a, b);
+  cudaEventDestroy(a);
+  cudaEventDestroy(b);
+  free_tmp(h);
+  if (e != cudaSuccess) return set_global(CK_ECUDA, "ck_bench_matvec: %s", cudaGetErrorString(e));
+  *us_per = (double)ms * 1000.0 / reps;
+  return CK_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,419 @@
+// Device weight layout for GGUF quantized tensors, and the per-unit decoders.
+//
+// The reference uploads GGUF block bytes unchanged and reads them one byte at
+// a time through u32 words (byte_at, llama-wgsl-runtime.ts:2219-2223).  On the
+// B200 the same blocks are re-laid once at upload so that every per-lane load
+// is a 16-byte aligned vector and every 32-weight "unit" is contiguous:
+//
+//   row = [metadata arrays][units]          (every array 16-byte aligned)
+//
+//   Q4_K : hdr[nsb] x16 B (fp16 d, fp16 dmin, 12 B packed 6-bit scale/min, the
+//          GGUF header verbatim) | units[8*nsb] x16 B: unit s of a super-block
+//          holds sub-block s (32 weights), byte i = q[i] | q[16+i] << 4.
+//   Q6_K : sc[nsb] x16 B (int8 scale per 16 weights) | d[nsb] fp16 |
+//          ql units[8*nsb] x16 B (low nibbles, same packing as Q4_K) |
+//          qh units[8*nsb] x8 B (high 2 bits, see q6_hbits below).
+//   Q8_0 : d[nb] fp16 | units[nb] x32 B int8.
+//   Q5_0 : d[nb] fp16 | qh'[nb] u32 (bit-permuted, see q5_hperm) | units x16 B.
+//   Q5_1 : d[nb] fp16 | m[nb] fp16 | qh'[nb] u32 | units x16 B.
+//
+// The re-layout is lossless: the same fp16 scales and integer codes, so the
+// dequantized values (dequant_at, WGSL operation order) are bit-identical to
+// the WGSL dequantizers' (:2234-2245, :2280-2289, :2321-2327, :2396-2410,
+// :2560-2580).  Total bytes equal the GGUF's up to 16-byte padding of the small
+// metadata arrays.
+#pragma once
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#define GT_F32 0
+#define GT_F16 1
+#define GT_Q5_0 6
+#define GT_Q5_1 7
+#define GT_Q8_0 8
+#define GT_Q4_K 12
+#define GT_Q6_K 14
+
+struct Lay {
+  int type;
+  int k;          // weights per row
+  int nb;         // blocks (32) or super-blocks (256) per row
+  int U;          // 32-weight units per row (k / 32)
+  uint32_t row_bytes;
+  uint32_t off_d, off_m, off_sc, off_qh, off_q, off_q2;
+};
+
+__host__ __device__ inline uint32_t ck_r16(uint32_t x) { return (x + 15u) & ~15u; }
+
+__host__ __device__ inline bool ck_type_ok(int t) {
+  return t == GT_Q4_K || t == GT_Q6_K || t == GT_Q8_0 || t == GT_Q5_0 || t == GT_Q5_1;
+}
+__host__ __device__ inline int ck_block_weights(int t) { return (t == GT_Q4_K || t == GT_Q6_K) ? 256 : 32; }
+__host__ __device__ inline int ck_block_bytes(int t) {
+  switch (t) {
+    case GT_Q4_K: return 144;
+    case GT_Q6_K: return 210;
+    case GT_Q8_0: return 34;
+    case GT_Q5_0: return 22;
+    case GT_Q5_1: return 24;
+  }
+  return 0;
+}
+
+__host__ __device__ inline Lay make_lay(int type, int k) {
+  Lay L;
+  L.type = type; L.k = k; L.U = k / 32;
+  L.off_d = L.off_m = L.off_sc = L.off_qh = L.off_q = L.off_q2 = 0;
+  uint32_t nb = (uint32_t)(k / ck_block_weights(type));
+  L.nb = (int)nb;
+  switch (type) {
+    case GT_Q4_K:
+      L.off_sc = 0;
+      L.off_q = 16 * nb;
+      L.row_bytes = L.off_q + 128 * nb;
+      break;
+    case GT_Q6_K:
+      L.off_sc = 0;
+      L.off_d = 16 * nb;
+      L.off_q = L.off_d + ck_r16(2 * nb);
+      L.off_q2 = L.off_q + 128 * nb;
+      L.row_bytes = L.off_q2 + 64 * nb;
+      break;
+    case GT_Q8_0:
+      L.off_d = 0;
+      L.off_q = ck_r16(2 * nb);
+      L.row_bytes = L.off_q + 32 * nb;
+      break;
+    case GT_Q5_0:
+      L.off_d = 0;
+      L.off_qh = ck_r16(2 * nb);
+      L.off_q = L.off_qh + ck_r16(4 * nb);
+      L.row_bytes = L.off_q + 16 * nb;
+      break;
+    case GT_Q5_1:
+      L.off_d = 0;
+      L.off_m = ck_r16(2 * nb);
+      L.off_qh = L.off_m + ck_r16(2 * nb);
+      L.off_q = L.off_qh + ck_r16(4 * nb);
+      L.row_bytes = L.off_q + 16 * nb;
+      break;
+    default:
+      L.row_bytes = 0;
+  }
+  return L;
+}
+
+// ---------------------------------------------------------------------------
+// Re-layout kernel: one thread per (row, GGUF block).
+
+// 6-bit code (0..63) of weight w (0..255) of a raw Q6_K super-block:
+// ql/qh addressing of GGUF_Q6_K_MATVEC_WGSL (:2560-2580).
+__device__ inline uint32_t raw_q6(const uint8_t* sb, int w) {
+  int half = w >> 7, local = w & 127, lane = local & 31, quarter = local >> 5;
+  uint32_t ql = sb[half * 64 + lane + ((quarter & 1) ? 32 : 0)];
+  uint32_t lo = quarter < 2 ? (ql & 15u) : (ql >> 4);
+  uint32_t qh = (sb[128 + half * 32 + lane] >> (quarter * 2)) & 3u;
+  return lo | (qh << 4);
+}
+
+// High 2 bits of a 32-weight Q6_K unit, packed so that for ql word t (bytes b
+// = weights 4t+b and 16+4t+b) word H[t & 1], shifted by (t >> 1) * 4, holds
+// the low-group bits at bit 0..1 and the high-group bits at 2..3 of each byte.
+__device__ inline void q6_hbits(const uint32_t q[32], uint32_t H[2]) {
+  H[0] = H[1] = 0;
+  for (int tp = 0; tp < 2; tp++)
+    for (int b = 0; b < 4; b++) {
+      uint32_t v = ((q[4 * tp + b] >> 4) & 3u) | (((q[16 + 4 * tp + b] >> 4) & 3u) << 2) |
+                   (((q[4 * (tp + 2) + b] >> 4) & 3u) << 4) | (((q[16 + 4 * (tp + 2) + b] >> 4) & 3u) << 6);
+      H[tp] |= v << (8 * b);
+    }
+}
+
+// Q5 high-bit permutation: bit (8b + t) <- weight 4t+b, bit (8b + 4 + t) <-
+// weight 16+4t+b (t, b in 0..3), so ql word t's fifth bits are one shift and
+// one mask away.
+__device__ inline uint32_t q5_hperm(uint32_t qh) {
+  uint32_t o = 0;
+  for (int t = 0; t < 4; t++)
+    for (int b = 0; b < 4; b++) {
+      o |= ((qh >> (4 * t + b)) & 1u) << (8 * b + t);
+      o |= ((qh >> (16 + 4 * t + b)) & 1u) << (8 * b + 4 + t);
+    }
+  return o;
+}
+
+__global__ void k_relayout(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, Lay L, int n) {
+  long long gid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  long long total = (long long)n * L.nb;
+  if (gid >= total) return;
+  int row = (int)(gid / L.nb), b = (int)(gid % L.nb);
+  size_t raw_row = (size_t)L.nb * ck_block_bytes(L.type);
+  const uint8_t* s = src + (size_t)row * raw_row + (size_t)b * ck_block_bytes(L.type);
+  uint8_t* d = dst + (size_t)row * L.row_bytes;
+  switch (L.type) {
+    case GT_Q4_K: {
+      for (int i = 0; i < 16; i++) d[L.off_sc + 16 * b + i] = s[i];
+      const uint8_t* qs = s + 16;
+      for (int sub = 0; sub < 8; sub++) {
+        int g = sub >> 1, nib = sub & 1;
+        uint8_t* u = d + L.off_q + (8 * b + sub) * 16;
+        for (int i = 0; i < 16; i++) {
+          uint32_t lo = (qs[32 * g + i] >> (4 * nib)) & 15u;
+          uint32_t hi = (qs[32 * g + 16 + i] >> (4 * nib)) & 15u;
+          u[i] = (uint8_t)(lo | (hi << 4));
+        }
+      }
+      break;
+    }
+    case GT_Q6_K: {
+      for (int i = 0; i < 16; i++) d[L.off_sc + 16 * b + i] = s[192 + i];
+      d[L.off_d + 2 * b] = s[208];
+      d[L.off_d + 2 * b + 1] = s[209];
+      for (int sub = 0; sub < 8; sub++) {
+        uint32_t q[32];
+        for (int j = 0; j < 32; j++) q[j] = raw_q6(s, 32 * sub + j);
+        uint8_t* u = d + L.off_q + (8 * b + sub) * 16;
+        for (int i = 0; i < 16; i++) u[i] = (uint8_t)((q[i] & 15u) | ((q[16 + i] & 15u) << 4));
+        uint32_t H[2];
+        q6_hbits(q, H);
+        uint8_t* h = d + L.off_q2 + (8 * b + sub) * 8;
+        for (int i = 0; i < 4; i++) { h[i] = (uint8_t)(H[0] >> (8 * i)); h[4 + i] = (uint8_t)(H[1] >> (8 * i)); }
+      }
+      break;
+    }
+    case GT_Q8_0:
+      d[L.off_d + 2 * b] = s[0];
+      d[L.off_d + 2 * b + 1] = s[1];
+      for (int i = 0; i < 32; i++) d[L.off_q + 32 * b + i] = s[2 + i];
+      break;
+    case GT_Q5_0:
+    case GT_Q5_1: {
+      int is1 = L.type == GT_Q5_1;
+      d[L.off_d + 2 * b] = s[0];
+      d[L.off_d + 2 * b + 1] = s[1];
+      if (is1) { d[L.off_m + 2 * b] = s[2]; d[L.off_m + 2 * b + 1] = s[3]; }
+      const uint8_t* qhp = s + (is1 ? 4 : 2);
+      uint32_t qh = (uint32_t)qhp[0] | ((uint32_t)qhp[1] << 8) | ((uint32_t)qhp[2] << 16) | ((uint32_t)qhp[3] << 24);
+      uint32_t p = q5_hperm(qh);
+      for (int i = 0; i < 4; i++) d[L.off_qh + 4 * b + i] = (uint8_t)(p >> (8 * i));
+      const uint8_t* qs = s + (is1 ? 8 : 6);
+      for (int i = 0; i < 16; i++) d[L.off_q + 16 * b + i] = qs[i];
+      break;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Exact dequantization from the device layout (WGSL operation order, each
+// product/difference rounded separately: no FMA contraction).
+
+__device__ __forceinline__ float ld_f16(const uint8_t* p) {
+  return __half2float(__ushort_as_half(*(const unsigned short*)p));
+}
+
+// scale_min_k4 (llama-wgsl-runtime.ts:2387-2394) over the 12 packed bytes.
+__device__ __forceinline__ void scale_min_k4(const uint8_t* q, int j, uint32_t& sc, uint32_t& m) {
+  if (j < 4) {
+    sc = q[j] & 63u;
+    m = q[j + 4] & 63u;
+  } else {
+    sc = (q[j + 4] & 15u) | ((q[j - 4] >> 6) << 4);
+    m = (q[j + 4] >> 4) | ((q[j] >> 6) << 4);
+  }
+}
+
+__device__ inline float dequant_at(const uint8_t* row, const Lay& L, int col) {
+  switch (L.type) {
+    case GT_Q4_K: {
+      int sb = col >> 8, within = col & 255, sub = within >> 5, j = within & 31;
+      const uint8_t* hdr = row + L.off_sc + 16 * sb;
+      float d = ld_f16(hdr), dmin = ld_f16(hdr + 2);
+      uint32_t sc, m;
+      scale_min_k4(hdr + 4, sub, sc, m);
+      uint32_t byte = row[L.off_q + (8 * sb + sub) * 16 + (j & 15)];
+      uint32_t q = j < 16 ? (byte & 15u) : (byte >> 4);
+      return __fsub_rn(__fmul_rn(__fmul_rn(d, (float)sc), (float)q), __fmul_rn(dmin, (float)m));
+    }
+    case GT_Q6_K: {
+      int sb = col >> 8, within = col & 255, sub = within >> 5, j = within & 31;
+      uint32_t byte = row[L.off_q + (8 * sb + sub) * 16 + (j & 15)];
+      uint32_t lo = j < 16 ? (byte & 15u) : (byte >> 4);
+      int jj = j & 15, t = jj >> 2, b = jj & 3;
+      uint32_t H = *(const uint32_t*)(row + L.off_q2 + (8 * sb + sub) * 8 + 4 * (t & 1));
+      int sh = (t >> 1) * 4 + (j < 16 ? 0 : 2);
+      uint32_t hi = (H >> (8 * b + sh)) & 3u;
+      int q = (int)(lo | (hi << 4)) - 32;
+      int sc = (int)(int8_t)row[L.off_sc + 16 * sb + (within >> 4)];
+      float d = ld_f16(row + L.off_d + 2 * sb);
+      return __fmul_rn(__fmul_rn(d, (float)sc), (float)q);
+    }
+    case GT_Q8_0: {
+      int b = col >> 5, j = col & 31;
+      int q = (int)(int8_t)row[L.off_q + 32 * b + j];
+      return __fmul_rn((float)q, ld_f16(row + L.off_d + 2 * b));
+    }
+    case GT_Q5_0:
+    case GT_Q5_1: {
+      int b = col >> 5, j = col & 31;
+      uint32_t byte = row[L.off_q + 16 * b + (j & 15)];
+      uint32_t lo = j < 16 ? (byte & 15u) : (byte >> 4);
+      uint32_t qh = *(const uint32_t*)(row + L.off_qh + 4 * b);
+      int jj = j & 15, t = jj >> 2, bb = jj & 3;
+      uint32_t hb = (qh >> (8 * bb + t + (j < 16 ? 0 : 4))) & 1u;
+      uint32_t q = lo | (hb << 4);
+      float d = ld_f16(row + L.off_d + 2 * b);
+      if (L.type == GT_Q5_0) return __fmul_rn(d, (float)((int)q - 16));
+      return __fadd_rn(__fmul_rn(d, (float)q), ld_f16(row + L.off_m + 2 * b));
+    }
+  }
+  return 0.f;
+}
+
+__global__ void k_dequant(const uint8_t* __restrict__ w, Lay L, int n, float* __restrict__ out) {
+  long long gid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (gid >= (long long)n * L.k) return;
+  int row = (int)(gid / L.k), col = (int)(gid % L.k);
+  out[gid] = dequant_at(w + (size_t)row * L.row_bytes, L, col);
+}
+
+// ---------------------------------------------------------------------------
+// Integer unit dot products for the matvec.
+//
+// The activation x is quantized per 32-element group into a 16-bit integer
+// X = hi * 256 + lo (hi, lo int8; |X| <= 32639) with a float step sx, so
+// sum_i x_i q_i = sx * (256 * dp4a(hi, q) + dp4a(lo, q)) is evaluated exactly
+// in int32; the only approximation is x's 16-bit grid (relative 1.5e-5 of the
+// group's max), far inside the 1e-3 logits tolerance.  Per unit a lane holds:
+struct XUnit {
+  int h[8];     // hi bytes of X for the unit's 32 weights, 4 per word, in order
+  int l[8];     // lo bytes
+  float sx;     // group step
+  int sa, sb;   // sum of X over weights 0..15 and 16..31
+};
+
+struct UnitRaw {   // raw bytes of one unit (per type, see load_unit)
+  uint4 q;
+  uint4 q2;       // Q4_K: header; Q8_0: second 16 weights
+  uint32_t a;     // Q6_K: H[0]; Q5: qh'
+  uint32_t b;     // Q6_K: H[1]
+  uint32_t dm;    // fp16 d (lo 16) and fp16 m / dmin-pair / scale pair (hi 16)
+};
+
+__device__ __forceinline__ uint4 ldg16(const uint8_t* p) { return __ldg((const uint4*)p); }
+__device__ __forceinline__ uint32_t ldg4(const uint8_t* p) { return __ldg((const unsigned int*)p); }
+__device__ __forceinline__ uint32_t ldg2(const uint8_t* p) { return (uint32_t)__ldg((const unsigned short*)p); }
+
+template <int T>
+__device__ __forceinline__ void load_unit(const uint8_t* row, const Lay& L, int c, UnitRaw& r) {
+  if (T == GT_Q4_K) {
+    r.q = ldg16(row + L.off_q + 16 * c);
+    r.q2 = ldg16(row + L.off_sc + 16 * (c >> 3));
+  } else if (T == GT_Q6_K) {
+    r.q = ldg16(row + L.off_q + 16 * c);
+    uint2 h = __ldg((const uint2*)(row + L.off_q2 + 8 * c));
+    r.a = h.x;
+    r.b = h.y;
+    int sb = c >> 3, sub = c & 7;
+    r.dm = ldg2(row + L.off_d + 2 * sb) | (ldg2(row + L.off_sc + 16 * sb + 2 * sub) << 16);
+  } else if (T == GT_Q8_0) {
+    r.q = ldg16(row + L.off_q + 32 * c);
+    r.q2 = ldg16(row + L.off_q + 32 * c + 16);
+    r.dm = ldg2(row + L.off_d + 2 * c);
+  } else if (T == GT_Q5_0) {
+    r.q = ldg16(row + L.off_q + 16 * c);
+    r.a = ldg4(row + L.off_qh + 4 * c);
+    r.dm = ldg2(row + L.off_d + 2 * c);
+  } else if (T == GT_Q5_1) {
+    r.q = ldg16(row + L.off_q + 16 * c);
+    r.a = ldg4(row + L.off_qh + 4 * c);
+    r.dm = ldg2(row + L.off_d + 2 * c) | (ldg2(row + L.off_m + 2 * c) << 16);
+  }
+}
+
+__device__ __forceinline__ float h2f_bits(uint32_t b) { return __half2float(__ushort_as_half((unsigned short)(b & 0xFFFFu))); }
+__device__ __forceinline__ uint32_t w_at(const uint4& v, int t) { return t == 0 ? v.x : t == 1 ? v.y : t == 2 ? v.z : v.w; }
+
+// Contribution of one unit (32 weights) to the row's dot product.
+template <int T>
+__device__ __forceinline__ float unit_dot(const UnitRaw& r, const XUnit& x, int c) {
+  if (T == GT_Q4_K) {
+    int ah = 0, al = 0;
+#pragma unroll
+    for (int t = 0; t < 4; t++) {
+      uint32_t w = w_at(r.q, t);
+      int lo = (int)(w & 0x0F0F0F0Fu), hi = (int)((w >> 4) & 0x0F0F0F0Fu);
+      ah = __dp4a(lo, x.h[t], ah);
+      ah = __dp4a(hi, x.h[4 + t], ah);
+      al = __dp4a(lo, x.l[t], al);
+      al = __dp4a(hi, x.l[4 + t], al);
+    }
+    int dot = ah * 256 + al;
+    float d = h2f_bits(r.q2.x), dmin = h2f_bits(r.q2.x >> 16);
+    int sub = c & 7;
+    // The 12 packed scale bytes q[0..11] are header words y (q0..3), z (q4..7)
+    // and w (q8..11); scale_min_k4 (llama-wgsl-runtime.ts:2387-2394).
+    uint32_t sc, m;
+    if (sub < 4) {
+      sc = (r.q2.y >> (8 * sub)) & 63u;
+      m = (r.q2.z >> (8 * sub)) & 63u;
+    } else {
+      uint32_t qj4 = (r.q2.w >> (8 * (sub - 4))) & 0xFFu;   // q[j+4]
+      uint32_t qjm4 = (r.q2.y >> (8 * (sub - 4))) & 0xFFu;  // q[j-4]
+      uint32_t qj = (r.q2.z >> (8 * (sub - 4))) & 0xFFu;    // q[j]
+      sc = (qj4 & 15u) | ((qjm4 >> 6) << 4);
+      m = (qj4 >> 4) | ((qj >> 6) << 4);
+    }
+    float ds = d * (float)sc, dm = dmin * (float)m;
+    return ds * (x.sx * (float)dot) - dm * (x.sx * (float)(x.sa + x.sb));
+  } else if (T == GT_Q6_K) {
+    int ahl = 0, all = 0, ahh = 0, alh = 0;
+#pragma unroll
+    for (int t = 0; t < 4; t++) {
+      uint32_t w = w_at(r.q, t);
+      uint32_t H = (t & 1) ? r.b : r.a;
+      int sh = (t >> 1) * 4;
+      int lo = (int)((w & 0x0F0F0F0Fu) | (((H >> sh) << 4) & 0x30303030u));
+      int hi = (int)(((w >> 4) & 0x0F0F0F0Fu) | (((H >> (sh + 2)) << 4) & 0x30303030u));
+      ahl = __dp4a(lo, x.h[t], ahl);
+      all = __dp4a(lo, x.l[t], all);
+      ahh = __dp4a(hi, x.h[4 + t], ahh);
+      alh = __dp4a(hi, x.l[4 + t], alh);
+    }
+    int dlo = ahl * 256 + all - 32 * x.sa;
+    int dhi = ahh * 256 + alh - 32 * x.sb;
+    float d = h2f_bits(r.dm);
+    float sc0 = (float)(int)(int8_t)((r.dm >> 16) & 0xFFu);
+    float sc1 = (float)(int)(int8_t)((r.dm >> 24) & 0xFFu);
+    return (d * sc0) * (x.sx * (float)dlo) + (d * sc1) * (x.sx * (float)dhi);
+  } else if (T == GT_Q8_0) {
+    int ah = 0, al = 0;
+#pragma unroll
+    for (int t = 0; t < 4; t++) {
+      int w0 = (int)w_at(r.q, t), w1 = (int)w_at(r.q2, t);
+      ah = __dp4a(w0, x.h[t], ah);
+      ah = __dp4a(w1, x.h[4 + t], ah);
+      al = __dp4a(w0, x.l[t], al);
+      al = __dp4a(w1, x.l[4 + t], al);
+    }
+    int dot = ah * 256 + al;
+    return h2f_bits(r.dm) * (x.sx * (float)dot);
+  } else {  // Q5_0 / Q5_1
+    int ah = 0, al = 0;
+    uint32_t qh = r.a;
+#pragma unroll
+    for (int t = 0; t < 4; t++) {
+      uint32_t w = w_at(r.q, t);
+      int lo = (int)((w & 0x0F0F0F0Fu) | ((qh << (4 - t)) & 0x10101010u));
+      int hi = (int)(((w >> 4) & 0x0F0F0F0Fu) | ((qh >> t) & 0x10101010u));
+      ah = __dp4a(lo, x.h[t], ah);
+      ah = __dp4a(hi, x.h[4 + t], ah);
+      al = __dp4a(lo, x.l[t], al);
+      al = __dp4a(hi, x.l[4 + t], al);
+    }
+    int dot = ah * 256 + al;
+    float d = h2f_bits(r.dm);
+    if (T == GT_Q5_0) return d * (x.sx * (float)(dot - 16 * (x.sa + x.sb)));
+    float m = h2f_bits(r.dm >> 16);
+    return d * (x.sx * (float)dot) + m * (x.sx * (float)(x.sa + x.sb));
+  }
+}
