@@ -268,7 +268,8 @@ def main():
     log(f"[bench r{rank}] loaded in {time.time() - t:.1f}s")
     eng = loaded.engine.dev
     eng.set_mode(args.mode)
-    stream = torch.cuda.current_stream()
+    # a real (non-default) stream shared by the engine and the timing events
+    stream = torch.cuda.Stream()
     eng.set_stream(stream.cuda_stream)
     prompt = np.random.default_rng(1 + rank).integers(0, S.vocab, size=prompt_len).tolist()
     samp = None
