@@ -104,6 +104,8 @@ def lib():
             L.ck_bench_matvec.argtypes = [I, P, S, I, I, I, pp(D), I]
             L.ck_abi_info.argtypes = [pp(I), pp(I)]
             L.ck_io_bytes.argtypes = [P, pp(ctypes.c_uint64), pp(ctypes.c_uint64)]
+            L.ck_trace.argtypes = [P, I]
+            L.ck_trace_read.argtypes = [P, P, S]
             _lib = L
     return _lib
 
@@ -224,6 +226,14 @@ class Engine:
         w, k = ctypes.c_double(), ctypes.c_double()
         _check(self._L.ck_step_bytes(self.h, ctypes.byref(w), ctypes.byref(k)), self.h)
         return w.value, k.value
+
+    def trace(self, enable: bool) -> None:
+        _check(self._L.ck_trace(self.h, 1 if enable else 0), self.h)
+
+    def trace_read(self, n: int = 16384) -> np.ndarray:
+        out = np.zeros(n, dtype=np.uint64)
+        _check(self._L.ck_trace_read(self.h, out.ctypes.data, n), self.h)
+        return out
 
     def io_bytes(self) -> Tuple[int, int]:
         a, b = ctypes.c_uint64(0), ctypes.c_uint64(0)

@@ -67,6 +67,7 @@ struct ck_engine {
   float *resA = nullptr, *resB = nullptr, *tmp = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *attn = nullptr,
         *g = nullptr, *u = nullptr, *part = nullptr;
   unsigned* counters = nullptr;
+  float* inv_freq = nullptr;  // [layers][head_dim/2] RoPE inverse frequencies
   uint8_t* kv = nullptr;
   size_t kv_bytes = 0;
   int smax = 1;
@@ -77,6 +78,8 @@ struct ck_engine {
   int mega_grid = 0;
   cudaGraphExec_t gx_logits[2] = {nullptr, nullptr}, gx_prefill[2] = {nullptr, nullptr};
 
+  CkDev Dlaunch;            // CkDev passed to kernels (trace pointer only when tracing)
+  bool trace_on = false;
   // host mirrors
   int pos = 0;
   unsigned long long io_h2d = 0, io_d2h = 0;  // bytes copied by step calls
@@ -207,14 +210,6 @@ MvSeg seg(const Weight& w, float* out, const float* add) {
   return s;
 }
 
-int mv_groups(const MvPhase& m) {
-  int upl = (m.k + 1023) >> 10;
-  int R = upl <= 1 ? 4 : (upl == 2 ? 2 : 1);
-  int g = 0;
-  for (int i = 0; i < m.nseg; i++) g += (m.seg[i].n + R - 1) / R;
-  return g;
-}
-
 Phase mk_mv(ck_engine* h, const Pro& pro, int k, std::initializer_list<MvSeg> segs) {
   Phase p;
   memset(&p, 0, sizeof p);
@@ -223,10 +218,10 @@ Phase mk_mv(ck_engine* h, const Pro& pro, int k, std::initializer_list<MvSeg> se
   p.mv.k = k;
   p.mv.nseg = 0;
   for (const MvSeg& s : segs) p.mv.seg[p.mv.nseg++] = s;
-  int groups = mv_groups(p.mv);
-  int grid = (groups + CK_WARPS - 1) / CK_WARPS;
-  int cap = h->sms * 4;
-  p.grid = grid < 1 ? 1 : (grid > cap ? cap : grid);
+  // one CTA per SM: each streams a contiguous row range through its tile ring
+  int rows = 0;
+  for (int i = 0; i < p.mv.nseg; i++) rows = rows > p.mv.seg[i].n ? rows : p.mv.seg[i].n;
+  p.grid = rows < h->sms ? (rows < 1 ? 1 : rows) : h->sms;
   return p;
 }
 
@@ -263,6 +258,7 @@ void build_schedule(ck_engine* h, bool logits, std::vector<Phase>& out) {
     a.at.qw = c.qk_norm ? W.q_norm : nullptr;
     a.at.kw = c.qk_norm ? W.k_norm : nullptr;
     size_t per = (size_t)c.kv_heads * c.context_length * hd * elem_kv(c);
+    a.at.inv_freq = h->inv_freq + (size_t)i * (hd / 2);
     a.at.kc = h->kv + (size_t)(2 * i) * per;
     a.at.vc = h->kv + (size_t)(2 * i + 1) * per;
     a.at.out = h->attn;
@@ -276,7 +272,7 @@ void build_schedule(ck_engine* h, bool logits, std::vector<Phase>& out) {
     a.at.theta = c.layer_rope_theta[i];
     a.at.eps = c.qk_norm_eps;
     a.at.scale = (float)(1.0 / sqrt((double)hd));  // ATTN_SCALE constant (:1711)
-    a.grid = c.kv_heads * h->smax;
+    a.grid = c.kv_heads * h->smax;  // units are split-major: unit = split * kv_heads + head
     out.push_back(a);
 
     Pro pc{};
@@ -310,20 +306,10 @@ void build_schedule(ck_engine* h, bool logits, std::vector<Phase>& out) {
     a1.grid = (c.vocab + 255) / 256;
     if (a1.grid > h->sms * 4) a1.grid = h->sms * 4;
     out.push_back(a1);
-    Phase a2;
-    memset(&a2, 0, sizeof a2);
-    a2.kind = PH_ARGMAX2;
-    a2.grid = 1;
-    out.push_back(a2);
-    Phase s;
-    memset(&s, 0, sizeof s);
-    s.kind = PH_SAMPLE;
-    s.grid = 1;
-    out.push_back(s);
   }
   Phase f;
   memset(&f, 0, sizeof f);
-  f.kind = PH_FINISH;
+  f.kind = logits ? PH_SELECT : PH_FINISH;   // select = argmax stage 2 + sampling + finish
   f.grid = 1;
   f.need_logits = logits ? 1 : 0;
   out.push_back(f);
@@ -332,17 +318,18 @@ void build_schedule(ck_engine* h, bool logits, std::vector<Phase>& out) {
 int enqueue_phases(ck_engine* h, const std::vector<Phase>& ph, const Phase* dph, int mode, cudaStream_t s) {
   if (mode == 1) {
     for (size_t i = 0; i < ph.size(); i++) {
-      if (ph[i].kind == PH_MATVEC) k_mv<<<ph[i].grid, CK_THREADS, 0, s>>>(dph + i, h->D);
-      else if (ph[i].kind == PH_ATTN) k_attn<<<ph[i].grid, CK_THREADS, 0, s>>>(dph + i, h->D);
-      else k_misc<<<ph[i].grid, CK_THREADS, 0, s>>>(dph + i, h->D);
+      if (ph[i].kind == PH_MATVEC) k_mv<<<ph[i].grid, CK_THREADS, CK_DYN_PHASES + sizeof(Phase), s>>>(dph + i, h->Dlaunch);
+      else if (ph[i].kind == PH_ATTN) k_attn<<<ph[i].grid, CK_THREADS, 0, s>>>(dph + i, h->Dlaunch);
+      else k_misc<<<ph[i].grid, CK_THREADS, 0, s>>>(dph + i, h->Dlaunch);
     }
     CKC(h, cudaGetLastError());
     return CK_OK;
   }
   CKC(h, cudaMemsetAsync(&h->st->bar, 0, sizeof(uint32_t), s));
   int nph = (int)ph.size();
-  void* args[] = {(void*)&dph, (void*)&nph, (void*)&h->D};
-  CKC(h, cudaLaunchCooperativeKernel((const void*)k_mega, dim3(h->mega_grid), dim3(CK_THREADS), args, 0, s));
+  void* args[] = {(void*)&dph, (void*)&nph, (void*)&h->Dlaunch};
+  size_t dyn = CK_DYN_PHASES + ph.size() * sizeof(Phase);
+  CKC(h, cudaLaunchCooperativeKernel((const void*)k_mega, dim3(h->mega_grid), dim3(CK_THREADS), args, dyn, s));
   return CK_OK;
 }
 
@@ -564,6 +551,7 @@ int ck_finalize(ck_engine* h) {
   if (h->smax < 1) h->smax = 1;
   if ((rc = dalloc(h, &h->st, sizeof(CkState)))) return rc;
   CKC(h, cudaMemset(h->st, 0, sizeof(CkState)));
+  memset(&h->D, 0, sizeof h->D);
   h->D.st = h->st;
   h->D.vocab = c.vocab;
   h->D.ctx = c.context_length;
@@ -588,10 +576,15 @@ int ck_finalize(ck_engine* h) {
   if ((rc = dalloc(h, &h->part, (size_t)c.kv_heads * h->smax * G * (hd + 2) * 4))) return rc;
   if ((rc = dalloc(h, &h->counters, (size_t)c.kv_heads * 4))) return rc;
   CKC(h, cudaMemset(h->counters, 0, (size_t)c.kv_heads * 4));
+  if ((rc = dalloc(h, &h->inv_freq, (size_t)c.layers * (hd / 2) * 4))) return rc;
+  for (int i = 0; i < c.layers; i++)
+    k_inv_freq<<<1, 128>>>(h->inv_freq + (size_t)i * (hd / 2), c.layer_rope_theta[i], hd);
+  CKC(h, cudaGetLastError());
   h->kv_bytes = (size_t)c.layers * 2 * c.kv_heads * c.context_length * hd * elem_kv(c);
   if ((rc = dalloc(h, &h->kv, h->kv_bytes))) return rc;
   CKC(h, cudaMemset(h->kv, 0, h->kv_bytes));
 
+  h->Dlaunch = h->D;
   build_schedule(h, true, h->ph_logits);
   build_schedule(h, false, h->ph_prefill);
   if ((rc = dalloc(h, &h->d_logits, h->ph_logits.size() * sizeof(Phase)))) return rc;
@@ -599,8 +592,14 @@ int ck_finalize(ck_engine* h) {
   CKC(h, cudaMemcpy(h->d_logits, h->ph_logits.data(), h->ph_logits.size() * sizeof(Phase), cudaMemcpyHostToDevice));
   CKC(h, cudaMemcpy(h->d_prefill, h->ph_prefill.data(), h->ph_prefill.size() * sizeof(Phase),
                     cudaMemcpyHostToDevice));
+  if (h->ph_logits.size() * sizeof(Phase) > CK_PHASE_SMEM_MAX)
+    return h->fail(CK_EINVAL, "%zu decode phases exceed the %d-byte descriptor stage", h->ph_logits.size(),
+                   CK_PHASE_SMEM_MAX);
+  CKC(h, cudaFuncSetAttribute(k_mega, cudaFuncAttributeMaxDynamicSharedMemorySize, CK_DYN_SMEM_MAX));
+  CKC(h, cudaFuncSetAttribute(k_mv, cudaFuncAttributeMaxDynamicSharedMemorySize, CK_DYN_SMEM_MAX));
   int per_sm = 0;
-  CKC(h, cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_mega, CK_THREADS, 0));
+  CKC(h, cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_mega, CK_THREADS,
+                                                       CK_DYN_PHASES + h->ph_logits.size() * sizeof(Phase)));
   int want = 1;
   const char* w = getenv("CK_MEGA_CTAS_PER_SM");
   if (w) want = atoi(w);
@@ -817,6 +816,38 @@ int ck_step_bytes(ck_engine* h, double* weight_bytes, double* kv_bytes) {
   return CK_OK;
 }
 
+int ck_trace(ck_engine* h, int enable) {
+  if (!h) return set_global(CK_EINVAL, "null engine");
+  if (!h->finalized) return h->fail(CK_ESTATE, "engine not finalized");
+  if (enable && !h->D.trace) {
+    int rc = dalloc(h, &h->D.trace, CK_TRACE_SLOTS * sizeof(unsigned long long));
+    if (rc) return rc;
+    CKC(h, cudaMemset(h->D.trace, 0, CK_TRACE_SLOTS * sizeof(unsigned long long)));
+  }
+  h->trace_on = enable != 0;
+  CkDev D = h->D;
+  if (!enable) D.trace = nullptr;
+  h->Dlaunch = D;
+  // graphs hold the kernel arguments: rebuild them with the new CkDev
+  for (int m = 0; m < 2; m++) {
+    if (h->gx_logits[m]) { cudaGraphExecDestroy(h->gx_logits[m]); h->gx_logits[m] = nullptr; }
+    if (h->gx_prefill[m]) { cudaGraphExecDestroy(h->gx_prefill[m]); h->gx_prefill[m] = nullptr; }
+    if (capture(h, h->ph_logits, h->d_logits, m, &h->gx_logits[m])) { cudaGetLastError(); h->gx_logits[m] = nullptr; }
+    if (capture(h, h->ph_prefill, h->d_prefill, m, &h->gx_prefill[m])) { cudaGetLastError(); h->gx_prefill[m] = nullptr; }
+  }
+  h->err.clear();
+  return CK_OK;
+}
+
+int ck_trace_read(ck_engine* h, uint64_t* out, size_t n) {
+  if (!h || !out) return set_global(CK_EINVAL, "bad argument");
+  if (!h->D.trace) return h->fail(CK_ESTATE, "tracing is off");
+  if (n > CK_TRACE_SLOTS) n = CK_TRACE_SLOTS;
+  CKC(h, cudaStreamSynchronize(h->stream));
+  CKC(h, cudaMemcpy(out, h->D.trace, n * 8, cudaMemcpyDeviceToHost));
+  return CK_OK;
+}
+
 int ck_io_bytes(ck_engine* h, uint64_t* h2d_bytes, uint64_t* d2h_bytes) {
   if (!h || !h2d_bytes || !d2h_bytes) return set_global(CK_EINVAL, "bad argument");
   *h2d_bytes = h->io_h2d;
@@ -854,6 +885,12 @@ int make_tmp(int device, ck_engine** out) {
   h->sms = prop.multiProcessorCount;
   CKG(cudaStreamCreateWithFlags(&h->own, cudaStreamNonBlocking));
   h->stream = h->own;
+  CKG(cudaFuncSetAttribute(k_mv, cudaFuncAttributeMaxDynamicSharedMemorySize, CK_DYN_SMEM_MAX));
+  int rc = dalloc(h, &h->st, sizeof(CkState));
+  if (rc) return set_global(rc, "%s", h->err.c_str());
+  CKG(cudaMemset(h->st, 0, sizeof(CkState)));
+  memset(&h->D, 0, sizeof h->D);
+  h->D.st = h->st;
   *out = h;
   return CK_OK;
 }
@@ -918,10 +955,9 @@ int ck_matvec(int ggml_type, const void* bytes, size_t nbytes, int k, int n, con
     free_tmp(h);
     return set_global(rc, "%s", m.c_str());
   }
-  CkDev D;
-  memset(&D, 0, sizeof D);
+  CkDev D = h->D;
   cudaMemcpyAsync(dx, x, (size_t)k * 4, cudaMemcpyHostToDevice, h->own);
-  k_mv<<<ph.grid, CK_THREADS, 0, h->own>>>(dph, D);
+  k_mv<<<ph.grid, CK_THREADS, CK_DYN_PHASES + sizeof(Phase), h->own>>>(dph, D);
   cudaError_t e = cudaGetLastError();
   if (e == cudaSuccess) e = cudaMemcpyAsync(y, dy, (size_t)n * 4, cudaMemcpyDeviceToHost, h->own);
   if (e == cudaSuccess) e = cudaStreamSynchronize(h->own);
@@ -945,8 +981,7 @@ int ck_bench_matvec(int ggml_type, const void* bytes, size_t nbytes, int k, int 
     free_tmp(h);
     return set_global(rc, "%s", m.c_str());
   }
-  CkDev D;
-  memset(&D, 0, sizeof D);
+  CkDev D = h->D;
   cudaMemsetAsync(dx, 0, (size_t)k * 4, h->own);
   // Rotate over enough weight copies to exceed L2 so every launch streams
   // from HBM.
@@ -967,12 +1002,12 @@ int ck_bench_matvec(int ggml_type, const void* bytes, size_t nbytes, int k, int 
     cudaMemcpyAsync(dpc, &pc, sizeof(Phase), cudaMemcpyHostToDevice, h->own);
     phs.push_back(dpc);
   }
-  for (int i = 0; i < 3; i++) k_mv<<<ph.grid, CK_THREADS, 0, h->own>>>(phs[i % phs.size()], D);
+  for (int i = 0; i < 3; i++) k_mv<<<ph.grid, CK_THREADS, CK_DYN_PHASES + sizeof(Phase), h->own>>>(phs[i % phs.size()], D);
   cudaEvent_t a, b;
   cudaEventCreate(&a);
   cudaEventCreate(&b);
   cudaEventRecord(a, h->own);
-  for (int i = 0; i < reps; i++) k_mv<<<ph.grid, CK_THREADS, 0, h->own>>>(phs[i % phs.size()], D);
+  for (int i = 0; i < reps; i++) k_mv<<<ph.grid, CK_THREADS, CK_DYN_PHASES + sizeof(Phase), h->own>>>(phs[i % phs.size()], D);
   cudaEventRecord(b, h->own);
   cudaError_t e = cudaEventSynchronize(b);
   float ms = 0.f;

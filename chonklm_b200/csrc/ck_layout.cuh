@@ -35,12 +35,12 @@
 #define GT_Q6_K 14
 
 struct Lay {
-  int type;
-  int k;          // weights per row
-  int nb;         // blocks (32) or super-blocks (256) per row
-  int U;          // 32-weight units per row (k / 32)
+  uint16_t type;
+  uint16_t k;         // weights per row (<= 4096)
+  uint16_t nb;        // blocks (32) or super-blocks (256) per row
+  uint16_t U;         // 32-weight units per row (k / 32)
   uint32_t row_bytes;
-  uint32_t off_d, off_m, off_sc, off_qh, off_q, off_q2;
+  uint16_t off_d, off_m, off_sc, off_qh, off_q, off_q2;   // byte offsets inside a row
 };
 
 __host__ __device__ inline uint32_t ck_r16(uint32_t x) { return (x + 15u) & ~15u; }
@@ -62,39 +62,39 @@ __host__ __device__ inline int ck_block_bytes(int t) {
 
 __host__ __device__ inline Lay make_lay(int type, int k) {
   Lay L;
-  L.type = type; L.k = k; L.U = k / 32;
+  L.type = (uint16_t)type; L.k = (uint16_t)k; L.U = (uint16_t)(k / 32);
   L.off_d = L.off_m = L.off_sc = L.off_qh = L.off_q = L.off_q2 = 0;
   uint32_t nb = (uint32_t)(k / ck_block_weights(type));
-  L.nb = (int)nb;
+  L.nb = (uint16_t)nb;
   switch (type) {
     case GT_Q4_K:
       L.off_sc = 0;
-      L.off_q = 16 * nb;
+      L.off_q = (uint16_t)(16 * nb);
       L.row_bytes = L.off_q + 128 * nb;
       break;
     case GT_Q6_K:
       L.off_sc = 0;
-      L.off_d = 16 * nb;
-      L.off_q = L.off_d + ck_r16(2 * nb);
-      L.off_q2 = L.off_q + 128 * nb;
+      L.off_d = (uint16_t)(16 * nb);
+      L.off_q = (uint16_t)(L.off_d + ck_r16(2 * nb));
+      L.off_q2 = (uint16_t)(L.off_q + 128 * nb);
       L.row_bytes = L.off_q2 + 64 * nb;
       break;
     case GT_Q8_0:
       L.off_d = 0;
-      L.off_q = ck_r16(2 * nb);
+      L.off_q = (uint16_t)ck_r16(2 * nb);
       L.row_bytes = L.off_q + 32 * nb;
       break;
     case GT_Q5_0:
       L.off_d = 0;
-      L.off_qh = ck_r16(2 * nb);
-      L.off_q = L.off_qh + ck_r16(4 * nb);
+      L.off_qh = (uint16_t)ck_r16(2 * nb);
+      L.off_q = (uint16_t)(L.off_qh + ck_r16(4 * nb));
       L.row_bytes = L.off_q + 16 * nb;
       break;
     case GT_Q5_1:
       L.off_d = 0;
-      L.off_m = ck_r16(2 * nb);
-      L.off_qh = L.off_m + ck_r16(2 * nb);
-      L.off_q = L.off_qh + ck_r16(4 * nb);
+      L.off_m = (uint16_t)ck_r16(2 * nb);
+      L.off_qh = (uint16_t)(L.off_m + ck_r16(2 * nb));
+      L.off_q = (uint16_t)(L.off_qh + ck_r16(4 * nb));
       L.row_bytes = L.off_q + 16 * nb;
       break;
     default:
@@ -291,129 +291,130 @@ struct XUnit {
   int sa, sb;   // sum of X over weights 0..15 and 16..31
 };
 
-struct UnitRaw {   // raw bytes of one unit (per type, see load_unit)
-  uint4 q;
-  uint4 q2;       // Q4_K: header; Q8_0: second 16 weights
-  uint32_t a;     // Q6_K: H[0]; Q5: qh'
-  uint32_t b;     // Q6_K: H[1]
-  uint32_t dm;    // fp16 d (lo 16) and fp16 m / dmin-pair / scale pair (hi 16)
+template <bool G>
+__device__ __forceinline__ uint4 ld16(const uint8_t* p) { return G ? __ldg((const uint4*)p) : *(const uint4*)p; }
+template <bool G>
+__device__ __forceinline__ uint2 ld8(const uint8_t* p) { return G ? __ldg((const uint2*)p) : *(const uint2*)p; }
+template <bool G>
+__device__ __forceinline__ uint32_t ld4(const uint8_t* p) {
+  return G ? __ldg((const unsigned int*)p) : *(const unsigned int*)p;
+}
+template <bool G>
+__device__ __forceinline__ uint32_t ld2(const uint8_t* p) {
+  return G ? (uint32_t)__ldg((const unsigned short*)p) : (uint32_t) * (const unsigned short*)p;
+}
+
+// Normalized unit: every block type decodes to the same form, so the dp4a
+// dot product is shared code and only the unpack differs per type.
+//   q[0..3]: byte codes of weights 0..15 (4 per word, in order), q[4..7]: 16..31
+//   contribution = sx * (a0 * (dlo + ko*sa) + a1 * (dhi + ko*sb) + b * (sa + sb))
+// with dlo/dhi the integer dots of X with the codes of each half.
+//   Q4_K  a0 = a1 = d*sc, ko = 0, b = -dmin*m      (w = d*sc*q - dmin*m)
+//   Q6_K  a0 = d*sc0, a1 = d*sc1, ko = -32, b = 0   (w = d*sc*(q - 32))
+//   Q8_0  a0 = a1 = d, ko = 0, b = 0                (w = q*d)
+//   Q5_0  a0 = a1 = d, ko = -16, b = 0              (w = d*(q - 16))
+//   Q5_1  a0 = a1 = d, ko = 0, b = m                (w = d*q + m)
+struct U8 {
+  int q[8];
+  float a0, a1, b;
+  int ko;
 };
 
-__device__ __forceinline__ uint4 ldg16(const uint8_t* p) { return __ldg((const uint4*)p); }
-__device__ __forceinline__ uint32_t ldg4(const uint8_t* p) { return __ldg((const unsigned int*)p); }
-__device__ __forceinline__ uint32_t ldg2(const uint8_t* p) { return (uint32_t)__ldg((const unsigned short*)p); }
+__device__ __forceinline__ float h2f_u16(uint32_t b) { return __half2float(__ushort_as_half((unsigned short)(b & 0xFFFFu))); }
 
-template <int T>
-__device__ __forceinline__ void load_unit(const uint8_t* row, const Lay& L, int c, UnitRaw& r) {
-  if (T == GT_Q4_K) {
-    r.q = ldg16(row + L.off_q + 16 * c);
-    r.q2 = ldg16(row + L.off_sc + 16 * (c >> 3));
-  } else if (T == GT_Q6_K) {
-    r.q = ldg16(row + L.off_q + 16 * c);
-    uint2 h = __ldg((const uint2*)(row + L.off_q2 + 8 * c));
-    r.a = h.x;
-    r.b = h.y;
-    int sb = c >> 3, sub = c & 7;
-    r.dm = ldg2(row + L.off_d + 2 * sb) | (ldg2(row + L.off_sc + 16 * sb + 2 * sub) << 16);
-  } else if (T == GT_Q8_0) {
-    r.q = ldg16(row + L.off_q + 32 * c);
-    r.q2 = ldg16(row + L.off_q + 32 * c + 16);
-    r.dm = ldg2(row + L.off_d + 2 * c);
-  } else if (T == GT_Q5_0) {
-    r.q = ldg16(row + L.off_q + 16 * c);
-    r.a = ldg4(row + L.off_qh + 4 * c);
-    r.dm = ldg2(row + L.off_d + 2 * c);
-  } else if (T == GT_Q5_1) {
-    r.q = ldg16(row + L.off_q + 16 * c);
-    r.a = ldg4(row + L.off_qh + 4 * c);
-    r.dm = ldg2(row + L.off_d + 2 * c) | (ldg2(row + L.off_m + 2 * c) << 16);
+template <bool G>
+__device__ __forceinline__ void unpack_unit(int type, const uint8_t* row, const Lay& L, int c, U8& u) {
+  switch (type) {  // folds away when `type` is a compile-time constant
+    case GT_Q4_K: {
+      uint4 w = ld16<G>(row + L.off_q + 16 * c);
+      uint4 hd = ld16<G>(row + L.off_sc + 16 * (c >> 3));
+      uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int t = 0; t < 4; t++) {
+        u.q[t] = (int)(ww[t] & 0x0F0F0F0Fu);
+        u.q[4 + t] = (int)((ww[t] >> 4) & 0x0F0F0F0Fu);
+      }
+      int sub = c & 7;
+      uint32_t sc, m;
+      // scale_min_k4 (llama-wgsl-runtime.ts:2387-2394): packed bytes q0..3 in
+      // header word y, q4..7 in z, q8..11 in w
+      if (sub < 4) {
+        sc = (hd.y >> (8 * sub)) & 63u;
+        m = (hd.z >> (8 * sub)) & 63u;
+      } else {
+        uint32_t s4 = 8 * (sub - 4);
+        uint32_t qj4 = (hd.w >> s4) & 0xFFu, qjm4 = (hd.y >> s4) & 0xFFu, qj = (hd.z >> s4) & 0xFFu;
+        sc = (qj4 & 15u) | ((qjm4 >> 6) << 4);
+        m = (qj4 >> 4) | ((qj >> 6) << 4);
+      }
+      float d = h2f_u16(hd.x), dmin = h2f_u16(hd.x >> 16);
+      u.a0 = u.a1 = d * (float)sc;
+      u.b = -(dmin * (float)m);
+      u.ko = 0;
+      break;
+    }
+    case GT_Q6_K: {
+      uint4 w = ld16<G>(row + L.off_q + 16 * c);
+      uint2 h = ld8<G>(row + L.off_q2 + 8 * c);
+      int sb = c >> 3, sub = c & 7;
+      uint32_t dd = ld2<G>(row + L.off_d + 2 * sb), scp = ld2<G>(row + L.off_sc + 16 * sb + 2 * sub);
+      uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int t = 0; t < 4; t++) {
+        uint32_t H = (t & 1) ? h.y : h.x;
+        int sh = (t >> 1) * 4;
+        u.q[t] = (int)((ww[t] & 0x0F0F0F0Fu) | (((H >> sh) << 4) & 0x30303030u));
+        u.q[4 + t] = (int)(((ww[t] >> 4) & 0x0F0F0F0Fu) | (((H >> (sh + 2)) << 4) & 0x30303030u));
+      }
+      float d = h2f_u16(dd);
+      u.a0 = d * (float)(int)(int8_t)(scp & 0xFFu);
+      u.a1 = d * (float)(int)(int8_t)(scp >> 8);
+      u.b = 0.f;
+      u.ko = -32;
+      break;
+    }
+    case GT_Q8_0: {
+      uint4 w0 = ld16<G>(row + L.off_q + 32 * c), w1 = ld16<G>(row + L.off_q + 32 * c + 16);
+      u.q[0] = (int)w0.x; u.q[1] = (int)w0.y; u.q[2] = (int)w0.z; u.q[3] = (int)w0.w;
+      u.q[4] = (int)w1.x; u.q[5] = (int)w1.y; u.q[6] = (int)w1.z; u.q[7] = (int)w1.w;
+      u.a0 = u.a1 = h2f_u16(ld2<G>(row + L.off_d + 2 * c));
+      u.b = 0.f;
+      u.ko = 0;
+      break;
+    }
+    default: {  // Q5_0, Q5_1
+      uint4 w = ld16<G>(row + L.off_q + 16 * c);
+      uint32_t qh = ld4<G>(row + L.off_qh + 4 * c);
+      uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int t = 0; t < 4; t++) {
+        u.q[t] = (int)((ww[t] & 0x0F0F0F0Fu) | ((qh << (4 - t)) & 0x10101010u));
+        u.q[4 + t] = (int)(((ww[t] >> 4) & 0x0F0F0F0Fu) | ((qh >> t) & 0x10101010u));
+      }
+      float d = h2f_u16(ld2<G>(row + L.off_d + 2 * c));
+      u.a0 = u.a1 = d;
+      if (type == GT_Q5_1) {
+        u.b = h2f_u16(ld2<G>(row + L.off_m + 2 * c));
+        u.ko = 0;
+      } else {
+        u.b = 0.f;
+        u.ko = -16;
+      }
+      break;
+    }
   }
 }
 
-__device__ __forceinline__ float h2f_bits(uint32_t b) { return __half2float(__ushort_as_half((unsigned short)(b & 0xFFFFu))); }
-__device__ __forceinline__ uint32_t w_at(const uint4& v, int t) { return t == 0 ? v.x : t == 1 ? v.y : t == 2 ? v.z : v.w; }
-
-// Contribution of one unit (32 weights) to the row's dot product.
-template <int T>
-__device__ __forceinline__ float unit_dot(const UnitRaw& r, const XUnit& x, int c) {
-  if (T == GT_Q4_K) {
-    int ah = 0, al = 0;
+__device__ __forceinline__ float unit_dot8(const U8& u, const XUnit& x) {
+  int hl = 0, ll = 0, hh = 0, lh = 0;
 #pragma unroll
-    for (int t = 0; t < 4; t++) {
-      uint32_t w = w_at(r.q, t);
-      int lo = (int)(w & 0x0F0F0F0Fu), hi = (int)((w >> 4) & 0x0F0F0F0Fu);
-      ah = __dp4a(lo, x.h[t], ah);
-      ah = __dp4a(hi, x.h[4 + t], ah);
-      al = __dp4a(lo, x.l[t], al);
-      al = __dp4a(hi, x.l[4 + t], al);
-    }
-    int dot = ah * 256 + al;
-    float d = h2f_bits(r.q2.x), dmin = h2f_bits(r.q2.x >> 16);
-    int sub = c & 7;
-    // The 12 packed scale bytes q[0..11] are header words y (q0..3), z (q4..7)
-    // and w (q8..11); scale_min_k4 (llama-wgsl-runtime.ts:2387-2394).
-    uint32_t sc, m;
-    if (sub < 4) {
-      sc = (r.q2.y >> (8 * sub)) & 63u;
-      m = (r.q2.z >> (8 * sub)) & 63u;
-    } else {
-      uint32_t qj4 = (r.q2.w >> (8 * (sub - 4))) & 0xFFu;   // q[j+4]
-      uint32_t qjm4 = (r.q2.y >> (8 * (sub - 4))) & 0xFFu;  // q[j-4]
-      uint32_t qj = (r.q2.z >> (8 * (sub - 4))) & 0xFFu;    // q[j]
-      sc = (qj4 & 15u) | ((qjm4 >> 6) << 4);
-      m = (qj4 >> 4) | ((qj >> 6) << 4);
-    }
-    float ds = d * (float)sc, dm = dmin * (float)m;
-    return ds * (x.sx * (float)dot) - dm * (x.sx * (float)(x.sa + x.sb));
-  } else if (T == GT_Q6_K) {
-    int ahl = 0, all = 0, ahh = 0, alh = 0;
-#pragma unroll
-    for (int t = 0; t < 4; t++) {
-      uint32_t w = w_at(r.q, t);
-      uint32_t H = (t & 1) ? r.b : r.a;
-      int sh = (t >> 1) * 4;
-      int lo = (int)((w & 0x0F0F0F0Fu) | (((H >> sh) << 4) & 0x30303030u));
-      int hi = (int)(((w >> 4) & 0x0F0F0F0Fu) | (((H >> (sh + 2)) << 4) & 0x30303030u));
-      ahl = __dp4a(lo, x.h[t], ahl);
-      all = __dp4a(lo, x.l[t], all);
-      ahh = __dp4a(hi, x.h[4 + t], ahh);
-      alh = __dp4a(hi, x.l[4 + t], alh);
-    }
-    int dlo = ahl * 256 + all - 32 * x.sa;
-    int dhi = ahh * 256 + alh - 32 * x.sb;
-    float d = h2f_bits(r.dm);
-    float sc0 = (float)(int)(int8_t)((r.dm >> 16) & 0xFFu);
-    float sc1 = (float)(int)(int8_t)((r.dm >> 24) & 0xFFu);
-    return (d * sc0) * (x.sx * (float)dlo) + (d * sc1) * (x.sx * (float)dhi);
-  } else if (T == GT_Q8_0) {
-    int ah = 0, al = 0;
-#pragma unroll
-    for (int t = 0; t < 4; t++) {
-      int w0 = (int)w_at(r.q, t), w1 = (int)w_at(r.q2, t);
-      ah = __dp4a(w0, x.h[t], ah);
-      ah = __dp4a(w1, x.h[4 + t], ah);
-      al = __dp4a(w0, x.l[t], al);
-      al = __dp4a(w1, x.l[4 + t], al);
-    }
-    int dot = ah * 256 + al;
-    return h2f_bits(r.dm) * (x.sx * (float)dot);
-  } else {  // Q5_0 / Q5_1
-    int ah = 0, al = 0;
-    uint32_t qh = r.a;
-#pragma unroll
-    for (int t = 0; t < 4; t++) {
-      uint32_t w = w_at(r.q, t);
-      int lo = (int)((w & 0x0F0F0F0Fu) | ((qh << (4 - t)) & 0x10101010u));
-      int hi = (int)(((w >> 4) & 0x0F0F0F0Fu) | ((qh >> t) & 0x10101010u));
-      ah = __dp4a(lo, x.h[t], ah);
-      ah = __dp4a(hi, x.h[4 + t], ah);
-      al = __dp4a(lo, x.l[t], al);
-      al = __dp4a(hi, x.l[4 + t], al);
-    }
-    int dot = ah * 256 + al;
-    float d = h2f_bits(r.dm);
-    if (T == GT_Q5_0) return d * (x.sx * (float)(dot - 16 * (x.sa + x.sb)));
-    float m = h2f_bits(r.dm >> 16);
-    return d * (x.sx * (float)dot) + m * (x.sx * (float)(x.sa + x.sb));
+  for (int t = 0; t < 4; t++) {
+    hl = __dp4a(u.q[t], x.h[t], hl);
+    ll = __dp4a(u.q[t], x.l[t], ll);
+    hh = __dp4a(u.q[4 + t], x.h[4 + t], hh);
+    lh = __dp4a(u.q[4 + t], x.l[4 + t], lh);
   }
+  int dlo = hl * 256 + ll + u.ko * x.sa;
+  int dhi = hh * 256 + lh + u.ko * x.sb;
+  return x.sx * (u.a0 * (float)dlo + u.a1 * (float)dhi + u.b * (float)(x.sa + x.sb));
 }

@@ -15,8 +15,8 @@
 
 #include "ck_layout.cuh"
 
-#define CK_THREADS 256
-#define CK_WARPS 8
+#define CK_THREADS 512
+#define CK_WARPS 16
 #define CK_KMAX 3072          // longest matvec input (x) handled (3 units per lane)
 #define CK_GMAX 8             // q heads per kv head handled by one attention unit
 #define CK_HDMAX 256          // head_dim handled
@@ -60,10 +60,27 @@ struct CkDev {
   uint32_t* cand_idx;
   int vocab;
   int ctx;
+  unsigned long long* trace;  // optional globaltimer stamps (null = off)
 };
 
+__device__ __forceinline__ unsigned long long gtimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+// Trace layout: k_mega: [phase][2] (CTA 0: phase start / phase end);
+// k_mv: [CK_TRACE_MV_BASE + cta * 8 + stage].
+#define CK_TRACE_MV_BASE 4096
+#define CK_TRACE_STAGE_BASE (CK_TRACE_MV_BASE + 8 * 1024)
+#define CK_TRACE_SLOTS (CK_TRACE_STAGE_BASE + 8 * 512)
+// sub-stage stamps of phase i on CTA 0: [CK_TRACE_STAGE_BASE + i * 8 + stage]
+__device__ __forceinline__ void stage_mark(unsigned long long* tp, int stage) {
+  if (tp && threadIdx.x == 0) tp[stage] = gtimer();
+}
+
 enum { PRO_COPY = 0, PRO_NORM = 1, PRO_SILU = 2, PRO_GELU = 3, PRO_GEMMA = 4 };
-enum { PH_EMBED = 0, PH_MATVEC = 1, PH_ATTN = 2, PH_ARGMAX1 = 3, PH_ARGMAX2 = 4, PH_SAMPLE = 5, PH_FINISH = 6 };
+enum { PH_EMBED = 0, PH_MATVEC = 1, PH_ATTN = 2, PH_ARGMAX1 = 3, PH_ARGMAX2 = 4, PH_SAMPLE = 5, PH_FINISH = 6,
+       PH_SELECT = 7 };
 
 struct Pro {
   int kind;
@@ -95,6 +112,7 @@ struct AttnPhase {
   const float *q, *k, *v;   // raw projections
   const float *qw, *kw;     // QK-norm weights (null when the model has none)
   void *kc, *vc;            // this layer's cache [kv_head][ctx][head_dim]
+  const float* inv_freq;    // [head_dim/2] theta^(-2d/head_dim) of this layer
   float* out;               // [heads * head_dim]
   float* part;              // split partials [kvh][smax][G][hd + 2]
   unsigned* counter;        // [kvh] finished splits (last CTA merges, resets)
@@ -111,7 +129,7 @@ struct EmbedPhase {
   int need_logits;
 };
 
-struct Phase {
+struct __align__(16) Phase {
   int kind;
   int grid;                 // CTAs for a standalone launch
   union {
@@ -121,10 +139,12 @@ struct Phase {
     int need_logits;        // PH_FINISH
   };
 };
+static_assert(sizeof(Phase) % 16 == 0, "phase descriptors are bulk-copied");
 
 // ---------------------------------------------------------------------------
 struct SmemMv {
   float xf[CK_KMAX];
+  float wf[CK_KMAX];
   int8_t xh[CK_KMAX];
   int8_t xl[CK_KMAX];
   float sx[CK_KMAX / 32];
@@ -133,9 +153,12 @@ struct SmemMv {
 };
 struct SmemAt {
   float qs[CK_GMAX * CK_HDMAX];
-  float wacc[CK_WARPS * 1024];
-  float wm[CK_WARPS * CK_GMAX];
-  float wl[CK_WARPS * CK_GMAX];
+  float raw[CK_GMAX * CK_HDMAX];   // q rows as produced by the projection
+  float kvw[4][CK_HDMAX];          // k, v, q-norm weight, k-norm weight
+  float wacc[CK_WARPS * CK_HDMAX];
+  float wm[CK_WARPS];
+  float wl[CK_WARPS];
+  float2 cs[CK_HDMAX / 2];
   float inv[CK_GMAX + 1];
   int last;
 };
@@ -199,71 +222,100 @@ __device__ __forceinline__ float gelu_tanh(float x) {
 __device__ void build_x(const Pro& p, int k, SmemMv& s, int cta) {
   const int tid = threadIdx.x;
   float* xf = s.xf;
+  float* wf = s.wf;
   if (p.kind == PRO_COPY) {
     for (int i = tid; i < k; i += CK_THREADS) xf[i] = p.a[i];
   } else if (p.kind == PRO_NORM) {
+    // activation and weight loads issued together; one reduction
     float ss = 0.f;
     for (int i = tid; i < k; i += CK_THREADS) {
-      float v = p.a[i];
+      float v = p.a[i], w = p.w0[i];
       xf[i] = v;
+      wf[i] = w;
       ss += v * v;
     }
     float inv = rms_inv(block_sum(ss, s.red), k, p.eps);
-    for (int i = tid; i < k; i += CK_THREADS) xf[i] = (xf[i] * inv) * p.w0[i];
+    for (int i = tid; i < k; i += CK_THREADS) xf[i] = (xf[i] * inv) * wf[i];
   } else if (p.kind == PRO_SILU) {
     for (int i = tid; i < k; i += CK_THREADS) {
-      float g = p.a[i];
-      xf[i] = (g / (1.0f + expf(-g))) * p.b[i];
+      float g = p.a[i], u = p.b[i];
+      xf[i] = (g / (1.0f + expf(-g))) * u;
     }
   } else if (p.kind == PRO_GELU) {
-    for (int i = tid; i < k; i += CK_THREADS) xf[i] = gelu_tanh(p.a[i]) * p.b[i];
-  } else {  // PRO_GEMMA
-    float ss = 0.f;
     for (int i = tid; i < k; i += CK_THREADS) {
-      float v = p.a[i];
-      xf[i] = v;
-      ss += v * v;
+      float g = p.a[i], u = p.b[i];
+      xf[i] = gelu_tanh(g) * u;
+    }
+  } else {  // PRO_GEMMA: t = rmsnorm(a) * w1; h = clamp(rin + t); x = rmsnorm(h) * w0
+    constexpr int PER = CK_KMAX / CK_THREADS;
+    float rr[PER], ww[PER];
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < PER; j++) {
+      int i = tid + j * CK_THREADS;
+      if (i < k) {
+        float v = p.a[i];
+        xf[i] = v;
+        wf[i] = p.w1[i];
+        rr[j] = p.rin[i];
+        ww[j] = p.w0[i];
+        ss += v * v;
+      }
     }
     float inv = rms_inv(block_sum(ss, s.red), k, p.eps);
     float ss2 = 0.f;
-    for (int i = tid; i < k; i += CK_THREADS) {
-      float t = (xf[i] * inv) * p.w1[i];
-      float h = fminf(fmaxf(p.rin[i] + t, -65000.0f), 65000.0f);
-      xf[i] = h;
-      if (cta == 0) p.rout[i] = h;
-      ss2 += h * h;
+#pragma unroll
+    for (int j = 0; j < PER; j++) {
+      int i = tid + j * CK_THREADS;
+      if (i < k) {
+        float t = (xf[i] * inv) * wf[i];
+        float h = fminf(fmaxf(rr[j] + t, -65000.0f), 65000.0f);
+        xf[i] = h;
+        if (cta == 0) p.rout[i] = h;
+        ss2 += h * h;
+      }
     }
     float inv2 = rms_inv(block_sum(ss2, s.red), k, p.eps);
-    for (int i = tid; i < k; i += CK_THREADS) xf[i] = (xf[i] * inv2) * p.w0[i];
+#pragma unroll
+    for (int j = 0; j < PER; j++) {
+      int i = tid + j * CK_THREADS;
+      if (i < k) xf[i] = (xf[i] * inv2) * ww[j];
+    }
   }
   __syncthreads();
 }
 
-// Quantize xf per 32-group into X = hi*256 + lo (see XUnit).
+// Quantize xf per 32-group into X = hi*256 + lo (see XUnit): half a warp per
+// group, two elements per lane, so k <= 3072 takes a single pass.
 __device__ void quant_x(int k, SmemMv& s) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31, half = (threadIdx.x >> 4) & 1, warp = threadIdx.x >> 5;
   const int U = k >> 5;
-  for (int g = warp; g < U; g += CK_WARPS) {
-    float v = s.xf[32 * g + lane];
-    float amax = warp_max(fabsf(v));
-    float step = amax / 32639.0f;
-    int X = 0;
-    if (step > 0.f && amax <= 3.0e38f) {
-      X = __float2int_rn(v / step);
-      X = max(-32639, min(32639, X));
-    }
-    int hi = (X + 128) >> 8;
-    int lo = X - 256 * hi;
-    s.xh[32 * g + lane] = (int8_t)hi;
-    s.xl[32 * g + lane] = (int8_t)lo;
-    int sum = X;
+  const int hl = lane & 15;
+  // the loop condition is warp-uniform (shuffles need the whole warp)
+  for (int gp = warp; 2 * gp < U; gp += CK_WARPS) {
+    const int g = 2 * gp + half;
+    const bool ok = g < U;
+    float2 v = ok ? *(const float2*)(s.xf + 32 * g + 2 * hl) : make_float2(0.f, 0.f);
+    float amax = fmaxf(fabsf(v.x), fabsf(v.y));
 #pragma unroll
-    for (int o = 8; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-    if (lane == 0) {
-      s.sx[g] = (amax <= 3.0e38f) ? step : __int_as_float(0x7fc00000);
-      s.s16[2 * g] = sum;
-    }
-    if (lane == 16) s.s16[2 * g + 1] = sum;
+    for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const bool fin = amax <= 3.0e38f;
+    const float step = amax * (1.0f / 32639.0f);
+    const float inv = (step > 0.f && fin) ? 32639.0f / amax : 0.f;
+    int X0 = max(-32639, min(32639, __float2int_rn(v.x * inv)));
+    int X1 = max(-32639, min(32639, __float2int_rn(v.y * inv)));
+    int h0 = (X0 + 128) >> 8, h1 = (X1 + 128) >> 8;
+    int l0 = X0 - 256 * h0, l1 = X1 - 256 * h1;
+    int sum = X0 + X1;
+#pragma unroll
+    for (int o = 4; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if (!ok) continue;
+    *(short*)(s.xh + 32 * g + 2 * hl) = (short)((h0 & 0xFF) | (h1 << 8));
+    *(short*)(s.xl + 32 * g + 2 * hl) = (short)((l0 & 0xFF) | (l1 << 8));
+    // lanes 0..7 hold weights 0..15 of the group, lanes 8..15 weights 16..31
+    if (hl == 0) s.sx[g] = fin ? step : __int_as_float(0x7fc00000);
+    if (hl == 0) s.s16[2 * g] = sum;
+    if (hl == 8) s.s16[2 * g + 1] = sum;
   }
   __syncthreads();
 }
@@ -281,92 +333,313 @@ __device__ __forceinline__ void load_xunit(const SmemMv& s, int c, XUnit& x) {
   x.sb = s.s16[2 * c + 1];
 }
 
-// R rows of one segment: all unit loads first (memory-level parallelism), the
-// lane's x units from shared memory while they are in flight, then the
-// integer dots and one warp reduction per row.
-template <int T, int UPL, int R>
-__device__ __forceinline__ void mv_group(const MvSeg& S, int row0, const SmemMv& sm, int lane) {
-  UnitRaw ur[R][UPL];
+// ---------------------------------------------------------------------------
+// Weight streaming: each CTA owns a contiguous row range of every matvec
+// segment (rows are self-contained and 16-byte aligned in the device layout),
+// packed into tiles of at most CK_TILE_BYTES.  One issuer thread copies tiles into a
+// two-buffer shared-memory ring with cp.async.bulk (TMA bulk copy, no
+// multicast) completing on an mbarrier; the ring runs ahead across phases, so
+// the next matvec's weights are in flight while this CTA is in a grid barrier
+// or an attention phase.  Consumers read the tile from shared memory.
+#define CK_TILE_BYTES (64 * 1024)
+#define CK_TILE_PIECES 4
+#define CK_ISSUER (CK_THREADS - 32)   // lane 0 of the last warp copies tiles
+
+struct Piece {
+  int seg, r0, r1;
+  uint32_t soff;
+};
+struct Tile {
+  int phase, npc;
+  uint32_t bytes;
+  Piece pc[CK_TILE_PIECES];
+};
+struct Cursor {
+  int phase, seg, row;
+};
+
+struct Ring {
+  uint8_t* buf;            // 2 x CK_TILE_BYTES, 128-byte aligned
+  uint64_t* full;          // 2 mbarriers
+  const Phase* ph;
+  int nph;
+  Cursor issue;            // issuer thread: next tile to copy
+  unsigned issued;         // issuer thread: tiles copied so far
+  unsigned consumed;       // every thread: tiles consumed so far
+  int ok;                  // 0 once a wait gave up
+};
+
+// Contiguous row range of a CTA (n * ncta < 2^31 for every model handled).
+__device__ __forceinline__ void seg_range(const MvSeg& S, int cta, int ncta, int& lo, int& hi) {
+  lo = (S.n * cta) / ncta;
+  hi = (S.n * (cta + 1)) / ncta;
+}
+
+// Next tile from cursor `c` (phases [c.phase, last)), false when none.
+// `last` bounds the search: nph for the issuer, phase + 1 for consumers.
+__device__ bool next_tile(const Phase* ph, int last, int cta, int ncta, Cursor& c, Tile& t) {
+  while (c.phase < last) {
+    const Phase& p = ph[c.phase];
+    if (p.kind != PH_MATVEC) {
+      c.phase++; c.seg = 0; c.row = -1;
+      continue;
+    }
+    const MvPhase& m = p.mv;
+    t.phase = c.phase;
+    t.npc = 0;
+    t.bytes = 0;
+    while (c.seg < m.nseg && t.npc < CK_TILE_PIECES) {
+      int lo, hi;
+      seg_range(m.seg[c.seg], cta, ncta, lo, hi);
+      if (c.row < lo) c.row = lo;
+      if (c.row >= hi) { c.seg++; c.row = -1; continue; }
+      uint32_t rb = m.seg[c.seg].L.row_bytes;
+      int fit = (int)((CK_TILE_BYTES - t.bytes) / rb);
+      if (fit <= 0) break;
+      int take = min(fit, hi - c.row);
+      t.pc[t.npc].seg = c.seg;
+      t.pc[t.npc].r0 = c.row;
+      t.pc[t.npc].r1 = c.row + take;
+      t.pc[t.npc].soff = t.bytes;
+      t.npc++;
+      t.bytes += (uint32_t)take * rb;
+      c.row += take;
+    }
+    if (t.npc > 0) return true;
+    c.phase++; c.seg = 0; c.row = -1;
+  }
+  return false;
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t* b, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_fence_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* b, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(done)
+      : "r"(smem_u32(b)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+// Same, marking the lines evict-first in L2: streamed weights are read once
+// per token and should not push activations, norms or the KV cache out.
+__device__ __forceinline__ void bulk_g2s_stream(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(pol)
+      : "memory");
+}
+
+// issuer thread: copy the next tile (if any) into buffer issued & 1
+__device__ void ring_issue(Ring& R, int cta, int ncta) {
+  Tile t;
+  if (!next_tile(R.ph, R.nph, cta, ncta, R.issue, t)) return;
+  int b = R.issued & 1;
+  uint64_t* bar = R.full + b;
+  mbar_expect_tx(bar, t.bytes);
+  const MvPhase& m = R.ph[t.phase].mv;
+  for (int i = 0; i < t.npc; i++) {
+    const MvSeg& S = m.seg[t.pc[i].seg];
+    uint32_t rb = S.L.row_bytes;
+    bulk_g2s_stream(R.buf + (size_t)b * CK_TILE_BYTES + t.pc[i].soff, S.w + (size_t)t.pc[i].r0 * rb,
+                    (uint32_t)(t.pc[i].r1 - t.pc[i].r0) * rb, bar);
+  }
+  R.issued++;
+}
+
+// Shared-memory layout of the streaming kernels (dynamic part):
+//   [tile buffer 0][tile buffer 1][3 mbarriers, 128 B][phase descriptors]
+#define CK_DYN_BARS (2 * CK_TILE_BYTES)
+#define CK_DYN_PHASES (2 * CK_TILE_BYTES + 128)
+#define CK_PHASE_SMEM_MAX (48 * 1024)
+#define CK_DYN_SMEM_MAX (CK_DYN_PHASES + CK_PHASE_SMEM_MAX)
+
+// Start of a launch: init the barriers, stage the phase descriptors in shared
+// memory with one bulk copy (every later descriptor read is a shared-memory
+// read), then put the first two weight tiles in flight.  Returns the staged
+// descriptors, or null when the wait gave up.
+__device__ const Phase* launch_start(Ring& R, uint8_t* dyn, const Phase* gph, int nph, int cta, int ncta,
+                                     int* err, int* abort_flag) {
+  uint64_t* bars = (uint64_t*)(dyn + CK_DYN_BARS);
+  Phase* sph = (Phase*)(dyn + CK_DYN_PHASES);
+  if (threadIdx.x == 0) {
+    mbar_init(bars, 1);
+    mbar_init(bars + 1, 1);
+    mbar_init(bars + 2, 1);
+    mbar_fence_init();
+    uint32_t bytes = (uint32_t)(nph * sizeof(Phase));
+    mbar_expect_tx(bars + 2, bytes);
+    bulk_g2s(sph, gph, bytes, bars + 2);
+  }
+  __syncthreads();
+  unsigned spins = 0;
+  while (!mbar_try_wait(bars + 2, 0)) {
+    if (++spins > (1u << 20)) {
+      atomicOr(err, CK_DERR_BARRIER);
+      atomicExch(abort_flag, 1);
+      return nullptr;
+    }
+  }
+  R.buf = dyn;
+  R.full = bars;
+  R.ph = sph;
+  R.nph = nph;
+  R.issue.phase = 0; R.issue.seg = 0; R.issue.row = -1;
+  R.issued = 0;
+  R.consumed = 0;
+  R.ok = 1;
+  if (threadIdx.x == CK_ISSUER) {
+    ring_issue(R, cta, ncta);
+    ring_issue(R, cta, ncta);
+  }
+  return sph;
+}
+
+// Wait for tile `consumed` (bounded: ~seconds, then flags and gives up).
+__device__ bool ring_wait(Ring& R, int* err, int* abort_flag) {
+  uint64_t* bar = R.full + (R.consumed & 1);
+  uint32_t par = (R.consumed >> 1) & 1u;
+  unsigned spins = 0;
+  while (!mbar_try_wait(bar, par)) {
+    if (++spins > (1u << 20)) {
+      if (err) atomicOr(err, CK_DERR_BARRIER);
+      if (abort_flag) atomicExch(abort_flag, 1);
+      return false;
+    }
+    if ((spins & 1023u) == 0 && abort_flag && *(volatile int*)abort_flag) return false;
+  }
+  return true;
+}
+
+// After every thread finished reading tile `consumed`: free its buffer and
+// refill it with the tile two ahead.
+__device__ __forceinline__ void ring_release(Ring& R, int cta, int ncta) {
+  __syncthreads();
+  R.consumed++;
+  if (threadIdx.x == CK_ISSUER && R.issued < R.consumed + 2) ring_issue(R, cta, ncta);
+}
+
+// Rows of one tile piece, read from shared memory.  With one unit per lane
+// (ONE) the lane's x unit stays in registers for the whole piece and a warp
+// step handles two rows so their unpacks, dots and reductions overlap; with
+// 2-3 units per lane the x units are re-read from shared memory per unit (the
+// units of a row already overlap) to stay inside the register budget.  The
+// block type is a runtime switch inside the unpack: compiling the row loop
+// per type multiplies register pressure past the 128-register budget.
+template <bool ONE>
+__device__ __forceinline__ void mv_piece(const MvSeg& S, const uint8_t* base, int r0, int nrows, const SmemMv& s) {
+  constexpr int R = ONE ? 2 : 1;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int U = S.L.U;
+  const int T = S.L.type;
+  const int upl = ONE ? 1 : (U + 31) >> 5;
+  const uint32_t rb = S.L.row_bytes;
+  float* __restrict__ out = S.out;
+  const float* __restrict__ add = S.add;
+  if (warp >= nrows) return;
+  XUnit x0;
+  if (ONE && lane < U) load_xunit(s, lane, x0);
+  for (int r = warp; r < nrows; r += R * CK_WARPS) {
+    float acc[R];
 #pragma unroll
-  for (int r = 0; r < R; r++) {
-    int row = row0 + r;
-    if (row < S.n) {
-      const uint8_t* base = S.w + (size_t)row * S.L.row_bytes;
-#pragma unroll
-      for (int j = 0; j < UPL; j++) {
-        int c = lane + 32 * j;
-        if (c < U) load_unit<T>(base, S.L, c, ur[r][j]);
+    for (int i = 0; i < R; i++) {
+      acc[i] = 0.f;
+      const int rr = r + i * CK_WARPS;
+      if (rr < nrows) {
+        const uint8_t* row = base + (size_t)rr * rb;
+        if (ONE) {
+          if (lane < U) {
+            U8 u;
+            unpack_unit<false>(T, row, S.L, lane, u);
+            acc[i] += unit_dot8(u, x0);
+          }
+        } else {
+#pragma unroll 1
+          for (int j = 0; j < upl; j++) {
+            int c = lane + 32 * j;
+            if (c < U) {
+              U8 u;
+              unpack_unit<false>(T, row, S.L, c, u);
+              XUnit xj;
+              load_xunit(s, c, xj);
+              acc[i] += unit_dot8(u, xj);
+            }
+          }
+        }
       }
     }
-  }
-  float acc[R];
 #pragma unroll
-  for (int r = 0; r < R; r++) acc[r] = 0.f;
+    for (int o = 16; o > 0; o >>= 1)
 #pragma unroll
-  for (int j = 0; j < UPL; j++) {
-    int c = lane + 32 * j;
-    if (c < U) {
-      XUnit xu;
-      load_xunit(sm, c, xu);
+      for (int i = 0; i < R; i++) acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], o);
+    float v = acc[0];
 #pragma unroll
-      for (int r = 0; r < R; r++)
-        if (row0 + r < S.n) acc[r] += unit_dot<T>(ur[r][j], xu, c);
-    }
-  }
-#pragma unroll
-  for (int r = 0; r < R; r++) {
-    int row = row0 + r;
-    float v = warp_sum(acc[r]);
-    if (lane == 0 && row < S.n) S.out[row] = S.add ? S.add[row] + v : v;
+    for (int i = 1; i < R; i++)
+      if (lane == i) v = acc[i];
+    const int rr = r + lane * CK_WARPS;
+    if (lane < R && rr < nrows) out[r0 + rr] = add ? add[r0 + rr] + v : v;
   }
 }
 
-template <int T, int UPL, int R>
-__device__ __noinline__ void mv_seg(const MvSeg& S, int first, int ngr, int nw, const SmemMv& sm, int lane) {
-  for (int gi = first; gi < ngr; gi += nw) mv_group<T, UPL, R>(S, gi * R, sm, lane);
-}
-
-template <int UPL>
-__device__ __forceinline__ void mv_run(const MvPhase& P, SmemMv& s, int cta, int ncta) {
-  constexpr int R = UPL == 1 ? 4 : (UPL == 2 ? 2 : 1);
+__device__ __forceinline__ void mv_run(const MvPhase& P, int phase_idx, SmemMv& s, Ring& R, int cta, int ncta,
+                                    int* err, int* abort_flag, unsigned long long* tp) {
+  stage_mark(tp, 0);
   build_x(P.pro, P.k, s, cta);
+  stage_mark(tp, 1);
   quant_x(P.k, s);
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  // consecutive row groups go to different CTAs first, spreading every
-  // segment over all SMs
-  const int gw = warp * ncta + cta, nw = ncta * CK_WARPS;
-  int base = 0;
-  for (int si = 0; si < P.nseg; si++) {
-    const MvSeg& S = P.seg[si];
-    const int ngr = (S.n + R - 1) / R;
-    int first = (gw - base) % nw;
-    if (first < 0) first += nw;
-    switch (S.L.type) {
-      case GT_Q4_K: mv_seg<GT_Q4_K, UPL, R>(S, first, ngr, nw, s, lane); break;
-      case GT_Q6_K: mv_seg<GT_Q6_K, UPL, R>(S, first, ngr, nw, s, lane); break;
-      case GT_Q8_0: mv_seg<GT_Q8_0, UPL, R>(S, first, ngr, nw, s, lane); break;
-      case GT_Q5_0: mv_seg<GT_Q5_0, UPL, R>(S, first, ngr, nw, s, lane); break;
-      case GT_Q5_1: mv_seg<GT_Q5_1, UPL, R>(S, first, ngr, nw, s, lane); break;
+  stage_mark(tp, 2);
+  int ntile = 0;
+  const int upl = (P.k + 1023) >> 10;
+  Cursor cur;
+  cur.phase = phase_idx; cur.seg = 0; cur.row = -1;
+  Tile t;
+  while (next_tile(R.ph, phase_idx + 1, cta, ncta, cur, t)) {
+    if (!ring_wait(R, err, abort_flag)) { R.ok = 0; return; }
+    if (ntile == 0) stage_mark(tp, 3);
+    const uint8_t* tb = R.buf + (size_t)(R.consumed & 1) * CK_TILE_BYTES;
+    for (int i = 0; i < t.npc; i++) {
+      const MvSeg& S = P.seg[t.pc[i].seg];
+      const uint8_t* base = tb + t.pc[i].soff;
+      int r0 = t.pc[i].r0, nrows = t.pc[i].r1 - t.pc[i].r0;
+      if (upl <= 1) mv_piece<true>(S, base, r0, nrows, s);
+      else mv_piece<false>(S, base, r0, nrows, s);
     }
-    base += ngr;
+    if (ntile == 0) stage_mark(tp, 4);
+    ring_release(R, cta, ncta);
+    if (ntile == 0) stage_mark(tp, 5);
+    ntile++;
   }
+  stage_mark(tp, 6);
 }
 
-__device__ __forceinline__ void phase_matvec(const MvPhase& P, Smem& sm, int cta, int ncta) {
-  int upl = (P.k + 1023) >> 10;
-  if (upl <= 1) mv_run<1>(P, sm.mv, cta, ncta);
-  else if (upl == 2) mv_run<2>(P, sm.mv, cta, ncta);
-  else mv_run<3>(P, sm.mv, cta, ncta);
+__device__ __forceinline__ void phase_matvec(const MvPhase& P, int phase_idx, Smem& sm, Ring& R, int cta,
+                                             int ncta, int* err, int* abort_flag, unsigned long long* tp = nullptr) {
+  mv_run(P, phase_idx, sm.mv, R, cta, ncta, err, abort_flag, tp);
 }
 
 // ---------------------------------------------------------------------------
 // Embedding (GGUF_*_EMBEDDING_WGSL, :2615-2866): row tokens[pos] of the
 // (tied) table dequantized in WGSL order, times EMBEDDING_SCALE.  Also marks
 // the repetition-penalty id set when this step computes logits.
-__device__ __forceinline__ void phase_embed(const EmbedPhase& P, const CkDev& D, int cta, int ncta) {
+__device__ __forceinline__ void phase_embed(const EmbedPhase& P, const CkDev& D, int cta, int ncta, int pos) {
   const CkState* st = D.st;
-  int pos = st->pos;
   uint32_t token = D.tokens[pos];
   if (token >= (uint32_t)D.vocab) {
     if (cta == 0 && threadIdx.x == 0) atomicOr(&D.st->err, CK_DERR_TOKEN);
@@ -393,15 +666,18 @@ __device__ __forceinline__ void phase_embed(const EmbedPhase& P, const CkDev& D,
 // scores over [start, pos] with start = pos+1-window for windowed layers,
 // scaled by 1/sqrt(head_dim), softmax, weighted sum of V.  The softmax is
 // computed online per split and merged by the last split to finish.
-__device__ __forceinline__ float rope_angle(uint32_t theta, int d, int hd, int pos) {
-  float e = (-2.0f * (float)d) / (float)hd;
-  return (float)pos * powf((float)theta, e);
+// theta^(-2d/hd) for d < hd/2, the inverse frequency of rope_angle
+// (llama-wgsl-runtime.ts:2885-2888), built once per layer at load time.
+__global__ void k_inv_freq(float* out, uint32_t theta, int hd) {
+  int d = threadIdx.x;
+  if (d < hd / 2) out[d] = powf((float)theta, (-2.0f * (float)d) / (float)hd);
 }
 
 // Normalize (optional) + rotate one head of length hd from src into dst
-// (shared memory); `inv` is the head's 1/rms (ignored without weights).
+// (shared memory); `inv` is the head's 1/rms (ignored without weights);
+// cs holds cos/sin of each pair's angle.
 __device__ __forceinline__ void rope_head(const float* src, const float* w, float inv, float* dst, int hd, int inter,
-                                          uint32_t theta, int pos, int t0, int tstride) {
+                                          const float2* cs, int t0, int tstride) {
   int half = hd >> 1;
   for (int d = t0; d < half; d += tstride) {
     int i0 = inter ? 2 * d : d, i1 = inter ? 2 * d + 1 : d + half;
@@ -410,8 +686,7 @@ __device__ __forceinline__ void rope_head(const float* src, const float* w, floa
       a = (a * inv) * w[i0];
       b = (b * inv) * w[i1];
     }
-    float ang = rope_angle(theta, d, hd, pos);
-    float co = cosf(ang), si = sinf(ang);
+    float co = cs[d].x, si = cs[d].y;
     dst[i0] = a * co - b * si;
     dst[i1] = a * si + b * co;
   }
@@ -447,8 +722,9 @@ __device__ __forceinline__ void load_kv(const void* base, int kv_f32, size_t off
   }
 }
 
-template <int E, int GM>
-__device__ __forceinline__ void attn_unit(const AttnPhase& P, SmemAt& s, int kvh, int split, int pos) {
+template <int E>
+__device__ __forceinline__ void attn_unit(const AttnPhase& P, SmemAt& s, int kvh, int split, int pos,
+                                          unsigned long long* tp) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int hd = P.hd, G = P.heads / P.kvh;
   const int start = (P.window != 0 && pos + 1 > P.window) ? pos + 1 - P.window : 0;
@@ -461,29 +737,49 @@ __device__ __forceinline__ void attn_unit(const AttnPhase& P, SmemAt& s, int kvh
   const int t1 = min(t0 + chunk, pos + 1);
   const bool owner = split == S - 1;   // the split holding `pos` stores K/V there
 
+  // --- every input of this unit in one round of loads ----------------------
+  stage_mark(tp, 0);
+  for (int d = tid; d < (hd >> 1); d += CK_THREADS) {
+    // angle = pos * theta^(-2d/hd) (rope_angle, :2885-2888); the power is the
+    // per-layer table built at load time with the same powf
+    float ang = (float)pos * P.inv_freq[d];
+    float sn, cn;
+    sincosf(ang, &sn, &cn);
+    s.cs[d] = make_float2(cn, sn);
+  }
+  for (int i = tid; i < G * hd; i += CK_THREADS) s.raw[i] = P.q[(size_t)kvh * G * hd + i];
+  for (int d = tid; d < hd; d += CK_THREADS) {
+    if (owner) {
+      s.kvw[0][d] = P.k[(size_t)kvh * hd + d];
+      s.kvw[1][d] = P.v[(size_t)kvh * hd + d];
+      if (P.kw) s.kvw[3][d] = P.kw[d];
+    }
+    if (P.qw) s.kvw[2][d] = P.qw[d];
+  }
+  __syncthreads();
   // --- per-head 1/rms of q (and k) for the QK-norm -----------------------
   if (P.qw) {
     for (int g = warp; g < G + (owner ? 1 : 0); g += CK_WARPS) {
-      const float* src = g < G ? P.q + (size_t)(kvh * G + g) * hd : P.k + (size_t)kvh * hd;
+      const float* src = g < G ? s.raw + g * hd : s.kvw[0];
       float ss = 0.f;
       for (int d = lane; d < hd; d += 32) ss += src[d] * src[d];
       ss = warp_sum(ss);
       if (lane == 0) s.inv[g] = rms_inv(ss, hd, P.eps);
     }
+    __syncthreads();
   }
-  __syncthreads();
   // --- q: norm + rope into shared memory; owner: k/v into the cache --------
   for (int g = 0; g < G; g++)
-    rope_head(P.q + (size_t)(kvh * G + g) * hd, P.qw, P.qw ? s.inv[g] : 1.f, s.qs + g * hd, hd, P.interleaved,
-              P.theta, pos, tid, CK_THREADS);
+    rope_head(s.raw + g * hd, P.qw ? s.kvw[2] : nullptr, P.qw ? s.inv[g] : 1.f, s.qs + g * hd, hd, P.interleaved,
+              s.cs, tid, CK_THREADS);
   if (owner) {
     float* kst = s.wacc;  // scratch for the rotated k row
-    rope_head(P.k + (size_t)kvh * hd, P.kw, P.kw ? s.inv[G] : 1.f, kst, hd, P.interleaved, P.theta, pos, tid,
+    rope_head(s.kvw[0], P.kw ? s.kvw[3] : nullptr, P.kw ? s.inv[G] : 1.f, kst, hd, P.interleaved, s.cs, tid,
               CK_THREADS);
     __syncthreads();
     size_t cb = ((size_t)kvh * P.ctx + pos) * hd;
     for (int d = tid; d < hd; d += CK_THREADS) {
-      float kv = kst[d], vv = P.v[(size_t)kvh * hd + d];
+      float kv = kst[d], vv = s.kvw[1][d];
       if (P.kv_f32) {
         ((float*)P.kc)[cb + d] = kv;
         ((float*)P.vc)[cb + d] = vv;
@@ -494,70 +790,97 @@ __device__ __forceinline__ void attn_unit(const AttnPhase& P, SmemAt& s, int kvh
     }
   }
   __syncthreads();
+  stage_mark(tp, 1);
 
-  // --- online softmax over this split's positions ---------------------------
-  float q[GM][E], acc[GM][E], m[GM], l[GM];
+  // --- online softmax: warps split into G groups, one q head per group -----
+  const int wpg = CK_WARPS / G;      // warps per head (G <= 8)
+  const int g = warp / wpg, sub = warp % wpg;
+  float q[E], acc[E], m = -INFINITY, l = 0.f;
 #pragma unroll
-  for (int g = 0; g < GM; g++) {
-    m[g] = -INFINITY;
-    l[g] = 0.f;
+  for (int e = 0; e < E; e++) {
+    q[e] = g < G ? s.qs[g * hd + lane * E + e] : 0.f;
+    acc[e] = 0.f;
+  }
+  if (g < G) {
+    const size_t base = (size_t)kvh * P.ctx * hd + lane * E;
+    int t = t0 + sub;
+    for (; t + wpg < t1; t += 2 * wpg) {   // two positions in flight
+      float k0[E], v0[E], k1[E], v1[E];
+      load_kv<E>(P.kc, P.kv_f32, base + (size_t)t * hd, k0);
+      load_kv<E>(P.kc, P.kv_f32, base + (size_t)(t + wpg) * hd, k1);
+      load_kv<E>(P.vc, P.kv_f32, base + (size_t)t * hd, v0);
+      load_kv<E>(P.vc, P.kv_f32, base + (size_t)(t + wpg) * hd, v1);
+      float d0 = 0.f, d1 = 0.f;
 #pragma unroll
-    for (int e = 0; e < E; e++) {
-      q[g][e] = g < G ? s.qs[g * hd + lane * E + e] : 0.f;
-      acc[g][e] = 0.f;
+      for (int e = 0; e < E; e++) { d0 += q[e] * k0[e]; d1 += q[e] * k1[e]; }
+      float s0 = warp_sum(d0) * P.scale, s1 = warp_sum(d1) * P.scale;
+      float mn = fmaxf(m, fmaxf(s0, s1));
+      float c = expf(m - mn), p0 = expf(s0 - mn), p1 = expf(s1 - mn);
+      l = l * c + p0 + p1;
+#pragma unroll
+      for (int e = 0; e < E; e++) acc[e] = acc[e] * c + p0 * v0[e] + p1 * v1[e];
+      m = mn;
+    }
+    if (t < t1) {
+      float k0[E], v0[E];
+      load_kv<E>(P.kc, P.kv_f32, base + (size_t)t * hd, k0);
+      load_kv<E>(P.vc, P.kv_f32, base + (size_t)t * hd, v0);
+      float d0 = 0.f;
+#pragma unroll
+      for (int e = 0; e < E; e++) d0 += q[e] * k0[e];
+      float s0 = warp_sum(d0) * P.scale;
+      float mn = fmaxf(m, s0);
+      float c = expf(m - mn), p0 = expf(s0 - mn);
+      l = l * c + p0;
+#pragma unroll
+      for (int e = 0; e < E; e++) acc[e] = acc[e] * c + p0 * v0[e];
+      m = mn;
     }
   }
-  for (int t = t0 + warp; t < t1; t += CK_WARPS) {
-    float kf[E], vf[E];
-    size_t off = ((size_t)kvh * P.ctx + t) * hd + lane * E;
-    load_kv<E>(P.kc, P.kv_f32, off, kf);
-    load_kv<E>(P.vc, P.kv_f32, off, vf);
-#pragma unroll
-    for (int g = 0; g < GM; g++) {
-      if (g < G) {
-        float d = 0.f;
-#pragma unroll
-        for (int e = 0; e < E; e++) d += q[g][e] * kf[e];
-        float sc = warp_sum(d) * P.scale;
-        float mn = fmaxf(m[g], sc);
-        float c = expf(m[g] - mn), p = expf(sc - mn);
-        l[g] = l[g] * c + p;
-#pragma unroll
-        for (int e = 0; e < E; e++) acc[g][e] = acc[g][e] * c + p * vf[e];
-        m[g] = mn;
-      }
-    }
+  // --- merge the warps of each head ------------------------------------------
+  stage_mark(tp, 2);
+  if (lane == 0) {
+    s.wm[warp] = m;
+    s.wl[warp] = l;
   }
-  // --- merge the warps --------------------------------------------------------
 #pragma unroll
-  for (int g = 0; g < GM; g++) {
-    if (g < G) {
-      if (lane == 0) {
-        s.wm[warp * CK_GMAX + g] = m[g];
-        s.wl[warp * CK_GMAX + g] = l[g];
-      }
-#pragma unroll
-      for (int e = 0; e < E; e++) s.wacc[warp * 1024 + g * hd + lane * E + e] = acc[g][e];
-    }
-  }
+  for (int e = 0; e < E; e++) s.wacc[warp * CK_HDMAX + lane * E + e] = acc[e];
   __syncthreads();
+  if (S == 1) {   // one split covers the context: no partials, no merge
+    for (int i = tid; i < G * hd; i += CK_THREADS) {
+      int gg = i / hd, d = i % hd;
+      float M = -INFINITY;
+      for (int w = gg * wpg; w < gg * wpg + wpg; w++) M = fmaxf(M, s.wm[w]);
+      float L = 0.f, A = 0.f;
+      for (int w = gg * wpg; w < gg * wpg + wpg; w++) {
+        float wm = s.wm[w];
+        if (wm == -INFINITY) continue;
+        float f = expf(wm - M);
+        L += s.wl[w] * f;
+        A += s.wacc[w * CK_HDMAX + d] * f;
+      }
+      P.out[(size_t)(kvh * G + gg) * hd + d] = A / L;
+    }
+    stage_mark(tp, 3);
+    return;
+  }
   float* part = P.part + ((size_t)kvh * P.smax + split) * G * (hd + 2);
   for (int i = tid; i < G * hd; i += CK_THREADS) {
-    int g = i / hd, d = i % hd;
+    int gg = i / hd, d = i % hd;
     float M = -INFINITY;
-    for (int w = 0; w < CK_WARPS; w++) M = fmaxf(M, s.wm[w * CK_GMAX + g]);
+    for (int w = gg * wpg; w < gg * wpg + wpg; w++) M = fmaxf(M, s.wm[w]);
     float L = 0.f, A = 0.f;
-    for (int w = 0; w < CK_WARPS; w++) {
-      float wm = s.wm[w * CK_GMAX + g];
+    for (int w = gg * wpg; w < gg * wpg + wpg; w++) {
+      float wm = s.wm[w];
       if (wm == -INFINITY) continue;
       float f = expf(wm - M);
-      L += s.wl[w * CK_GMAX + g] * f;
-      A += s.wacc[w * 1024 + g * hd + d] * f;
+      L += s.wl[w] * f;
+      A += s.wacc[w * CK_HDMAX + d] * f;
     }
-    part[g * (hd + 2) + 2 + d] = A;
+    part[gg * (hd + 2) + 2 + d] = A;
     if (d == 0) {
-      part[g * (hd + 2)] = M;
-      part[g * (hd + 2) + 1] = L;
+      part[gg * (hd + 2)] = M;
+      part[gg * (hd + 2) + 1] = L;
     }
   }
   // --- last split to finish merges all splits --------------------------------
@@ -572,38 +895,32 @@ __device__ __forceinline__ void attn_unit(const AttnPhase& P, SmemAt& s, int kvh
   __threadfence();
   const float* pk = P.part + (size_t)kvh * P.smax * G * (hd + 2);
   for (int i = tid; i < G * hd; i += CK_THREADS) {
-    int g = i / hd, d = i % hd;
+    int gg = i / hd, d = i % hd;
     float M = -INFINITY;
-    for (int sp = 0; sp < S; sp++) M = fmaxf(M, __ldcg(pk + ((size_t)sp * G + g) * (hd + 2)));
+    for (int sp = 0; sp < S; sp++) M = fmaxf(M, __ldcg(pk + ((size_t)sp * G + gg) * (hd + 2)));
     float L = 0.f, A = 0.f;
     for (int sp = 0; sp < S; sp++) {
-      const float* pp = pk + ((size_t)sp * G + g) * (hd + 2);
+      const float* pp = pk + ((size_t)sp * G + gg) * (hd + 2);
       float f = expf(__ldcg(pp) - M);
       L += __ldcg(pp + 1) * f;
       A += __ldcg(pp + 2 + d) * f;
     }
-    P.out[(size_t)(kvh * G + g) * hd + d] = A / L;
+    P.out[(size_t)(kvh * G + gg) * hd + d] = A / L;
   }
   if (tid == 0) P.counter[kvh] = 0u;
 }
 
-// group sizes reachable under the host's G * head_dim <= 1024 limit
-template <int E>
-__device__ __forceinline__ void attn_dispatch_g(const AttnPhase& P, SmemAt& s, int kvh, int split, int pos) {
-  int G = P.heads / P.kvh;
-  if (G <= 2) attn_unit<E, 2>(P, s, kvh, split, pos);
-  else if (G <= 4 || E == 8) attn_unit<E, 4>(P, s, kvh, split, pos);
-  else attn_unit<E, (E == 8 ? 4 : 8)>(P, s, kvh, split, pos);
-}
-
-__device__ __forceinline__ void phase_attn(const AttnPhase& P, Smem& sm, const CkDev& D, int cta, int ncta) {
-  int pos = D.st->pos;
+__device__ __forceinline__ void phase_attn(const AttnPhase& P, Smem& sm, const CkDev& D, int cta, int ncta, int pos,
+                                           unsigned long long* tp = nullptr) {
+  // split-major: the active split 0 units of every kv head land on
+  // different CTAs even when the context needs one split only
   int units = P.kvh * P.smax;
   for (int u = cta; u < units; u += ncta) {
-    int kvh = u / P.smax, split = u % P.smax;
-    if (P.hd == 64) attn_dispatch_g<2>(P, sm.at, kvh, split, pos);
-    else if (P.hd == 128) attn_dispatch_g<4>(P, sm.at, kvh, split, pos);
-    else attn_dispatch_g<8>(P, sm.at, kvh, split, pos);
+    int kvh = u % P.kvh, split = u / P.kvh;
+    unsigned long long* up = (tp && u == cta) ? tp : nullptr;
+    if (P.hd == 64) attn_unit<2>(P, sm.at, kvh, split, pos, up);
+    else if (P.hd == 128) attn_unit<4>(P, sm.at, kvh, split, pos, up);
+    else attn_unit<8>(P, sm.at, kvh, split, pos, up);
     __syncthreads();
   }
 }
@@ -645,7 +962,7 @@ __device__ __forceinline__ void phase_argmax1(const CkDev& D, Smem& sm, int cta,
     uint32_t i = (uint32_t)g * 256u + threadIdx.x;
     float v;
     uint32_t idx;
-    if (i < (uint32_t)D.vocab) {
+    if (threadIdx.x < 256 && i < (uint32_t)D.vocab) {
       v = D.logits[i];
       if (pen && ((D.pen_mask[i >> 5] >> (i & 31)) & 1u)) v = v > 0.f ? v / penalty : v * penalty;
       idx = i;
@@ -801,36 +1118,66 @@ __device__ __forceinline__ void phase_finish(int need_logits, const CkDev& D, in
   }
 }
 
+// argmax stage 2 -> sampling -> end of step, on CTA 0 in one phase.
+__device__ __forceinline__ void phase_select(int need_logits, const CkDev& D, Smem& sm, int cta) {
+  if (cta != 0) return;
+  phase_argmax2(D, sm, 0);
+  __syncthreads();
+  phase_sample(D, sm, 0);
+  __syncthreads();
+  phase_finish(need_logits, D, 0);
+}
+
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ void run_phase(const Phase& p, Smem& sm, const CkDev& D, int cta, int ncta) {
+__device__ __forceinline__ void run_phase(const Phase* ph, int i, Smem& sm, Ring& R, const CkDev& D, int cta,
+                                          int ncta, int pos) {
+  const Phase& p = ph[i];
+  unsigned long long* tp =
+      (D.trace && cta == 0 && i < 512) ? D.trace + CK_TRACE_STAGE_BASE + i * 8 : nullptr;
   switch (p.kind) {
-    case PH_EMBED: phase_embed(p.em, D, cta, ncta); break;
-    case PH_MATVEC: phase_matvec(p.mv, sm, cta, ncta); break;
-    case PH_ATTN: phase_attn(p.at, sm, D, cta, ncta); break;
+    case PH_EMBED: phase_embed(p.em, D, cta, ncta, pos); break;
+    case PH_MATVEC: phase_matvec(p.mv, i, sm, R, cta, ncta, &D.st->err, &D.st->abort_flag, tp); break;
+    case PH_ATTN: phase_attn(p.at, sm, D, cta, ncta, pos, tp); break;
     case PH_ARGMAX1: phase_argmax1(D, sm, cta, ncta); break;
     case PH_ARGMAX2: phase_argmax2(D, sm, cta); break;
     case PH_SAMPLE: phase_sample(D, sm, cta); break;
     case PH_FINISH: phase_finish(p.need_logits, D, cta); break;
+    case PH_SELECT: phase_select(p.need_logits, D, sm, cta); break;
   }
 }
 
+// Dynamic shared memory: the tile ring (2 x CK_TILE_BYTES) + 2 mbarriers.
+
 // One launch per phase (CUDA-graph mode): one kernel per phase kind so each
 // gets its own register allocation.
-__global__ void __launch_bounds__(CK_THREADS, 2) k_mv(const Phase* __restrict__ ph, CkDev D) {
-  __shared__ SmemMv sm;
-  const MvPhase& P = ph->mv;
-  int upl = (P.k + 1023) >> 10;
-  if (upl <= 1) mv_run<1>(P, sm, blockIdx.x, gridDim.x);
-  else if (upl == 2) mv_run<2>(P, sm, blockIdx.x, gridDim.x);
-  else mv_run<3>(P, sm, blockIdx.x, gridDim.x);
-}
-__global__ void __launch_bounds__(CK_THREADS, 2) k_attn(const Phase* __restrict__ ph, CkDev D) {
+__global__ void __launch_bounds__(CK_THREADS, 1) k_mv(const Phase* __restrict__ ph, CkDev D) {
+  extern __shared__ __align__(128) uint8_t dyn[];
   __shared__ Smem sm;
-  phase_attn(ph->at, sm, D, blockIdx.x, gridDim.x);
+  unsigned long long* tr = (D.trace && threadIdx.x == 0 && blockIdx.x < 1024)
+                               ? D.trace + CK_TRACE_MV_BASE + blockIdx.x * 8 : nullptr;
+  if (tr) tr[0] = gtimer();
+  Ring R;
+  const Phase* sph = launch_start(R, dyn, ph, 1, blockIdx.x, gridDim.x, &D.st->err, &D.st->abort_flag);
+  if (!sph) return;
+  if (tr) tr[1] = gtimer();
+  phase_matvec(sph->mv, 0, sm, R, blockIdx.x, gridDim.x, &D.st->err, &D.st->abort_flag);
+  if (tr) tr[2] = gtimer();
 }
-__global__ void __launch_bounds__(CK_THREADS, 2) k_misc(const Phase* __restrict__ ph, CkDev D) {
+__global__ void __launch_bounds__(CK_THREADS, 1) k_attn(const Phase* __restrict__ ph, CkDev D) {
   __shared__ Smem sm;
-  run_phase(*ph, sm, D, blockIdx.x, gridDim.x);
+  phase_attn(ph->at, sm, D, blockIdx.x, gridDim.x, D.st->pos);
+}
+__global__ void __launch_bounds__(CK_THREADS, 1) k_misc(const Phase* __restrict__ ph, CkDev D) {
+  __shared__ Smem sm;
+  const Phase& p = *ph;
+  switch (p.kind) {
+    case PH_EMBED: phase_embed(p.em, D, blockIdx.x, gridDim.x, D.st->pos); break;
+    case PH_ARGMAX1: phase_argmax1(D, sm, blockIdx.x, gridDim.x); break;
+    case PH_ARGMAX2: phase_argmax2(D, sm, blockIdx.x); break;
+    case PH_SAMPLE: phase_sample(D, sm, blockIdx.x); break;
+    case PH_FINISH: phase_finish(p.need_logits, D, blockIdx.x); break;
+    case PH_SELECT: phase_select(p.need_logits, D, sm, blockIdx.x); break;
+  }
 }
 
 __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
@@ -851,16 +1198,14 @@ __device__ bool grid_sync(CkState* st, unsigned target) {
     int ok = 1;
     unsigned spins = 0;
     while (ld_acquire_u32(&st->bar) < target) {
-      if (*(volatile int*)&st->abort_flag) { ok = 0; break; }
-      if (++spins > (1u << 21)) {
+      if (++spins > (1u << 23)) {
         atomicOr(&st->err, CK_DERR_BARRIER);
         atomicExch(&st->abort_flag, 1);
         ok = 0;
         break;
       }
-      __nanosleep(64);
+      if ((spins & 255u) == 0 && *(volatile int*)&st->abort_flag) { ok = 0; break; }
     }
-    __threadfence();
     s_ok = ok;
   }
   __syncthreads();
@@ -868,11 +1213,20 @@ __device__ bool grid_sync(CkState* st, unsigned target) {
 }
 
 // Whole step in one cooperative launch (megakernel mode).
-__global__ void __launch_bounds__(CK_THREADS, 2) k_mega(const Phase* __restrict__ ph, int nph, CkDev D) {
+__global__ void __launch_bounds__(CK_THREADS, 1) k_mega(const Phase* __restrict__ ph, int nph, CkDev D) {
+  extern __shared__ __align__(128) uint8_t dyn[];
   __shared__ Smem sm;
+  const int pos = D.st->pos;   // constant for the whole step (phase_finish runs last)
+  Ring R;
+  const Phase* sph = launch_start(R, dyn, ph, nph, blockIdx.x, gridDim.x, &D.st->err, &D.st->abort_flag);
+  if (!sph) return;
   unsigned target = 0;
+  const bool tr = D.trace && blockIdx.x == 0 && threadIdx.x == 0;
   for (int i = 0; i < nph; i++) {
-    run_phase(ph[i], sm, D, blockIdx.x, gridDim.x);
+    if (tr && 2 * i + 1 < CK_TRACE_MV_BASE) D.trace[2 * i] = gtimer();
+    run_phase(sph, i, sm, R, D, blockIdx.x, gridDim.x, pos);
+    if (tr && 2 * i + 1 < CK_TRACE_MV_BASE) D.trace[2 * i + 1] = gtimer();
+    if (!R.ok) return;
     if (i + 1 < nph) {
       target += gridDim.x;
       if (!grid_sync(D.st, target)) return;

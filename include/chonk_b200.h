@@ -136,6 +136,12 @@ int ck_sync(ck_engine* h);
 /* Host<->device bytes copied so far by the step calls (run_token, prefill,
  * decode, reset, truncate): the e2e transfer count. */
 int ck_io_bytes(ck_engine* h, uint64_t* h2d_bytes, uint64_t* d2h_bytes);
+/* Device timeline: with tracing on, the megakernel stamps %globaltimer (ns)
+ * at the start and end of every phase on CTA 0 (slots [2i], [2i+1]) and the
+ * per-phase kernels stamp start / after-prefetch / end per CTA (slots
+ * 4096 + cta*8 + {0,1,2}).  ck_trace_read copies the first n slots. */
+int ck_trace(ck_engine* h, int enable);
+int ck_trace_read(ck_engine* h, uint64_t* out, size_t n);
 /* Bytes of weights + KV the next decode step reads (roofline numerator). */
 int ck_step_bytes(ck_engine* h, double* weight_bytes, double* kv_bytes);
 
