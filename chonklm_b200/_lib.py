@@ -104,6 +104,7 @@ def lib():
             L.ck_bench_matvec.argtypes = [I, P, S, I, I, I, pp(D), I]
             L.ck_abi_info.argtypes = [pp(I), pp(I)]
             L.ck_io_bytes.argtypes = [P, pp(ctypes.c_uint64), pp(ctypes.c_uint64)]
+            L.ck_matvec_noalloc.argtypes = [I, P, S, I, I, P, P, P]
             L.ck_trace.argtypes = [P, I]
             L.ck_trace_read.argtypes = [P, P, S]
             _lib = L
@@ -265,6 +266,14 @@ def matvec(ggml_type: int, data: bytes, k: int, n: int, x: np.ndarray, device: i
     y = np.empty(n, dtype=np.float32)
     _check(lib().ck_matvec(ggml_type, buf.ctypes.data, buf.nbytes, k, n, xx.ctypes.data, y.ctypes.data, device))
     return y
+
+
+def matvec_noalloc(ggml_type: int, w_dev: int, nbytes: int, k: int, n: int, x_dev: int, y_dev: int,
+                   stream: int = 0) -> None:
+    """ck_matvec_noalloc on caller-owned device buffers (raw integer device
+    addresses): for callers that cannot allocate device memory themselves."""
+    _check(lib().ck_matvec_noalloc(ggml_type, ctypes.c_void_p(w_dev), nbytes, k, n, ctypes.c_void_p(x_dev),
+                                   ctypes.c_void_p(y_dev), ctypes.c_void_p(stream)))
 
 
 def bench_matvec(ggml_type: int, data: bytes, k: int, n: int, reps: int = 200, device: int = 0) -> float:

@@ -1021,3 +1021,93 @@ int ck_bench_matvec(int ggml_type, const void* bytes, size_t nbytes, int k, int 
 }
 
 }  // extern "C"
+
+// ---- matvec without device allocation -------------------------------------
+// For callers that cannot allocate device memory of their own: hosts whose
+// device memory is owned by another caching allocator (a framework pool that
+// already holds the device's memory, so a raw cudaMalloc would fail or bypass
+// its accounting), and latency-bound serving loops where cudaMalloc/cudaFree
+// would synchronise the device and stall every other stream.  The caller
+// passes its own device buffers; this entry point's scratch -- the step state,
+// the phase descriptor and the device-layout copy of the weights -- lives in
+// the one static array below, which every GPU that loads this library holds
+// until the process exits.  Every call shares it and it keeps the last call's
+// contents, so calls that overlap on the GPU (other threads, other streams)
+// race; the state words that must start at zero are cleared on every call.
+#define CK_NOALLOC_STATE_BYTES 256
+#define CK_NOALLOC_PHASE_BYTES 4096
+#define CK_NOALLOC_WEIGHT_BYTES (16u << 20)   // largest device-layout weight: 16 MiB
+#define CK_NOALLOC_SCRATCH_BYTES (CK_NOALLOC_STATE_BYTES + CK_NOALLOC_PHASE_BYTES + CK_NOALLOC_WEIGHT_BYTES)
+static __device__ __align__(256) uint8_t g_noalloc_scratch[CK_NOALLOC_SCRATCH_BYTES];
+static_assert(sizeof(CkState) <= CK_NOALLOC_STATE_BYTES, "state slot");
+static_assert(sizeof(Phase) <= CK_NOALLOC_PHASE_BYTES, "phase slot");
+
+#define CK_NOALLOC_MAX_DEVICES 64
+static uint8_t* g_noalloc_dev[CK_NOALLOC_MAX_DEVICES];   // device address of the array, per device
+static int g_noalloc_sms[CK_NOALLOC_MAX_DEVICES];
+
+extern "C" int ck_matvec_noalloc(int ggml_type, const void* w_dev, size_t nbytes, int k, int n, const float* x_dev,
+                                 float* y_dev, void* stream) {
+  if (!w_dev || !x_dev || !y_dev || k <= 0 || n <= 0) return set_global(CK_EINVAL, "ck_matvec_noalloc: bad argument");
+  if (!ck_type_ok(ggml_type)) return set_global(CK_EINVAL, "ck_matvec_noalloc: unsupported GGML type %d", ggml_type);
+  if (k % ck_block_weights(ggml_type) || k > CK_KMAX)
+    return set_global(CK_EINVAL, "ck_matvec_noalloc: row length %d unsupported for type %d", k, ggml_type);
+  size_t raw = (size_t)n * (k / ck_block_weights(ggml_type)) * ck_block_bytes(ggml_type);
+  if (nbytes != raw) return set_global(CK_EINVAL, "ck_matvec_noalloc: %zu bytes, expected %zu", nbytes, raw);
+  Lay L = make_lay(ggml_type, k);
+  size_t need = (size_t)L.row_bytes * n;
+  if (need > CK_NOALLOC_WEIGHT_BYTES)
+    return set_global(CK_EINVAL, "ck_matvec_noalloc: %d x %d weights need %zu device bytes, the static scratch holds %u",
+                      n, k, need, CK_NOALLOC_WEIGHT_BYTES);
+  int dev = 0;
+  CKG(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= CK_NOALLOC_MAX_DEVICES) return set_global(CK_EINVAL, "ck_matvec_noalloc: device %d", dev);
+  if (!g_noalloc_dev[dev]) {
+    // one-time set-up on this device (the device is current): resolve the
+    // array's device address; the first call on a device should therefore
+    // come before any stream capture
+    void* p = nullptr;
+    CKG(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+    CKG(cudaFuncSetAttribute(k_mv, cudaFuncAttributeMaxDynamicSharedMemorySize, CK_DYN_SMEM_MAX));
+    int sms = 0;
+    CKG(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    g_noalloc_sms[dev] = sms;
+    g_noalloc_dev[dev] = (uint8_t*)p;
+  }
+  uint8_t* base = g_noalloc_dev[dev];
+  CkState* st = (CkState*)base;
+  Phase* dph = (Phase*)(base + CK_NOALLOC_STATE_BYTES);
+  uint8_t* wl = base + CK_NOALLOC_STATE_BYTES + CK_NOALLOC_PHASE_BYTES;
+  cudaStream_t s = (cudaStream_t)stream;
+
+  Phase ph;
+  memset(&ph, 0, sizeof ph);
+  ph.kind = PH_MATVEC;
+  ph.mv.pro.kind = PRO_COPY;
+  ph.mv.pro.a = x_dev;
+  ph.mv.k = k;
+  ph.mv.nseg = 1;
+  ph.mv.seg[0].w = wl;
+  ph.mv.seg[0].out = y_dev;
+  ph.mv.seg[0].add = nullptr;
+  ph.mv.seg[0].L = L;
+  ph.mv.seg[0].n = n;
+  int grid = n < g_noalloc_sms[dev] ? n : g_noalloc_sms[dev];
+  CkDev D;
+  memset(&D, 0, sizeof D);
+  D.st = st;
+
+  CKG(cudaMemsetAsync(st, 0, sizeof(CkState), s));          // error and abort words start at zero
+  CKG(cudaMemcpyAsync(dph, &ph, sizeof(Phase), cudaMemcpyHostToDevice, s));
+  long long total = (long long)n * L.nb;
+  k_relayout<<<(unsigned)((total + 255) / 256), 256, 0, s>>>((const uint8_t*)w_dev, wl, L, n);
+  CKG(cudaGetLastError());
+  k_mv<<<grid, CK_THREADS, CK_DYN_PHASES + sizeof(Phase), s>>>(dph, D);
+  CKG(cudaGetLastError());
+  int derr = 0;
+  CKG(cudaMemcpyAsync(&derr, &st->err, sizeof(int), cudaMemcpyDeviceToHost, s));
+  CKG(cudaStreamSynchronize(s));
+  if (derr) return set_global(CK_EDEVICE, "ck_matvec_noalloc: device error bits 0x%x", derr);
+  return CK_OK;
+}
+

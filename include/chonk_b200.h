@@ -157,6 +157,22 @@ int ck_matvec(int ggml_type, const void* bytes, size_t nbytes, int k, int n, con
 int ck_bench_matvec(int ggml_type, const void* bytes, size_t nbytes, int k, int n, int reps, double* us_per,
                     int device);
 
+/* y = W x like ck_matvec, for callers that cannot allocate device memory
+ * (their device memory is owned by another caching allocator, or a serving
+ * loop cannot afford the device synchronisation of cudaMalloc/cudaFree).  No
+ * counterpart in the reference: it has no native code.  w_dev holds the raw
+ * GGUF block bytes of n rows x k weights, x_dev fp32[k], y_dev fp32[n], all in
+ * caller-owned device memory; stream is a cudaStream_t (NULL = default
+ * stream) and the call returns after the result is ready.  Nothing is
+ * allocated: the device-layout copy of the weights goes to a static device
+ * array of 16 MiB (plus 4.25 KiB of state), held by every GPU that loads the
+ * library until exit; larger weights are rejected with CK_EINVAL.  The first
+ * call on a device resolves that array's address (one-time set-up) and should
+ * come before any stream capture.  All calls share the array: calls that
+ * overlap on the GPU race. */
+int ck_matvec_noalloc(int ggml_type, const void* w_dev, size_t nbytes, int k, int n, const float* x_dev,
+                      float* y_dev, void* stream);
+
 /* sizeof(ck_model_cfg) and sizeof(ck_sampling) as compiled, so bindings can
  * check their struct mirrors; needs no GPU. */
 void ck_abi_info(int* sizeof_cfg, int* sizeof_sampling);
