@@ -74,7 +74,8 @@ struct ck_engine {
 
   // schedules
   std::vector<Phase> ph_logits, ph_prefill;
-  Phase *d_logits = nullptr, *d_prefill = nullptr;
+  Phase *d_logits = nullptr, *d_prefill = nullptr;     // per-phase launches (mode 1)
+  Phase *dm_logits = nullptr, *dm_prefill = nullptr;   // same phases partitioned for the megakernel grid
   int mega_grid = 0;
   cudaGraphExec_t gx_logits[2] = {nullptr, nullptr}, gx_prefill[2] = {nullptr, nullptr};
 
@@ -222,6 +223,7 @@ Phase mk_mv(ck_engine* h, const Pro& pro, int k, std::initializer_list<MvSeg> se
   int rows = 0;
   for (int i = 0; i < p.mv.nseg; i++) rows = rows > p.mv.seg[i].n ? rows : p.mv.seg[i].n;
   p.grid = rows < h->sms ? (rows < 1 ? 1 : rows) : h->sms;
+  set_partition(p, p.grid);
   return p;
 }
 
@@ -265,6 +267,7 @@ void build_schedule(ck_engine* h, bool logits, std::vector<Phase>& out) {
     a.at.part = h->part;
     a.at.counter = h->counters;
     a.at.heads = c.heads; a.at.kvh = c.kv_heads; a.at.hd = hd; a.at.ctx = c.context_length;
+    a.at.group = c.heads / c.kv_heads;
     a.at.window = (int)c.layer_window[i];
     a.at.interleaved = c.rope_interleaved;
     a.at.kv_f32 = c.kv_dtype == CK_KV_F32;
@@ -313,10 +316,13 @@ void build_schedule(ck_engine* h, bool logits, std::vector<Phase>& out) {
   f.grid = 1;
   f.need_logits = logits ? 1 : 0;
   out.push_back(f);
+  for (size_t i = 0; i < out.size(); i++) out[i].index = (int)i;
 }
 
-int enqueue_phases(ck_engine* h, const std::vector<Phase>& ph, const Phase* dph, int mode, cudaStream_t s) {
+int enqueue_phases(ck_engine* h, bool logits, int mode, cudaStream_t s) {
+  const std::vector<Phase>& ph = logits ? h->ph_logits : h->ph_prefill;
   if (mode == 1) {
+    const Phase* dph = logits ? h->d_logits : h->d_prefill;
     for (size_t i = 0; i < ph.size(); i++) {
       if (ph[i].kind == PH_MATVEC) k_mv<<<ph[i].grid, CK_THREADS, CK_DYN_PHASES + sizeof(Phase), s>>>(dph + i, h->Dlaunch);
       else if (ph[i].kind == PH_ATTN) k_attn<<<ph[i].grid, CK_THREADS, 0, s>>>(dph + i, h->Dlaunch);
@@ -326,6 +332,7 @@ int enqueue_phases(ck_engine* h, const std::vector<Phase>& ph, const Phase* dph,
     return CK_OK;
   }
   CKC(h, cudaMemsetAsync(&h->st->bar, 0, sizeof(uint32_t), s));
+  const Phase* dph = logits ? h->dm_logits : h->dm_prefill;
   int nph = (int)ph.size();
   void* args[] = {(void*)&dph, (void*)&nph, (void*)&h->Dlaunch};
   size_t dyn = CK_DYN_PHASES + ph.size() * sizeof(Phase);
@@ -333,11 +340,11 @@ int enqueue_phases(ck_engine* h, const std::vector<Phase>& ph, const Phase* dph,
   return CK_OK;
 }
 
-int capture(ck_engine* h, const std::vector<Phase>& ph, const Phase* dph, int mode, cudaGraphExec_t* out) {
+int capture(ck_engine* h, bool logits, int mode, cudaGraphExec_t* out) {
   cudaStream_t s = h->own;
   cudaGraph_t g = nullptr;
   CKC(h, cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
-  int rc = enqueue_phases(h, ph, dph, mode, s);
+  int rc = enqueue_phases(h, logits, mode, s);
   cudaError_t e = cudaStreamEndCapture(s, &g);
   if (rc) { if (g) cudaGraphDestroy(g); return rc; }
   if (e != cudaSuccess) return h->fail(CK_ECUDA, "graph capture: %s", cudaGetErrorString(e));
@@ -353,8 +360,7 @@ int launch_step(ck_engine* h, bool logits) {
     CKC(h, cudaGraphLaunch(gx, h->stream));
     return CK_OK;
   }
-  return enqueue_phases(h, logits ? h->ph_logits : h->ph_prefill, logits ? h->d_logits : h->d_prefill, h->mode,
-                        h->stream);
+  return enqueue_phases(h, logits, h->mode, h->stream);
 }
 
 // Host option block -> device (sampling.ts SamplingOptions + penalty plumbing
@@ -606,12 +612,19 @@ int ck_finalize(ck_engine* h) {
   if (want < 1) want = 1;
   if (per_sm < 1) return h->fail(CK_ECUDA, "megakernel does not fit on an SM");
   h->mega_grid = h->sms * (want < per_sm ? want : per_sm);
+  for (int l = 0; l < 2; l++) {
+    std::vector<Phase> mp = l ? h->ph_logits : h->ph_prefill;
+    for (Phase& p : mp) set_partition(p, h->mega_grid);
+    Phase** dst = l ? &h->dm_logits : &h->dm_prefill;
+    if ((rc = dalloc(h, dst, mp.size() * sizeof(Phase)))) return rc;
+    CKC(h, cudaMemcpy(*dst, mp.data(), mp.size() * sizeof(Phase), cudaMemcpyHostToDevice));
+  }
   for (int m = 0; m < 2; m++) {
-    if ((rc = capture(h, h->ph_logits, h->d_logits, m, &h->gx_logits[m]))) {
+    if ((rc = capture(h, true, m, &h->gx_logits[m]))) {
       cudaGetLastError();
       h->gx_logits[m] = nullptr;  // fall back to direct launches
     }
-    if ((rc = capture(h, h->ph_prefill, h->d_prefill, m, &h->gx_prefill[m]))) {
+    if ((rc = capture(h, false, m, &h->gx_prefill[m]))) {
       cudaGetLastError();
       h->gx_prefill[m] = nullptr;
     }
@@ -832,8 +845,8 @@ int ck_trace(ck_engine* h, int enable) {
   for (int m = 0; m < 2; m++) {
     if (h->gx_logits[m]) { cudaGraphExecDestroy(h->gx_logits[m]); h->gx_logits[m] = nullptr; }
     if (h->gx_prefill[m]) { cudaGraphExecDestroy(h->gx_prefill[m]); h->gx_prefill[m] = nullptr; }
-    if (capture(h, h->ph_logits, h->d_logits, m, &h->gx_logits[m])) { cudaGetLastError(); h->gx_logits[m] = nullptr; }
-    if (capture(h, h->ph_prefill, h->d_prefill, m, &h->gx_prefill[m])) { cudaGetLastError(); h->gx_prefill[m] = nullptr; }
+    if (capture(h, true, m, &h->gx_logits[m])) { cudaGetLastError(); h->gx_logits[m] = nullptr; }
+    if (capture(h, false, m, &h->gx_prefill[m])) { cudaGetLastError(); h->gx_prefill[m] = nullptr; }
   }
   h->err.clear();
   return CK_OK;
@@ -1093,6 +1106,7 @@ extern "C" int ck_matvec_noalloc(int ggml_type, const void* w_dev, size_t nbytes
   ph.mv.seg[0].L = L;
   ph.mv.seg[0].n = n;
   int grid = n < g_noalloc_sms[dev] ? n : g_noalloc_sms[dev];
+  set_partition(ph, grid);
   CkDev D;
   memset(&D, 0, sizeof D);
   D.st = st;

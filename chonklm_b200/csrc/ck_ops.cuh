@@ -22,6 +22,7 @@
 #define CK_HDMAX 256          // head_dim handled
 #define CK_SAMPLE_MAX 1024    // ARGMAX_STAGE1 candidates handled by the sampler
 #define CK_MIN_SPLIT 32       // positions per attention split (lower bound)
+#define CK_TILE_BYTES (64 * 1024)   // one buffer of the weight ring
 
 // device error bits (CkState::err)
 #define CK_DERR_TOKEN 1
@@ -69,13 +70,18 @@ __device__ __forceinline__ unsigned long long gtimer() {
   return t;
 }
 // Trace layout: k_mega: [phase][2] (CTA 0: phase start / phase end);
-// k_mv: [CK_TRACE_MV_BASE + cta * 8 + stage].
+// k_mv: [CK_TRACE_MV_BASE + cta * 8 + stage];
+// sub-stage stamps of phase i on CTA 0: [CK_TRACE_STAGE_BASE + i * 8 + stage];
+// k_mega per CTA: [CK_TRACE_CTA_BASE + cta * 16 + j], j 0..3 end of phases
+// 1..4, j 4..7 exit of their barriers, j 8..15 sub-stages of phase 2.
 #define CK_TRACE_MV_BASE 4096
 #define CK_TRACE_STAGE_BASE (CK_TRACE_MV_BASE + 8 * 1024)
-#define CK_TRACE_SLOTS (CK_TRACE_STAGE_BASE + 8 * 512)
-// sub-stage stamps of phase i on CTA 0: [CK_TRACE_STAGE_BASE + i * 8 + stage]
+#define CK_TRACE_CTA_BASE (CK_TRACE_STAGE_BASE + 8 * 512)
+#define CK_TRACE_SLOTS (CK_TRACE_CTA_BASE + 16 * 1024)
+// Sub-stage stamps are SM cycles (clock64): finer than the global timer, and
+// only ever differenced within one CTA.
 __device__ __forceinline__ void stage_mark(unsigned long long* tp, int stage) {
-  if (tp && threadIdx.x == 0) tp[stage] = gtimer();
+  if (tp && threadIdx.x == 0) tp[stage] = (unsigned long long)clock64();
 }
 
 enum { PRO_COPY = 0, PRO_NORM = 1, PRO_SILU = 2, PRO_GELU = 3, PRO_GEMMA = 4 };
@@ -99,12 +105,17 @@ struct MvSeg {
   const float* add;         // y = add + W x when non-null (residual epilogue)
   Lay L;
   int n;
+  int per;                  // rows per CTA of the launch this descriptor is for
+  int tile_rows;            // rows that fill an empty tile (CK_TILE_BYTES / row_bytes)
+  uint32_t soff;            // byte offset of this segment's rows in a packed tile
 };
 
 struct MvPhase {
   Pro pro;
   int k;
   int nseg;
+  int packed;               // every CTA's rows of all segments fit one tile
+  int pad_;
   MvSeg seg[3];
 };
 
@@ -117,6 +128,7 @@ struct AttnPhase {
   float* part;              // split partials [kvh][smax][G][hd + 2]
   unsigned* counter;        // [kvh] finished splits (last CTA merges, resets)
   int heads, kvh, hd, ctx, window, interleaved, kv_f32, smax;
+  int group;                // q heads per kv head (heads / kvh)
   uint32_t theta;
   float eps, scale;
 };
@@ -132,6 +144,7 @@ struct EmbedPhase {
 struct __align__(16) Phase {
   int kind;
   int grid;                 // CTAs for a standalone launch
+  int index;                // position in its schedule (trace slots)
   union {
     MvPhase mv;
     AttnPhase at;
@@ -141,14 +154,34 @@ struct __align__(16) Phase {
 };
 static_assert(sizeof(Phase) % 16 == 0, "phase descriptors are bulk-copied");
 
+// Host: the row partition of every matvec segment of `p` for a launch of
+// `grid` CTAs (CTA c owns rows [c*per, min(n, (c+1)*per))) and the rows that
+// fill an empty tile.  Every row fits a tile (rows are <= 3072 weights).
+// A phase is packed when a CTA's full share of every segment fits one tile:
+// then segment s sits at a fixed offset (the shares before it); otherwise
+// each segment is cut into tiles of its own.
+inline void set_partition(Phase& p, int grid) {
+  if (p.kind != PH_MATVEC) return;
+  uint32_t off = 0;
+  for (int i = 0; i < p.mv.nseg; i++) {
+    MvSeg& s = p.mv.seg[i];
+    s.per = (s.n + grid - 1) / grid;
+    s.tile_rows = (int)(CK_TILE_BYTES / s.L.row_bytes);
+    s.soff = off;
+    off += (uint32_t)s.per * s.L.row_bytes;
+  }
+  p.mv.packed = off <= CK_TILE_BYTES ? 1 : 0;
+  if (!p.mv.packed)
+    for (int i = 0; i < p.mv.nseg; i++) p.mv.seg[i].soff = 0;
+}
+
 // ---------------------------------------------------------------------------
 struct SmemMv {
   float xf[CK_KMAX];
-  float wf[CK_KMAX];
-  int8_t xh[CK_KMAX];
+  alignas(16) int8_t xh[CK_KMAX];
   int8_t xl[CK_KMAX];
   float sx[CK_KMAX / 32];
-  int s16[CK_KMAX / 16];
+  alignas(8) int s16[CK_KMAX / 16];
   float red[CK_WARPS * 2];
 };
 struct SmemAt {
@@ -156,6 +189,7 @@ struct SmemAt {
   float raw[CK_GMAX * CK_HDMAX];   // q rows as produced by the projection
   float kvw[4][CK_HDMAX];          // k, v, q-norm weight, k-norm weight
   float wacc[CK_WARPS * CK_HDMAX];
+  float kst[CK_HDMAX];             // the new k row after norm + rope
   float wm[CK_WARPS];
   float wl[CK_WARPS];
   float2 cs[CK_HDMAX / 2];
@@ -220,66 +254,75 @@ __device__ __forceinline__ float gelu_tanh(float x) {
 //   GEMMA rmsNorm(post) -> ADD_CLAMP (:3510-3527) -> rmsNorm(pre), the gemma3
 //         sandwich of runToken (:1050-1064); CTA 0 stores the new residual.
 __device__ void build_x(const Pro& p, int k, SmemMv& s, int cta) {
+  // Every global load of the prologue is issued in one round into registers
+  // before anything is stored: interleaving them with the shared-memory
+  // stores lets the compiler serialise each load behind the previous store.
+  constexpr int PER = CK_KMAX / CK_THREADS;
   const int tid = threadIdx.x;
+  const int kind = p.kind;
   float* xf = s.xf;
-  float* wf = s.wf;
-  if (p.kind == PRO_COPY) {
-    for (int i = tid; i < k; i += CK_THREADS) xf[i] = p.a[i];
-  } else if (p.kind == PRO_NORM) {
-    // activation and weight loads issued together; one reduction
-    float ss = 0.f;
-    for (int i = tid; i < k; i += CK_THREADS) {
-      float v = p.a[i], w = p.w0[i];
-      xf[i] = v;
-      wf[i] = w;
-      ss += v * v;
-    }
-    float inv = rms_inv(block_sum(ss, s.red), k, p.eps);
-    for (int i = tid; i < k; i += CK_THREADS) xf[i] = (xf[i] * inv) * wf[i];
-  } else if (p.kind == PRO_SILU) {
-    for (int i = tid; i < k; i += CK_THREADS) {
-      float g = p.a[i], u = p.b[i];
-      xf[i] = (g / (1.0f + expf(-g))) * u;
-    }
-  } else if (p.kind == PRO_GELU) {
-    for (int i = tid; i < k; i += CK_THREADS) {
-      float g = p.a[i], u = p.b[i];
-      xf[i] = gelu_tanh(g) * u;
-    }
-  } else {  // PRO_GEMMA: t = rmsnorm(a) * w1; h = clamp(rin + t); x = rmsnorm(h) * w0
-    constexpr int PER = CK_KMAX / CK_THREADS;
-    float rr[PER], ww[PER];
-    float ss = 0.f;
+  float va[PER], vb[PER], vc[PER], vd[PER];
+  const float* pb = (kind == PRO_SILU || kind == PRO_GELU) ? p.b : p.w0;
+#pragma unroll
+  for (int j = 0; j < PER; j++) {
+    const int i = tid + j * CK_THREADS;
+    const bool ok = i < k;
+    va[j] = ok ? p.a[i] : 0.f;
+    vb[j] = (ok && kind != PRO_COPY) ? pb[i] : 0.f;
+    vc[j] = (ok && kind == PRO_GEMMA) ? p.w1[i] : 0.f;
+    vd[j] = (ok && kind == PRO_GEMMA) ? p.rin[i] : 0.f;
+  }
+  if (kind == PRO_COPY) {
 #pragma unroll
     for (int j = 0; j < PER; j++) {
-      int i = tid + j * CK_THREADS;
-      if (i < k) {
-        float v = p.a[i];
-        xf[i] = v;
-        wf[i] = p.w1[i];
-        rr[j] = p.rin[i];
-        ww[j] = p.w0[i];
-        ss += v * v;
-      }
+      const int i = tid + j * CK_THREADS;
+      if (i < k) xf[i] = va[j];
     }
-    float inv = rms_inv(block_sum(ss, s.red), k, p.eps);
+  } else if (kind == PRO_NORM) {
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < PER; j++) ss += va[j] * va[j];
+    const float inv = rms_inv(block_sum(ss, s.red), k, p.eps);
+#pragma unroll
+    for (int j = 0; j < PER; j++) {
+      const int i = tid + j * CK_THREADS;
+      if (i < k) xf[i] = (va[j] * inv) * vb[j];
+    }
+  } else if (kind == PRO_SILU) {
+#pragma unroll
+    for (int j = 0; j < PER; j++) {
+      const int i = tid + j * CK_THREADS;
+      const float g = va[j];
+      if (i < k) xf[i] = (g / (1.0f + expf(-g))) * vb[j];
+    }
+  } else if (kind == PRO_GELU) {
+#pragma unroll
+    for (int j = 0; j < PER; j++) {
+      const int i = tid + j * CK_THREADS;
+      if (i < k) xf[i] = gelu_tanh(va[j]) * vb[j];
+    }
+  } else {  // PRO_GEMMA: t = rmsnorm(a) * w1; h = clamp(rin + t); x = rmsnorm(h) * w0
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < PER; j++) ss += va[j] * va[j];
+    const float inv = rms_inv(block_sum(ss, s.red), k, p.eps);
     float ss2 = 0.f;
 #pragma unroll
     for (int j = 0; j < PER; j++) {
-      int i = tid + j * CK_THREADS;
+      const int i = tid + j * CK_THREADS;
+      const float t = (va[j] * inv) * vc[j];
+      const float h = fminf(fmaxf(vd[j] + t, -65000.0f), 65000.0f);
+      va[j] = h;
       if (i < k) {
-        float t = (xf[i] * inv) * wf[i];
-        float h = fminf(fmaxf(rr[j] + t, -65000.0f), 65000.0f);
-        xf[i] = h;
         if (cta == 0) p.rout[i] = h;
         ss2 += h * h;
       }
     }
-    float inv2 = rms_inv(block_sum(ss2, s.red), k, p.eps);
+    const float inv2 = rms_inv(block_sum(ss2, s.red), k, p.eps);
 #pragma unroll
     for (int j = 0; j < PER; j++) {
-      int i = tid + j * CK_THREADS;
-      if (i < k) xf[i] = (xf[i] * inv2) * ww[j];
+      const int i = tid + j * CK_THREADS;
+      if (i < k) xf[i] = (va[j] * inv2) * vb[j];
     }
   }
   __syncthreads();
@@ -320,17 +363,20 @@ __device__ void quant_x(int k, SmemMv& s) {
   __syncthreads();
 }
 
+// The x unit of column c: two 16-byte shared loads per plane (a scalar load
+// per word would be an 8-way bank conflict at the 32-byte unit stride).
 __device__ __forceinline__ void load_xunit(const SmemMv& s, int c, XUnit& x) {
-  const int* h = (const int*)s.xh;
-  const int* l = (const int*)s.xl;
-#pragma unroll
-  for (int i = 0; i < 8; i++) {
-    x.h[i] = h[8 * c + i];
-    x.l[i] = l[8 * c + i];
-  }
+  const int4* h = (const int4*)s.xh + 2 * c;
+  const int4* l = (const int4*)s.xl + 2 * c;
+  const int4 h0 = h[0], h1 = h[1], l0 = l[0], l1 = l[1];
+  x.h[0] = h0.x; x.h[1] = h0.y; x.h[2] = h0.z; x.h[3] = h0.w;
+  x.h[4] = h1.x; x.h[5] = h1.y; x.h[6] = h1.z; x.h[7] = h1.w;
+  x.l[0] = l0.x; x.l[1] = l0.y; x.l[2] = l0.z; x.l[3] = l0.w;
+  x.l[4] = l1.x; x.l[5] = l1.y; x.l[6] = l1.z; x.l[7] = l1.w;
   x.sx = s.sx[c];
-  x.sa = s.s16[2 * c];
-  x.sb = s.s16[2 * c + 1];
+  const int2 ss = *(const int2*)(s.s16 + 2 * c);
+  x.sa = ss.x;
+  x.sb = ss.y;
 }
 
 // ---------------------------------------------------------------------------
@@ -341,72 +387,106 @@ __device__ __forceinline__ void load_xunit(const SmemMv& s, int c, XUnit& x) {
 // multicast) completing on an mbarrier; the ring runs ahead across phases, so
 // the next matvec's weights are in flight while this CTA is in a grid barrier
 // or an attention phase.  Consumers read the tile from shared memory.
-#define CK_TILE_BYTES (64 * 1024)
-#define CK_TILE_PIECES 4
 #define CK_ISSUER (CK_THREADS - 32)   // lane 0 of the last warp copies tiles
+// Dynamic shared memory: [tile buffer 0][tile buffer 1][3 mbarriers, 128 B][phase descriptors]
+#define CK_DYN_BARS (2 * CK_TILE_BYTES)
+#define CK_DYN_PHASES (2 * CK_TILE_BYTES + 128)
+#define CK_PHASE_SMEM_MAX (48 * 1024)
+#define CK_DYN_SMEM_MAX (CK_DYN_PHASES + CK_PHASE_SMEM_MAX)
 
-struct Piece {
-  int seg, r0, r1;
-  uint32_t soff;
-};
-struct Tile {
-  int phase, npc;
-  uint32_t bytes;
-  Piece pc[CK_TILE_PIECES];
-};
 struct Cursor {
   int phase, seg, row;
 };
 
+// Ring state.  The buffers, barriers and staged descriptors sit at fixed
+// offsets of the dynamic shared memory (no registers); the issuer's cursor
+// lives in shared memory (one thread uses it); every thread keeps the count
+// of consumed tiles, which is CTA-uniform.
 struct Ring {
-  uint8_t* buf;            // 2 x CK_TILE_BYTES, 128-byte aligned
-  uint64_t* full;          // 2 mbarriers
-  const Phase* ph;
-  int nph;
-  Cursor issue;            // issuer thread: next tile to copy
-  unsigned issued;         // issuer thread: tiles copied so far
-  unsigned consumed;       // every thread: tiles consumed so far
+  unsigned consumed;       // tiles consumed so far
   int ok;                  // 0 once a wait gave up
 };
-
-// Contiguous row range of a CTA (n * ncta < 2^31 for every model handled).
-__device__ __forceinline__ void seg_range(const MvSeg& S, int cta, int ncta, int& lo, int& hi) {
-  lo = (S.n * cta) / ncta;
-  hi = (S.n * (cta + 1)) / ncta;
+struct IssueState {
+  Cursor issue;            // next row to copy
+  unsigned issued;         // tiles copied so far
+  int nph;                 // phases staged for this launch
+};
+__device__ __forceinline__ uint8_t* dyn_smem() {
+  extern __shared__ __align__(128) uint8_t ck_dyn[];
+  return ck_dyn;
+}
+__device__ __forceinline__ uint8_t* ring_buf(unsigned tile) {
+  return dyn_smem() + (size_t)(tile & 1) * CK_TILE_BYTES;
+}
+__device__ __forceinline__ IssueState& issue_state() {
+  __shared__ IssueState st;
+  return st;
 }
 
-// Next tile from cursor `c` (phases [c.phase, last)), false when none.
-// `last` bounds the search: nph for the issuer, phase + 1 for consumers.
-__device__ bool next_tile(const Phase* ph, int last, int cta, int ncta, Cursor& c, Tile& t) {
-  while (c.phase < last) {
-    const Phase& p = ph[c.phase];
-    if (p.kind != PH_MATVEC) {
-      c.phase++; c.seg = 0; c.row = -1;
-      continue;
+// A CTA's tiles of a phase, followed identically by the issuer and the
+// consumers: a packed phase is one tile holding the CTA's rows of every
+// segment at the segment's fixed offset; otherwise segment by segment in
+// tiles of tile_rows rows.  The row partition (CTA c owns rows
+// [c*per, min(n, (c+1)*per))) and the tile shapes are precomputed on the host
+// for the launch's grid, so the walk has no division and no dependent chain.
+__device__ __forceinline__ void seg_range(const MvSeg& S, int cta, int& lo, int& hi) {
+  lo = min(S.n, cta * S.per);
+  hi = min(S.n, lo + S.per);
+}
+
+// The row ranges ("pieces") of one tile, at most one per segment, kept as
+// scalars so they stay in registers.  Flat row t of the tile belongs to
+// piece (t >= st1) + (t >= st2).
+struct TileList {
+  int n, total;            // pieces, rows
+  int st1, st2;            // first flat row of pieces 1 and 2
+  int seg0, seg1, seg2;    // segment of each piece
+  int r00, r01, r02;       // first output row of each piece
+  uint32_t off0, off1, off2;   // byte offset of each piece in the tile
+};
+__device__ __forceinline__ int pick3(int p, int a, int b, int c) { return p == 0 ? a : (p == 1 ? b : c); }
+__device__ __forceinline__ uint32_t pick3u(int p, uint32_t a, uint32_t b, uint32_t c) {
+  return p == 0 ? a : (p == 1 ? b : c);
+}
+__device__ __forceinline__ void tile_clear(TileList& T) {
+  T.n = 0; T.total = 0; T.st1 = T.st2 = 1 << 30;
+  T.seg0 = T.seg1 = T.seg2 = 0; T.r00 = T.r01 = T.r02 = 0; T.off0 = T.off1 = T.off2 = 0u;
+}
+__device__ __forceinline__ void tile_add(TileList& T, int seg, int r0, int rows, uint32_t off) {
+  if (T.n == 0) { T.seg0 = seg; T.r00 = r0; T.off0 = off; }
+  else if (T.n == 1) { T.seg1 = seg; T.r01 = r0; T.off1 = off; T.st1 = T.total; }
+  else { T.seg2 = seg; T.r02 = r0; T.off2 = off; T.st2 = T.total; }
+  T.n++;
+  T.total += rows;
+}
+
+// Next tile of phase m for this CTA from position (seg, row) (seg = 0,
+// row = -1 at the start of the phase); false when the phase has no more.
+__device__ __forceinline__ bool next_tile(const MvPhase& m, int cta, int& seg, int& row, TileList& T) {
+  tile_clear(T);
+  if (m.packed) {
+    if (seg != 0) return false;
+    seg = 1;
+#pragma unroll
+    for (int i = 0; i < 3; i++) {
+      if (i < m.nseg) {
+        int lo, hi;
+        seg_range(m.seg[i], cta, lo, hi);
+        if (hi > lo) tile_add(T, i, lo, hi - lo, m.seg[i].soff);
+      }
     }
-    const MvPhase& m = p.mv;
-    t.phase = c.phase;
-    t.npc = 0;
-    t.bytes = 0;
-    while (c.seg < m.nseg && t.npc < CK_TILE_PIECES) {
-      int lo, hi;
-      seg_range(m.seg[c.seg], cta, ncta, lo, hi);
-      if (c.row < lo) c.row = lo;
-      if (c.row >= hi) { c.seg++; c.row = -1; continue; }
-      uint32_t rb = m.seg[c.seg].L.row_bytes;
-      int fit = (int)((CK_TILE_BYTES - t.bytes) / rb);
-      if (fit <= 0) break;
-      int take = min(fit, hi - c.row);
-      t.pc[t.npc].seg = c.seg;
-      t.pc[t.npc].r0 = c.row;
-      t.pc[t.npc].r1 = c.row + take;
-      t.pc[t.npc].soff = t.bytes;
-      t.npc++;
-      t.bytes += (uint32_t)take * rb;
-      c.row += take;
-    }
-    if (t.npc > 0) return true;
-    c.phase++; c.seg = 0; c.row = -1;
+    return T.total > 0;
+  }
+  while (seg < m.nseg) {
+    const MvSeg& S = m.seg[seg];
+    int lo, hi;
+    seg_range(S, cta, lo, hi);
+    if (row < lo) row = lo;
+    if (row >= hi) { seg++; row = -1; continue; }
+    const int take = min(S.tile_rows, hi - row);
+    tile_add(T, seg, row, take, 0u);
+    row += take;
+    return true;
   }
   return false;
 }
@@ -419,6 +499,13 @@ __device__ __forceinline__ void mbar_init(uint64_t* b, unsigned count) {
 __device__ __forceinline__ void mbar_fence_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
 __device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes) : "memory");
+}
+// expect_tx without an arrival: one per copy of a tile, then one arrive
+__device__ __forceinline__ void mbar_expect_tx_only(uint64_t* b, uint32_t bytes) {
+  asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
 }
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* b, uint32_t parity) {
   uint32_t done;
@@ -447,36 +534,46 @@ __device__ __forceinline__ void bulk_g2s_stream(void* dst, const void* src, uint
       : "memory");
 }
 
-// issuer thread: copy the next tile (if any) into buffer issued & 1
-__device__ void ring_issue(Ring& R, int cta, int ncta) {
-  Tile t;
-  if (!next_tile(R.ph, R.nph, cta, ncta, R.issue, t)) return;
-  int b = R.issued & 1;
-  uint64_t* bar = R.full + b;
-  mbar_expect_tx(bar, t.bytes);
-  const MvPhase& m = R.ph[t.phase].mv;
-  for (int i = 0; i < t.npc; i++) {
-    const MvSeg& S = m.seg[t.pc[i].seg];
-    uint32_t rb = S.L.row_bytes;
-    bulk_g2s_stream(R.buf + (size_t)b * CK_TILE_BYTES + t.pc[i].soff, S.w + (size_t)t.pc[i].r0 * rb,
-                    (uint32_t)(t.pc[i].r1 - t.pc[i].r0) * rb, bar);
+// Issuer thread: copy the next tile (if any) into buffer issued & 1, one bulk
+// copy per piece, each preceded by its expect_tx; the single arrival after
+// the last copy lets the barrier's phase complete.
+__device__ __forceinline__ void ring_issue(int cta) {
+  IssueState& is = issue_state();
+  Cursor& c = is.issue;
+  const Phase* ph = (const Phase*)(dyn_smem() + CK_DYN_PHASES);
+  TileList T;
+  while (c.phase < is.nph) {
+    const Phase& p = ph[c.phase];
+    if (p.kind == PH_MATVEC && next_tile(p.mv, cta, c.seg, c.row, T)) {
+      const int b = is.issued & 1;
+      uint64_t* bar = (uint64_t*)(dyn_smem() + CK_DYN_BARS) + b;
+      uint8_t* dst = ring_buf(b);
+      for (int i = 0; i < T.n; i++) {
+        const int sg = pick3(i, T.seg0, T.seg1, T.seg2);
+        const int r0 = pick3(i, T.r00, T.r01, T.r02);
+        const int rows = (i + 1 < T.n ? pick3(i + 1, 0, T.st1, T.st2) : T.total) - pick3(i, 0, T.st1, T.st2);
+        const MvSeg& S = p.mv.seg[sg];
+        const uint32_t rb = S.L.row_bytes, bytes = (uint32_t)rows * rb;
+        mbar_expect_tx_only(bar, bytes);
+        bulk_g2s_stream(dst + pick3u(i, T.off0, T.off1, T.off2), S.w + (size_t)r0 * rb, bytes, bar);
+      }
+      mbar_arrive(bar);
+      is.issued++;
+      return;
+    }
+    c.phase++; c.seg = 0; c.row = -1;
   }
-  R.issued++;
 }
 
 // Shared-memory layout of the streaming kernels (dynamic part):
 //   [tile buffer 0][tile buffer 1][3 mbarriers, 128 B][phase descriptors]
-#define CK_DYN_BARS (2 * CK_TILE_BYTES)
-#define CK_DYN_PHASES (2 * CK_TILE_BYTES + 128)
-#define CK_PHASE_SMEM_MAX (48 * 1024)
-#define CK_DYN_SMEM_MAX (CK_DYN_PHASES + CK_PHASE_SMEM_MAX)
 
 // Start of a launch: init the barriers, stage the phase descriptors in shared
 // memory with one bulk copy (every later descriptor read is a shared-memory
 // read), then put the first two weight tiles in flight.  Returns the staged
 // descriptors, or null when the wait gave up.
-__device__ const Phase* launch_start(Ring& R, uint8_t* dyn, const Phase* gph, int nph, int cta, int ncta,
-                                     int* err, int* abort_flag) {
+__device__ __forceinline__ const Phase* launch_start(Ring& R, const Phase* gph, int nph, int cta, int* err, int* abort_flag) {
+  uint8_t* dyn = dyn_smem();
   uint64_t* bars = (uint64_t*)(dyn + CK_DYN_BARS);
   Phase* sph = (Phase*)(dyn + CK_DYN_PHASES);
   if (threadIdx.x == 0) {
@@ -488,6 +585,12 @@ __device__ const Phase* launch_start(Ring& R, uint8_t* dyn, const Phase* gph, in
     mbar_expect_tx(bars + 2, bytes);
     bulk_g2s(sph, gph, bytes, bars + 2);
   }
+  if (threadIdx.x == CK_ISSUER) {
+    IssueState& is = issue_state();
+    is.issue.phase = 0; is.issue.seg = 0; is.issue.row = -1;
+    is.issued = 0;
+    is.nph = nph;
+  }
   __syncthreads();
   unsigned spins = 0;
   while (!mbar_try_wait(bars + 2, 0)) {
@@ -497,24 +600,18 @@ __device__ const Phase* launch_start(Ring& R, uint8_t* dyn, const Phase* gph, in
       return nullptr;
     }
   }
-  R.buf = dyn;
-  R.full = bars;
-  R.ph = sph;
-  R.nph = nph;
-  R.issue.phase = 0; R.issue.seg = 0; R.issue.row = -1;
-  R.issued = 0;
   R.consumed = 0;
   R.ok = 1;
   if (threadIdx.x == CK_ISSUER) {
-    ring_issue(R, cta, ncta);
-    ring_issue(R, cta, ncta);
+    ring_issue(cta);
+    ring_issue(cta);
   }
   return sph;
 }
 
 // Wait for tile `consumed` (bounded: ~seconds, then flags and gives up).
-__device__ bool ring_wait(Ring& R, int* err, int* abort_flag) {
-  uint64_t* bar = R.full + (R.consumed & 1);
+__device__ __forceinline__ bool ring_wait(const Ring& R, int* err, int* abort_flag) {
+  uint64_t* bar = (uint64_t*)(dyn_smem() + CK_DYN_BARS) + (R.consumed & 1);
   uint32_t par = (R.consumed >> 1) & 1u;
   unsigned spins = 0;
   while (!mbar_try_wait(bar, par)) {
@@ -530,108 +627,261 @@ __device__ bool ring_wait(Ring& R, int* err, int* abort_flag) {
 
 // After every thread finished reading tile `consumed`: free its buffer and
 // refill it with the tile two ahead.
-__device__ __forceinline__ void ring_release(Ring& R, int cta, int ncta) {
+__device__ __forceinline__ void ring_release(Ring& R, int cta) {
   __syncthreads();
   R.consumed++;
-  if (threadIdx.x == CK_ISSUER && R.issued < R.consumed + 2) ring_issue(R, cta, ncta);
+  if (threadIdx.x == CK_ISSUER && issue_state().issued < R.consumed + 2) ring_issue(cta);
 }
 
-// Rows of one tile piece, read from shared memory.  With one unit per lane
-// (ONE) the lane's x unit stays in registers for the whole piece and a warp
-// step handles two rows so their unpacks, dots and reductions overlap; with
-// 2-3 units per lane the x units are re-read from shared memory per unit (the
-// units of a row already overlap) to stay inside the register budget.  The
-// block type is a runtime switch inside the unpack: compiling the row loop
-// per type multiplies register pressure past the 128-register budget.
+// Rows of a tile, read from shared memory, as one flat list over the tile's
+// pieces so every warp has rows even when each piece is short (a QKV tile
+// holds a few rows of each projection).  A warp step covers rows t and
+// t + CK_WARPS (ONE) or row t: first every unit of those rows is unpacked
+// into registers (step_unpack: needs only the weights), then dotted with x
+// (step_dot).  The first step of a phase is unpacked before x exists, under
+// the latency of the prologue's loads.  With one unit per lane (ONE, k <= 1024)
+// the lane's x unit stays in registers (every segment of a phase has the
+// same k); with 2-3 units per lane the x units are read from shared memory
+// per unit.  The block type is a runtime switch inside the unpack: compiling
+// the row loop per type multiplies register pressure past the budget.
 template <bool ONE>
-__device__ __forceinline__ void mv_piece(const MvSeg& S, const uint8_t* base, int r0, int nrows, const SmemMv& s) {
-  constexpr int R = ONE ? 2 : 1;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int U = S.L.U;
-  const int T = S.L.type;
-  const int upl = ONE ? 1 : (U + 31) >> 5;
-  const uint32_t rb = S.L.row_bytes;
-  float* __restrict__ out = S.out;
-  const float* __restrict__ add = S.add;
-  if (warp >= nrows) return;
-  XUnit x0;
-  if (ONE && lane < U) load_xunit(s, lane, x0);
-  for (int r = warp; r < nrows; r += R * CK_WARPS) {
-    float acc[R];
+struct MvStep {
+  static constexpr int R = ONE ? 2 : 1;        // rows per warp step
+  static constexpr int UPL = 1;                // units per lane (ONE steps only)
+  U8 u[R][UPL];
+  int sg[R], orow[R];
+};
+
+template <bool ONE>
+__device__ __forceinline__ void step_unpack(const MvPhase& P, const uint8_t* tb, const TileList& T, int t,
+                                            MvStep<ONE>& w) {
+  const int lane = threadIdx.x & 31;
+  const int U = P.seg[0].L.U;
 #pragma unroll
-    for (int i = 0; i < R; i++) {
-      acc[i] = 0.f;
-      const int rr = r + i * CK_WARPS;
-      if (rr < nrows) {
-        const uint8_t* row = base + (size_t)rr * rb;
-        if (ONE) {
-          if (lane < U) {
-            U8 u;
-            unpack_unit<false>(T, row, S.L, lane, u);
-            acc[i] += unit_dot8(u, x0);
-          }
-        } else {
-#pragma unroll 1
-          for (int j = 0; j < upl; j++) {
-            int c = lane + 32 * j;
-            if (c < U) {
-              U8 u;
-              unpack_unit<false>(T, row, S.L, c, u);
-              XUnit xj;
-              load_xunit(s, c, xj);
-              acc[i] += unit_dot8(u, xj);
-            }
+  for (int i = 0; i < MvStep<ONE>::R; i++) {
+    const int tt = t + i * CK_WARPS;
+    const int pc = (tt >= T.st1) + (tt >= T.st2);
+    w.sg[i] = pick3(pc, T.seg0, T.seg1, T.seg2);
+    const int local = tt - pick3(pc, 0, T.st1, T.st2);
+    w.orow[i] = pick3(pc, T.r00, T.r01, T.r02) + local;
+    if (tt < T.total) {
+      const MvSeg& S = P.seg[w.sg[i]];
+      const uint8_t* row = tb + pick3u(pc, T.off0, T.off1, T.off2) + (uint32_t)local * S.L.row_bytes;
+      const int type = S.L.type;
+#pragma unroll
+      for (int j = 0; j < MvStep<ONE>::UPL; j++) {
+        const int c = lane + 32 * j;
+        if (c < U) unpack_unit<false>(type, row, S.L, c, w.u[i][j]);
+      }
+    }
+  }
+}
+
+template <bool ONE>
+__device__ __forceinline__ void step_dot(const MvPhase& P, const TileList& T, int t, const MvStep<ONE>& w,
+                                         const SmemMv& s, const XUnit& x0, float xscale) {
+  constexpr int R = MvStep<ONE>::R;
+  const int lane = threadIdx.x & 31;
+  const int U = P.seg[0].L.U;
+  float acc[R];
+#pragma unroll
+  for (int i = 0; i < R; i++) {
+    acc[i] = 0.f;
+    if (t + i * CK_WARPS < T.total) {
+#pragma unroll
+      for (int j = 0; j < MvStep<ONE>::UPL; j++) {
+        const int c = lane + 32 * j;
+        if (c < U) {
+          if (ONE) {
+            acc[i] += unit_dot8(w.u[i][j], x0);
+          } else {
+            XUnit xj;
+            load_xunit(s, c, xj);
+            acc[i] += unit_dot8(w.u[i][j], xj);
           }
         }
       }
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-      for (int i = 0; i < R; i++) acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], o);
-    float v = acc[0];
-#pragma unroll
-    for (int i = 1; i < R; i++)
-      if (lane == i) v = acc[i];
-    const int rr = r + lane * CK_WARPS;
-    if (lane < R && rr < nrows) out[r0 + rr] = add ? add[r0 + rr] + v : v;
   }
-}
-
-__device__ __forceinline__ void mv_run(const MvPhase& P, int phase_idx, SmemMv& s, Ring& R, int cta, int ncta,
-                                    int* err, int* abort_flag, unsigned long long* tp) {
-  stage_mark(tp, 0);
-  build_x(P.pro, P.k, s, cta);
-  stage_mark(tp, 1);
-  quant_x(P.k, s);
-  stage_mark(tp, 2);
-  int ntile = 0;
-  const int upl = (P.k + 1023) >> 10;
-  Cursor cur;
-  cur.phase = phase_idx; cur.seg = 0; cur.row = -1;
-  Tile t;
-  while (next_tile(R.ph, phase_idx + 1, cta, ncta, cur, t)) {
-    if (!ring_wait(R, err, abort_flag)) { R.ok = 0; return; }
-    if (ntile == 0) stage_mark(tp, 3);
-    const uint8_t* tb = R.buf + (size_t)(R.consumed & 1) * CK_TILE_BYTES;
-    for (int i = 0; i < t.npc; i++) {
-      const MvSeg& S = P.seg[t.pc[i].seg];
-      const uint8_t* base = tb + t.pc[i].soff;
-      int r0 = t.pc[i].r0, nrows = t.pc[i].r1 - t.pc[i].r0;
-      if (upl <= 1) mv_piece<true>(S, base, r0, nrows, s);
-      else mv_piece<false>(S, base, r0, nrows, s);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+    for (int i = 0; i < R; i++) acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], o);
+#pragma unroll
+  for (int i = 0; i < R; i++) {
+    if (lane == i && t + i * CK_WARPS < T.total) {
+      const MvSeg& S = P.seg[w.sg[i]];
+      const float v = xscale * acc[i];
+      S.out[w.orow[i]] = S.add ? S.add[w.orow[i]] + v : v;
     }
-    if (ntile == 0) stage_mark(tp, 4);
-    ring_release(R, cta, ncta);
-    if (ntile == 0) stage_mark(tp, 5);
-    ntile++;
   }
-  stage_mark(tp, 6);
 }
 
-__device__ __forceinline__ void phase_matvec(const MvPhase& P, int phase_idx, Smem& sm, Ring& R, int cta,
-                                             int ncta, int* err, int* abort_flag, unsigned long long* tp = nullptr) {
-  mv_run(P, phase_idx, sm.mv, R, cta, ncta, err, abort_flag, tp);
+// Warp steps t0, t0 + R*CK_WARPS, ... of a tile.  With 2-3 units per lane
+// each unit is unpacked and dotted in turn (its x unit read from shared
+// memory), which keeps a single unpacked unit live.
+template <bool ONE>
+__device__ __forceinline__ void mv_tile(const MvPhase& P, const uint8_t* tb, const TileList& T, int t0,
+                                        const SmemMv& s, const XUnit& x0, float xscale) {
+  constexpr int R = MvStep<ONE>::R;
+  if (ONE) {
+    for (int t = t0; t < T.total; t += R * CK_WARPS) {
+      MvStep<true> w;
+      step_unpack<true>(P, tb, T, t, w);
+      step_dot<true>(P, T, t, w, s, x0, xscale);
+    }
+    return;
+  }
+  const int lane = threadIdx.x & 31;
+  const int U = P.seg[0].L.U;
+  const int upl = (U + 31) >> 5;
+  for (int t = t0; t < T.total; t += CK_WARPS) {
+    const int pc = (t >= T.st1) + (t >= T.st2);
+    const int sg = pick3(pc, T.seg0, T.seg1, T.seg2);
+    const int local = t - pick3(pc, 0, T.st1, T.st2);
+    const MvSeg& S = P.seg[sg];
+    const uint8_t* row = tb + pick3u(pc, T.off0, T.off1, T.off2) + (uint32_t)local * S.L.row_bytes;
+    const int type = S.L.type;
+    float acc = 0.f;
+#pragma unroll 1
+    for (int j = 0; j < upl; j++) {
+      const int c = lane + 32 * j;
+      if (c < U) {
+        U8 u;
+        unpack_unit<false>(type, row, S.L, c, u);
+        XUnit xj;
+        load_xunit(s, c, xj);
+        acc += unit_dot8(u, xj);
+      }
+    }
+    acc = warp_sum(acc);
+    if (lane == 0) {
+      const int orow = pick3(pc, T.r00, T.r01, T.r02) + local;
+      const float v = xscale * acc;
+      S.out[orow] = S.add ? S.add[orow] + v : v;
+    }
+  }
+}
+
+// Prologue loads (fused path): element 32 g + lane of every group g of this
+// warp, issued before anything waits on them.
+template <int GPW>
+__device__ __forceinline__ void prologue_load(const Pro& p, int k, float (&va)[GPW], float (&vb)[GPW]) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int U = k >> 5, kind = p.kind;
+  const float* pb = (kind == PRO_SILU || kind == PRO_GELU) ? p.b : p.w0;
+#pragma unroll
+  for (int j = 0; j < GPW; j++) {
+    const int g = warp + j * CK_WARPS;
+    const int i = 32 * g + lane;
+    va[j] = g < U ? p.a[i] : 0.f;
+    vb[j] = (g < U && kind != PRO_COPY) ? pb[i] : 0.f;
+  }
+}
+
+// Fused prologue for COPY / NORM / SILU / GELU: one warp per 32-group, one
+// element per lane, into the quantized form of quant_x.  The RMS scale of
+// NORM is a scalar over the whole vector, so x is quantized without it (the
+// per-group quantization is scale-invariant) and the caller applies it to
+// each output row: y = inv * (W (a * w)), the RMS_NORM_WGSL product
+// (a * inv) * w with the scalar moved past the dot.  Returns that scale.
+template <int GPW>
+__device__ float prologue_quant(const Pro& p, int k, const float (&va)[GPW], const float (&vb)[GPW], SmemMv& s) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int U = k >> 5, kind = p.kind;
+  // the kind switch sits outside the group loop so the groups interleave
+  float ss = 0.f, vx[GPW];
+  if (kind == PRO_COPY) {
+#pragma unroll
+    for (int j = 0; j < GPW; j++) vx[j] = va[j];
+  } else if (kind == PRO_NORM) {
+#pragma unroll
+    for (int j = 0; j < GPW; j++) { vx[j] = va[j] * vb[j]; ss += va[j] * va[j]; }
+  } else if (kind == PRO_SILU) {
+#pragma unroll
+    for (int j = 0; j < GPW; j++) vx[j] = (va[j] / (1.0f + expf(-va[j]))) * vb[j];
+  } else {
+#pragma unroll
+    for (int j = 0; j < GPW; j++) vx[j] = gelu_tanh(va[j]) * vb[j];
+  }
+#pragma unroll
+  for (int j = 0; j < GPW; j++) {
+    const int g = warp + j * CK_WARPS;
+    const bool ok = g < U;                           // warp-uniform
+    const float v = vx[j];
+    const float amax = warp_max(fabsf(v));
+    const bool fin = amax <= 3.0e38f;
+    const float step = amax * (1.0f / 32639.0f);
+    const float inv = (step > 0.f && fin) ? 32639.0f / amax : 0.f;
+    const int X = max(-32639, min(32639, __float2int_rn(v * inv)));
+    const int h = (X + 128) >> 8;
+    int sum = X;
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if (ok) {
+      s.xh[32 * g + lane] = (int8_t)h;
+      s.xl[32 * g + lane] = (int8_t)(X - 256 * h);
+      if (lane == 0) s.sx[g] = fin ? step : __int_as_float(0x7fc00000);
+      if ((lane & 15) == 0) s.s16[2 * g + (lane >> 4)] = sum;
+    }
+  }
+  if (kind == PRO_NORM) {
+    ss = warp_sum(ss);
+    if (lane == 0) s.red[warp] = ss;
+  }
+  __syncthreads();
+  if (kind != PRO_NORM) return 1.0f;
+  float t = 0.f;
+#pragma unroll
+  for (int w = 0; w < CK_WARPS; w++) t += s.red[w];
+  return rms_inv(t, k, p.eps);
+}
+
+// One matvec phase on this CTA.  GPW = 32-groups of x per warp (k <= 512 *
+// GPW); ONE (k <= 1024) keeps the lane's x unit in registers.
+template <int GPW>
+__device__ __forceinline__ void mv_run_t(const MvPhase& P, SmemMv& s, Ring& R, int cta, int* err, int* abort_flag,
+                                         unsigned long long* tp) {
+  constexpr bool ONE = GPW <= 2;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  stage_mark(tp, 0);
+  float xscale = 1.0f;
+  if (P.pro.kind == PRO_GEMMA) {
+    build_x(P.pro, P.k, s, cta);
+    quant_x(P.k, s);
+  } else {
+    float va[GPW], vb[GPW];
+    prologue_load<GPW>(P.pro, P.k, va, vb);
+    xscale = prologue_quant<GPW>(P.pro, P.k, va, vb, s);
+  }
+  stage_mark(tp, 1);
+  XUnit x0;
+  if (ONE && lane < (P.k >> 5)) load_xunit(s, lane, x0);
+  int seg = 0, row = -1;
+  TileList T;
+  bool first = true;
+  while (next_tile(P, cta, seg, row, T)) {
+    if (!ring_wait(R, err, abort_flag)) { R.ok = 0; return; }
+    if (first) stage_mark(tp, 2);
+    mv_tile<ONE>(P, ring_buf(R.consumed), T, warp, s, x0, xscale);
+    if (first) stage_mark(tp, 3);
+    first = false;
+    ring_release(R, cta);
+  }
+  stage_mark(tp, 4);
+}
+
+__device__ __forceinline__ void mv_run(const MvPhase& P, SmemMv& s, Ring& R, int cta, int* err, int* abort_flag,
+                                       unsigned long long* tp) {
+  const int U = P.k >> 5;
+  if (U <= 2 * CK_WARPS) mv_run_t<2>(P, s, R, cta, err, abort_flag, tp);
+  else if (U <= 4 * CK_WARPS) mv_run_t<4>(P, s, R, cta, err, abort_flag, tp);
+  else mv_run_t<CK_KMAX / 32 / CK_WARPS>(P, s, R, cta, err, abort_flag, tp);
+}
+
+__device__ __forceinline__ void phase_matvec(const MvPhase& P, Smem& sm, Ring& R, int cta, int* err,
+                                             int* abort_flag, unsigned long long* tp = nullptr) {
+  mv_run(P, sm.mv, R, cta, err, abort_flag, tp);
 }
 
 // ---------------------------------------------------------------------------
@@ -692,41 +942,145 @@ __device__ __forceinline__ void rope_head(const float* src, const float* w, floa
   }
 }
 
-template <int E>
-__device__ __forceinline__ void load_kv(const void* base, int kv_f32, size_t off, float (&f)[E]) {
-  if (kv_f32) {
-    const float* p = (const float*)base + off;
+// E elements (one lane's share of a head row) of the KV cache, held in
+// registers in the cache's storage type until used: fp16 pairs or fp32 words.
+template <int E, bool F32>
+struct KvRow {
+  uint32_t w[F32 ? E : E / 2];
+};
+template <int E, bool F32>
+__device__ __forceinline__ void kv_zero(KvRow<E, F32>& r) {
 #pragma unroll
-    for (int e = 0; e < E; e += 2) {
-      float2 v = *(const float2*)(p + e);
-      f[e] = v.x;
-      f[e + 1] = v.y;
+  for (int i = 0; i < (F32 ? E : E / 2); i++) r.w[i] = 0u;
+}
+template <int E, bool F32>
+__device__ __forceinline__ void kv_load(const void* base, size_t off, KvRow<E, F32>& r) {
+  if (F32) {
+    const uint32_t* p = (const uint32_t*)base + off;
+    if (E == 2) {
+      const uint2 v = *(const uint2*)p;
+      r.w[0] = v.x; r.w[1] = v.y;
+    } else {
+#pragma unroll
+      for (int i = 0; i < E / 4; i++) {
+        const uint4 v = ((const uint4*)p)[i];
+        r.w[4 * i] = v.x; r.w[4 * i + 1] = v.y; r.w[4 * i + 2] = v.z; r.w[4 * i + 3] = v.w;
+      }
     }
   } else {
-    const __half* p = (const __half*)base + off;
-    if (E == 8) {
-      uint4 v = *(const uint4*)p;
-      const __half2* h = (const __half2*)&v;
-#pragma unroll
-      for (int e = 0; e < 4; e++) { float2 t = __half22float2(h[e]); f[2 * e] = t.x; f[2 * e + 1] = t.y; }
+    const uint16_t* p = (const uint16_t*)base + off;
+    if (E == 2) {
+      r.w[0] = *(const uint32_t*)p;
     } else if (E == 4) {
-      uint2 v = *(const uint2*)p;
-      const __half2* h = (const __half2*)&v;
-#pragma unroll
-      for (int e = 0; e < 2; e++) { float2 t = __half22float2(h[e]); f[2 * e] = t.x; f[2 * e + 1] = t.y; }
+      const uint2 v = *(const uint2*)p;
+      r.w[0] = v.x; r.w[1] = v.y;
     } else {
-      float2 t = __half22float2(*(const __half2*)p);
-      f[0] = t.x;
-      f[1] = t.y;
+      const uint4 v = *(const uint4*)p;
+      r.w[0] = v.x; r.w[1] = v.y; r.w[2] = v.z; r.w[3] = v.w;
     }
   }
 }
+template <int E, bool F32>
+__device__ __forceinline__ float kv_at(const KvRow<E, F32>& r, int e) {
+  if (F32) return __uint_as_float(r.w[e]);
+  const uint32_t w = r.w[e >> 1];
+  return __half2float(__ushort_as_half((unsigned short)((e & 1) ? (w >> 16) : (w & 0xFFFFu))));
+}
+// a value as the cache stores it (what a later read of the cache returns)
+template <bool F32>
+__device__ __forceinline__ float kv_round(float x) {
+  return F32 ? x : __half2float(__float2half_rn(x));
+}
 
+// One online-softmax step over two positions of a warp (the second may be
+// absent: score -inf and a zero row add nothing).
+template <int E, bool F32>
+__device__ __forceinline__ void softmax_pair(const float (&q)[E], const KvRow<E, F32>& k0, const KvRow<E, F32>& v0,
+                                             const KvRow<E, F32>& k1, const KvRow<E, F32>& v1, bool has1,
+                                             float scale, float& m, float& l, float (&acc)[E]) {
+  float d0 = 0.f, d1 = 0.f;
+#pragma unroll
+  for (int e = 0; e < E; e++) {
+    d0 += q[e] * kv_at(k0, e);
+    d1 += q[e] * kv_at(k1, e);
+  }
+  const float s0 = warp_sum(d0) * scale;
+  const float s1 = has1 ? warp_sum(d1) * scale : -INFINITY;
+  const float mn = fmaxf(m, fmaxf(s0, s1));
+  const float c = expf(m - mn), p0 = expf(s0 - mn), p1 = expf(s1 - mn);
+  l = l * c + p0 + p1;
+#pragma unroll
+  for (int e = 0; e < E; e++) acc[e] = acc[e] * c + p0 * kv_at(v0, e) + p1 * kv_at(v1, e);
+  m = mn;
+}
+
+// Merge of the S split partials (m, l, acc) of one kv head's G query heads:
+// out = sum_s acc_s * exp(m_s - M) / sum_s l_s * exp(m_s - M), M = max_s m_s.
+// Every load is issued in parallel: one round for the (m, l) pairs, one warp
+// per head for the weights, then each output element's S accumulator values
+// split over P adjacent lanes, eight loads in flight per lane.
 template <int E>
+__device__ __forceinline__ void attn_merge(const AttnPhase& P, SmemAt& s, int kvh, int S) {
+  constexpr int hd = 32 * E;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int G = P.group, NE = G * hd;
+  const float* pk = P.part + (size_t)kvh * P.smax * G * (hd + 2);
+  float* sm_m = s.wacc;                 // [S * G] split maxima, then weights
+  float* sm_l = s.wacc + 1024;          // [S * G] split sums
+  float* sm_L = s.wacc + 2048;          // [G] merged sums
+  for (int i = tid; i < S * G; i += CK_THREADS) {
+    const float* pp = pk + (size_t)i * (hd + 2);     // i = split * G + head
+    sm_m[i] = __ldcg(pp);
+    sm_l[i] = __ldcg(pp + 1);
+  }
+  __syncthreads();
+  for (int gg = warp; gg < G; gg += CK_WARPS) {
+    float M = -INFINITY;
+    for (int sp = lane; sp < S; sp += 32) M = fmaxf(M, sm_m[sp * G + gg]);
+    M = warp_max(M);
+    float L = 0.f;
+    for (int sp = lane; sp < S; sp += 32) {
+      const float f = expf(sm_m[sp * G + gg] - M);
+      L += sm_l[sp * G + gg] * f;
+      sm_m[sp * G + gg] = f;
+    }
+    L = warp_sum(L);
+    if (lane == 0) sm_L[gg] = L;
+  }
+  __syncthreads();
+  int Pw = 1;                                        // lanes per element (power of two)
+  while (Pw < 32 && 2 * Pw * NE <= CK_THREADS) Pw *= 2;
+  const int part = tid & (Pw - 1);
+  for (int e = tid / Pw; e < (CK_THREADS / Pw) * ((NE + CK_THREADS / Pw - 1) / (CK_THREADS / Pw));
+       e += CK_THREADS / Pw) {
+    const bool ok = e < NE;
+    const int gg = ok ? e / hd : 0, d = e % hd;
+    float A = 0.f;
+    for (int sp0 = part; sp0 < S; sp0 += 8 * Pw) {
+      float v[8];
+#pragma unroll
+      for (int j = 0; j < 8; j++) {
+        const int sp = sp0 + j * Pw;
+        v[j] = (ok && sp < S) ? __ldcg(pk + ((size_t)sp * G + gg) * (hd + 2) + 2 + d) : 0.f;
+      }
+#pragma unroll
+      for (int j = 0; j < 8; j++) {
+        const int sp = sp0 + j * Pw;
+        if (ok && sp < S) A += v[j] * sm_m[sp * G + gg];
+      }
+    }
+    for (int o = 1; o < Pw; o <<= 1) A += __shfl_xor_sync(0xffffffffu, A, o);
+    if (ok && part == 0) P.out[(size_t)(kvh * G + gg) * hd + d] = A / sm_L[gg];
+  }
+  if (tid == 0) P.counter[kvh] = 0u;
+}
+
+template <int E, bool F32>
 __device__ __forceinline__ void attn_unit(const AttnPhase& P, SmemAt& s, int kvh, int split, int pos,
                                           unsigned long long* tp) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int hd = P.hd, G = P.heads / P.kvh;
+  constexpr int hd = 32 * E;        // head_dim: one lane holds E elements of a row
+  const int G = P.group;
   const int start = (P.window != 0 && pos + 1 > P.window) ? pos + 1 - P.window : 0;
   const int npos = pos - start + 1;
   int chunk = (npos + P.smax - 1) / P.smax;
@@ -736,56 +1090,83 @@ __device__ __forceinline__ void attn_unit(const AttnPhase& P, SmemAt& s, int kvh
   const int t0 = start + split * chunk;
   const int t1 = min(t0 + chunk, pos + 1);
   const bool owner = split == S - 1;   // the split holding `pos` stores K/V there
+  // positions read from the cache; the owner takes `pos` from shared memory
+  const int tend = owner ? pos : t1;
+  const int wpg = CK_WARPS / G;      // warps per q head (G <= 8)
+  const int g = warp / wpg, sub = warp % wpg;
 
-  // --- every input of this unit in one round of loads ----------------------
+  // --- every global load of the unit issued in one round ---------------------
   stage_mark(tp, 0);
-  for (int d = tid; d < (hd >> 1); d += CK_THREADS) {
+  const size_t kvbase = (size_t)kvh * P.ctx * hd + lane * E;
+  int t = t0 + sub;
+  KvRow<E, F32> ka, va, kb, vb;      // the warp's first two positions
+  kv_zero(ka); kv_zero(va); kv_zero(kb); kv_zero(vb);
+  if (g < G) {
+    if (t < tend) { kv_load(P.kc, kvbase + (size_t)t * hd, ka); kv_load(P.vc, kvbase + (size_t)t * hd, va); }
+    if (t + wpg < tend) {
+      kv_load(P.kc, kvbase + (size_t)(t + wpg) * hd, kb);
+      kv_load(P.vc, kvbase + (size_t)(t + wpg) * hd, vb);
+    }
+  }
+  float invf = 0.f, qv0 = 0.f, qv1 = 0.f, kk = 0.f, vv = 0.f, wq = 0.f, wk = 0.f;
+  const float* qsrc = P.q + (size_t)kvh * G * hd;
+  if (tid < (hd >> 1)) invf = P.inv_freq[tid];
+  if (tid < G * hd) qv0 = qsrc[tid];
+  if (tid + CK_THREADS < G * hd) qv1 = qsrc[tid + CK_THREADS];
+  if (tid < hd) {
+    if (owner) {
+      kk = P.k[(size_t)kvh * hd + tid];
+      vv = P.v[(size_t)kvh * hd + tid];
+      if (P.kw) wk = P.kw[tid];
+    }
+    if (P.qw) wq = P.qw[tid];
+  }
+  if (tid < (hd >> 1)) {
     // angle = pos * theta^(-2d/hd) (rope_angle, :2885-2888); the power is the
     // per-layer table built at load time with the same powf
-    float ang = (float)pos * P.inv_freq[d];
     float sn, cn;
-    sincosf(ang, &sn, &cn);
-    s.cs[d] = make_float2(cn, sn);
+    sincosf((float)pos * invf, &sn, &cn);
+    s.cs[tid] = make_float2(cn, sn);
   }
-  for (int i = tid; i < G * hd; i += CK_THREADS) s.raw[i] = P.q[(size_t)kvh * G * hd + i];
-  for (int d = tid; d < hd; d += CK_THREADS) {
+  if (tid < G * hd) s.raw[tid] = qv0;
+  if (tid + CK_THREADS < G * hd) s.raw[tid + CK_THREADS] = qv1;
+  if (tid < hd) {
     if (owner) {
-      s.kvw[0][d] = P.k[(size_t)kvh * hd + d];
-      s.kvw[1][d] = P.v[(size_t)kvh * hd + d];
-      if (P.kw) s.kvw[3][d] = P.kw[d];
+      s.kvw[0][tid] = kk;
+      s.kvw[1][tid] = vv;
+      if (P.kw) s.kvw[3][tid] = wk;
     }
-    if (P.qw) s.kvw[2][d] = P.qw[d];
+    if (P.qw) s.kvw[2][tid] = wq;
   }
   __syncthreads();
   // --- per-head 1/rms of q (and k) for the QK-norm -----------------------
   if (P.qw) {
-    for (int g = warp; g < G + (owner ? 1 : 0); g += CK_WARPS) {
-      const float* src = g < G ? s.raw + g * hd : s.kvw[0];
+    for (int gg = warp; gg < G + (owner ? 1 : 0); gg += CK_WARPS) {
+      const float* src = gg < G ? s.raw + gg * hd : s.kvw[0];
       float ss = 0.f;
       for (int d = lane; d < hd; d += 32) ss += src[d] * src[d];
       ss = warp_sum(ss);
-      if (lane == 0) s.inv[g] = rms_inv(ss, hd, P.eps);
+      if (lane == 0) s.inv[gg] = rms_inv(ss, hd, P.eps);
     }
     __syncthreads();
   }
   // --- q: norm + rope into shared memory; owner: k/v into the cache --------
-  for (int g = 0; g < G; g++)
-    rope_head(s.raw + g * hd, P.qw ? s.kvw[2] : nullptr, P.qw ? s.inv[g] : 1.f, s.qs + g * hd, hd, P.interleaved,
-              s.cs, tid, CK_THREADS);
+  for (int gg = 0; gg < G; gg++)
+    rope_head(s.raw + gg * hd, P.qw ? s.kvw[2] : nullptr, P.qw ? s.inv[gg] : 1.f, s.qs + gg * hd, hd,
+              P.interleaved, s.cs, tid, CK_THREADS);
   if (owner) {
-    float* kst = s.wacc;  // scratch for the rotated k row
-    rope_head(s.kvw[0], P.kw ? s.kvw[3] : nullptr, P.kw ? s.inv[G] : 1.f, kst, hd, P.interleaved, s.cs, tid,
+    rope_head(s.kvw[0], P.kw ? s.kvw[3] : nullptr, P.kw ? s.inv[G] : 1.f, s.kst, hd, P.interleaved, s.cs, tid,
               CK_THREADS);
     __syncthreads();
-    size_t cb = ((size_t)kvh * P.ctx + pos) * hd;
-    for (int d = tid; d < hd; d += CK_THREADS) {
-      float kv = kst[d], vv = s.kvw[1][d];
-      if (P.kv_f32) {
-        ((float*)P.kc)[cb + d] = kv;
-        ((float*)P.vc)[cb + d] = vv;
+    const size_t cb = ((size_t)kvh * P.ctx + pos) * hd;
+    if (tid < hd) {
+      const float kv = s.kst[tid], vv2 = s.kvw[1][tid];
+      if (F32) {
+        ((float*)P.kc)[cb + tid] = kv;
+        ((float*)P.vc)[cb + tid] = vv2;
       } else {
-        ((__half*)P.kc)[cb + d] = __float2half_rn(kv);
-        ((__half*)P.vc)[cb + d] = __float2half_rn(vv);
+        ((__half*)P.kc)[cb + tid] = __float2half_rn(kv);
+        ((__half*)P.vc)[cb + tid] = __float2half_rn(vv2);
       }
     }
   }
@@ -793,8 +1174,6 @@ __device__ __forceinline__ void attn_unit(const AttnPhase& P, SmemAt& s, int kvh
   stage_mark(tp, 1);
 
   // --- online softmax: warps split into G groups, one q head per group -----
-  const int wpg = CK_WARPS / G;      // warps per head (G <= 8)
-  const int g = warp / wpg, sub = warp % wpg;
   float q[E], acc[E], m = -INFINITY, l = 0.f;
 #pragma unroll
   for (int e = 0; e < E; e++) {
@@ -802,38 +1181,43 @@ __device__ __forceinline__ void attn_unit(const AttnPhase& P, SmemAt& s, int kvh
     acc[e] = 0.f;
   }
   if (g < G) {
-    const size_t base = (size_t)kvh * P.ctx * hd + lane * E;
-    int t = t0 + sub;
-    for (; t + wpg < t1; t += 2 * wpg) {   // two positions in flight
-      float k0[E], v0[E], k1[E], v1[E];
-      load_kv<E>(P.kc, P.kv_f32, base + (size_t)t * hd, k0);
-      load_kv<E>(P.kc, P.kv_f32, base + (size_t)(t + wpg) * hd, k1);
-      load_kv<E>(P.vc, P.kv_f32, base + (size_t)t * hd, v0);
-      load_kv<E>(P.vc, P.kv_f32, base + (size_t)(t + wpg) * hd, v1);
-      float d0 = 0.f, d1 = 0.f;
-#pragma unroll
-      for (int e = 0; e < E; e++) { d0 += q[e] * k0[e]; d1 += q[e] * k1[e]; }
-      float s0 = warp_sum(d0) * P.scale, s1 = warp_sum(d1) * P.scale;
-      float mn = fmaxf(m, fmaxf(s0, s1));
-      float c = expf(m - mn), p0 = expf(s0 - mn), p1 = expf(s1 - mn);
-      l = l * c + p0 + p1;
-#pragma unroll
-      for (int e = 0; e < E; e++) acc[e] = acc[e] * c + p0 * v0[e] + p1 * v1[e];
-      m = mn;
+    // two positions per step, the next two loads in flight during the step
+    // (except for 256-wide fp32 rows, whose second pair would not fit the
+    // register budget: those load after the step)
+    constexpr bool PIPE = !(F32 && E == 8);
+    for (; t < tend; t += 2 * wpg) {
+      const int tn = t + 2 * wpg;
+      KvRow<E, F32> nka, nva, nkb, nvb;
+      if (PIPE) {
+        kv_zero(nka); kv_zero(nva); kv_zero(nkb); kv_zero(nvb);
+        if (tn < tend) { kv_load(P.kc, kvbase + (size_t)tn * hd, nka); kv_load(P.vc, kvbase + (size_t)tn * hd, nva); }
+        if (tn + wpg < tend) {
+          kv_load(P.kc, kvbase + (size_t)(tn + wpg) * hd, nkb);
+          kv_load(P.vc, kvbase + (size_t)(tn + wpg) * hd, nvb);
+        }
+      }
+      softmax_pair<E, F32>(q, ka, va, kb, vb, t + wpg < tend, P.scale, m, l, acc);
+      if (PIPE) {
+        ka = nka; va = nva; kb = nkb; vb = nvb;
+      } else {
+        kv_zero(ka); kv_zero(va); kv_zero(kb); kv_zero(vb);
+        if (tn < tend) { kv_load(P.kc, kvbase + (size_t)tn * hd, ka); kv_load(P.vc, kvbase + (size_t)tn * hd, va); }
+        if (tn + wpg < tend) {
+          kv_load(P.kc, kvbase + (size_t)(tn + wpg) * hd, kb);
+          kv_load(P.vc, kvbase + (size_t)(tn + wpg) * hd, vb);
+        }
+      }
     }
-    if (t < t1) {
-      float k0[E], v0[E];
-      load_kv<E>(P.kc, P.kv_f32, base + (size_t)t * hd, k0);
-      load_kv<E>(P.vc, P.kv_f32, base + (size_t)t * hd, v0);
+    if (owner && sub == 0) {   // position pos, as the cache now holds it
       float d0 = 0.f;
 #pragma unroll
-      for (int e = 0; e < E; e++) d0 += q[e] * k0[e];
-      float s0 = warp_sum(d0) * P.scale;
-      float mn = fmaxf(m, s0);
-      float c = expf(m - mn), p0 = expf(s0 - mn);
+      for (int e = 0; e < E; e++) d0 += q[e] * kv_round<F32>(s.kst[lane * E + e]);
+      const float s0 = warp_sum(d0) * P.scale;
+      const float mn = fmaxf(m, s0);
+      const float c = expf(m - mn), p0 = expf(s0 - mn);
       l = l * c + p0;
 #pragma unroll
-      for (int e = 0; e < E; e++) acc[e] = acc[e] * c + p0 * v0[e];
+      for (int e = 0; e < E; e++) acc[e] = acc[e] * c + p0 * kv_round<F32>(s.kvw[1][lane * E + e]);
       m = mn;
     }
   }
@@ -883,31 +1267,21 @@ __device__ __forceinline__ void attn_unit(const AttnPhase& P, SmemAt& s, int kvh
       part[gg * (hd + 2) + 1] = L;
     }
   }
+  stage_mark(tp, 4);
   // --- last split to finish merges all splits --------------------------------
-  __threadfence();
+  // (acq_rel: this CTA's partials are published before the count; the last
+  // CTA's read of the count orders its reads of the other partials after it)
   __syncthreads();
   if (tid == 0) {
-    unsigned prev = atomicAdd(&P.counter[kvh], 1u);
+    unsigned prev;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(P.counter + kvh) : "memory");
     s.last = (prev == (unsigned)(S - 1));
   }
   __syncthreads();
+  stage_mark(tp, 5);
   if (!s.last) return;
-  __threadfence();
-  const float* pk = P.part + (size_t)kvh * P.smax * G * (hd + 2);
-  for (int i = tid; i < G * hd; i += CK_THREADS) {
-    int gg = i / hd, d = i % hd;
-    float M = -INFINITY;
-    for (int sp = 0; sp < S; sp++) M = fmaxf(M, __ldcg(pk + ((size_t)sp * G + gg) * (hd + 2)));
-    float L = 0.f, A = 0.f;
-    for (int sp = 0; sp < S; sp++) {
-      const float* pp = pk + ((size_t)sp * G + gg) * (hd + 2);
-      float f = expf(__ldcg(pp) - M);
-      L += __ldcg(pp + 1) * f;
-      A += __ldcg(pp + 2 + d) * f;
-    }
-    P.out[(size_t)(kvh * G + gg) * hd + d] = A / L;
-  }
-  if (tid == 0) P.counter[kvh] = 0u;
+  attn_merge<E>(P, s, kvh, S);
+  stage_mark(tp, 6);
 }
 
 __device__ __forceinline__ void phase_attn(const AttnPhase& P, Smem& sm, const CkDev& D, int cta, int ncta, int pos,
@@ -918,9 +1292,15 @@ __device__ __forceinline__ void phase_attn(const AttnPhase& P, Smem& sm, const C
   for (int u = cta; u < units; u += ncta) {
     int kvh = u % P.kvh, split = u / P.kvh;
     unsigned long long* up = (tp && u == cta) ? tp : nullptr;
-    if (P.hd == 64) attn_unit<2>(P, sm.at, kvh, split, pos, up);
-    else if (P.hd == 128) attn_unit<4>(P, sm.at, kvh, split, pos, up);
-    else attn_unit<8>(P, sm.at, kvh, split, pos, up);
+    if (P.kv_f32) {
+      if (P.hd == 64) attn_unit<2, true>(P, sm.at, kvh, split, pos, up);
+      else if (P.hd == 128) attn_unit<4, true>(P, sm.at, kvh, split, pos, up);
+      else attn_unit<8, true>(P, sm.at, kvh, split, pos, up);
+    } else {
+      if (P.hd == 64) attn_unit<2, false>(P, sm.at, kvh, split, pos, up);
+      else if (P.hd == 128) attn_unit<4, false>(P, sm.at, kvh, split, pos, up);
+      else attn_unit<8, false>(P, sm.at, kvh, split, pos, up);
+    }
     __syncthreads();
   }
 }
@@ -1133,10 +1513,12 @@ __device__ __forceinline__ void run_phase(const Phase* ph, int i, Smem& sm, Ring
                                           int ncta, int pos) {
   const Phase& p = ph[i];
   unsigned long long* tp =
-      (D.trace && cta == 0 && i < 512) ? D.trace + CK_TRACE_STAGE_BASE + i * 8 : nullptr;
+      !D.trace ? nullptr
+      : (i == 2 && cta < 1024) ? D.trace + CK_TRACE_CTA_BASE + cta * 16 + 8
+      : (cta == 0 && i < 512) ? D.trace + CK_TRACE_STAGE_BASE + i * 8 : nullptr;
   switch (p.kind) {
     case PH_EMBED: phase_embed(p.em, D, cta, ncta, pos); break;
-    case PH_MATVEC: phase_matvec(p.mv, i, sm, R, cta, ncta, &D.st->err, &D.st->abort_flag, tp); break;
+    case PH_MATVEC: phase_matvec(p.mv, sm, R, cta, &D.st->err, &D.st->abort_flag, tp); break;
     case PH_ATTN: phase_attn(p.at, sm, D, cta, ncta, pos, tp); break;
     case PH_ARGMAX1: phase_argmax1(D, sm, cta, ncta); break;
     case PH_ARGMAX2: phase_argmax2(D, sm, cta); break;
@@ -1151,16 +1533,17 @@ __device__ __forceinline__ void run_phase(const Phase* ph, int i, Smem& sm, Ring
 // One launch per phase (CUDA-graph mode): one kernel per phase kind so each
 // gets its own register allocation.
 __global__ void __launch_bounds__(CK_THREADS, 1) k_mv(const Phase* __restrict__ ph, CkDev D) {
-  extern __shared__ __align__(128) uint8_t dyn[];
   __shared__ Smem sm;
   unsigned long long* tr = (D.trace && threadIdx.x == 0 && blockIdx.x < 1024)
                                ? D.trace + CK_TRACE_MV_BASE + blockIdx.x * 8 : nullptr;
   if (tr) tr[0] = gtimer();
   Ring R;
-  const Phase* sph = launch_start(R, dyn, ph, 1, blockIdx.x, gridDim.x, &D.st->err, &D.st->abort_flag);
+  const Phase* sph = launch_start(R, ph, 1, blockIdx.x, &D.st->err, &D.st->abort_flag);
   if (!sph) return;
   if (tr) tr[1] = gtimer();
-  phase_matvec(sph->mv, 0, sm, R, blockIdx.x, gridDim.x, &D.st->err, &D.st->abort_flag);
+  unsigned long long* tp = (D.trace && blockIdx.x == 0 && sph->index < 512)
+                               ? D.trace + CK_TRACE_STAGE_BASE + sph->index * 8 : nullptr;
+  phase_matvec(sph->mv, sm, R, blockIdx.x, &D.st->err, &D.st->abort_flag, tp);
   if (tr) tr[2] = gtimer();
 }
 __global__ void __launch_bounds__(CK_THREADS, 1) k_attn(const Phase* __restrict__ ph, CkDev D) {
@@ -1189,12 +1572,13 @@ __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
 // Grid-wide barrier for the cooperative megakernel.  Bounded: after ~2^21
 // polls (seconds) the CTA flags CK_DERR_BARRIER + abort and returns false;
 // every other CTA sees the abort flag and returns too.
-__device__ bool grid_sync(CkState* st, unsigned target) {
+__device__ __forceinline__ bool grid_sync(CkState* st, unsigned target) {
   __shared__ int s_ok;
   __syncthreads();
   if (threadIdx.x == 0) {
-    __threadfence();
-    atomicAdd(&st->bar, 1u);
+    // release: every write of this CTA before the __syncthreads above is
+    // visible to a CTA whose acquire load sees the count
+    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(&st->bar) : "memory");
     int ok = 1;
     unsigned spins = 0;
     while (ld_acquire_u32(&st->bar) < target) {
@@ -1214,22 +1598,27 @@ __device__ bool grid_sync(CkState* st, unsigned target) {
 
 // Whole step in one cooperative launch (megakernel mode).
 __global__ void __launch_bounds__(CK_THREADS, 1) k_mega(const Phase* __restrict__ ph, int nph, CkDev D) {
-  extern __shared__ __align__(128) uint8_t dyn[];
   __shared__ Smem sm;
   const int pos = D.st->pos;   // constant for the whole step (phase_finish runs last)
   Ring R;
-  const Phase* sph = launch_start(R, dyn, ph, nph, blockIdx.x, gridDim.x, &D.st->err, &D.st->abort_flag);
+  const Phase* sph = launch_start(R, ph, nph, blockIdx.x, &D.st->err, &D.st->abort_flag);
   if (!sph) return;
   unsigned target = 0;
   const bool tr = D.trace && blockIdx.x == 0 && threadIdx.x == 0;
+  // per-CTA stamps of phases 1..4: end of the phase and exit of its barrier
+  unsigned long long* ct = (D.trace && threadIdx.x == 0 && blockIdx.x < 1024)
+                               ? D.trace + CK_TRACE_CTA_BASE + blockIdx.x * 16 : nullptr;
+#pragma unroll 1
   for (int i = 0; i < nph; i++) {
     if (tr && 2 * i + 1 < CK_TRACE_MV_BASE) D.trace[2 * i] = gtimer();
     run_phase(sph, i, sm, R, D, blockIdx.x, gridDim.x, pos);
     if (tr && 2 * i + 1 < CK_TRACE_MV_BASE) D.trace[2 * i + 1] = gtimer();
+    if (ct && i >= 1 && i <= 4) ct[i - 1] = gtimer();
     if (!R.ok) return;
     if (i + 1 < nph) {
       target += gridDim.x;
       if (!grid_sync(D.st, target)) return;
     }
+    if (ct && i >= 1 && i <= 4) ct[i + 3] = gtimer();
   }
 }
