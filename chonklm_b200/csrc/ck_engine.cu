@@ -227,6 +227,27 @@ Phase mk_mv(ck_engine* h, const Pro& pro, int k, std::initializer_list<MvSeg> se
   return p;
 }
 
+// The down projection's prologue.  When every CTA's share of the gate/up
+// rows fits the staging rows, the gate/up phase applies the activation to its
+// own rows (act(gate) * up into h->g) and down copies that; otherwise down
+// applies it to the whole vector in its prologue.
+Pro glu_input(ck_engine* h, Phase& gateup, int epi) {
+  const int n = gateup.mv.seg[0].n;
+  const int grid = n < h->sms ? n : h->sms;    // the smallest grid either mode launches
+  Pro p{};
+  if ((n + grid - 1) / grid <= CK_GLU_MAX && gateup.mv.seg[1].n == n) {
+    gateup.mv.epi = epi;
+    gateup.mv.glu_out = h->g;
+    p.kind = PRO_COPY;
+    p.a = h->g;
+  } else {
+    p.kind = epi == EPI_SILU ? PRO_SILU : PRO_GELU;
+    p.a = h->g;
+    p.b = h->u;
+  }
+  return p;
+}
+
 void build_schedule(ck_engine* h, bool logits, std::vector<Phase>& out) {
   const ck_model_cfg& c = h->cfg;
   const int H = c.hidden, hd = c.head_dim, qd = c.heads * hd;
@@ -286,17 +307,13 @@ void build_schedule(ck_engine* h, bool logits, std::vector<Phase>& out) {
       out.push_back(mk_mv(h, pc, qd, {seg(W.o, cur, cur)}));
       out.push_back(mk_mv(h, pro_norm(cur, W.post_norm, c.norm_eps), H,
                           {seg(W.gate, h->g, nullptr), seg(W.up, h->u, nullptr)}));
-      Pro ps{};
-      ps.kind = PRO_SILU; ps.a = h->g; ps.b = h->u;
-      out.push_back(mk_mv(h, ps, c.intermediate, {seg(W.down, cur, cur)}));
+      out.push_back(mk_mv(h, glu_input(h, out.back(), EPI_SILU), c.intermediate, {seg(W.down, cur, cur)}));
     } else {
       out.push_back(mk_mv(h, pc, qd, {seg(W.o, h->tmp, nullptr)}));
       out.push_back(mk_mv(h, pro_gemma(h->tmp, W.post_norm, cur, other, W.pre_ffn, c.norm_eps), H,
                           {seg(W.gate, h->g, nullptr), seg(W.up, h->u, nullptr)}));
       std::swap(cur, other);
-      Pro pg{};
-      pg.kind = PRO_GELU; pg.a = h->g; pg.b = h->u;
-      out.push_back(mk_mv(h, pg, c.intermediate, {seg(W.down, h->tmp, nullptr)}));
+      out.push_back(mk_mv(h, glu_input(h, out.back(), EPI_GELU), c.intermediate, {seg(W.down, h->tmp, nullptr)}));
     }
   }
   if (logits) {

@@ -110,12 +110,16 @@ struct MvSeg {
   uint32_t soff;            // byte offset of this segment's rows in a packed tile
 };
 
+enum { EPI_NONE = 0, EPI_SILU = 1, EPI_GELU = 2 };
+#define CK_GLU_MAX 256        // rows per CTA a fused gate/up epilogue stages
+
 struct MvPhase {
   Pro pro;
   int k;
   int nseg;
   int packed;               // every CTA's rows of all segments fit one tile
-  int pad_;
+  int epi;                  // EPI_SILU / EPI_GELU: segments 0, 1 are gate, up
+  float* glu_out;           // with epi: act(gate) * up, the down projection's input
   MvSeg seg[3];
 };
 
@@ -183,6 +187,7 @@ struct SmemMv {
   float sx[CK_KMAX / 32];
   alignas(8) int s16[CK_KMAX / 16];
   float red[CK_WARPS * 2];
+  float glu[2][CK_GLU_MAX];        // this CTA's gate and up rows (fused epilogue)
 };
 struct SmemAt {
   float qs[CK_GMAX * CK_HDMAX];
@@ -677,9 +682,17 @@ __device__ __forceinline__ void step_unpack(const MvPhase& P, const uint8_t* tb,
   }
 }
 
+// Store one output row: y = add + v, or, with a fused gate/up epilogue, the
+// CTA's staging row in shared memory.
+__device__ __forceinline__ void mv_store(const MvPhase& P, int sg, int orow, float v, SmemMv& s, int cta) {
+  const MvSeg& S = P.seg[sg];
+  if (P.epi) s.glu[sg][orow - cta * S.per] = v;
+  else S.out[orow] = S.add ? S.add[orow] + v : v;
+}
+
 template <bool ONE>
 __device__ __forceinline__ void step_dot(const MvPhase& P, const TileList& T, int t, const MvStep<ONE>& w,
-                                         const SmemMv& s, const XUnit& x0, float xscale) {
+                                         SmemMv& s, const XUnit& x0, float xscale, int cta) {
   constexpr int R = MvStep<ONE>::R;
   const int lane = threadIdx.x & 31;
   const int U = P.seg[0].L.U;
@@ -709,11 +722,7 @@ __device__ __forceinline__ void step_dot(const MvPhase& P, const TileList& T, in
     for (int i = 0; i < R; i++) acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], o);
 #pragma unroll
   for (int i = 0; i < R; i++) {
-    if (lane == i && t + i * CK_WARPS < T.total) {
-      const MvSeg& S = P.seg[w.sg[i]];
-      const float v = xscale * acc[i];
-      S.out[w.orow[i]] = S.add ? S.add[w.orow[i]] + v : v;
-    }
+    if (lane == i && t + i * CK_WARPS < T.total) mv_store(P, w.sg[i], w.orow[i], xscale * acc[i], s, cta);
   }
 }
 
@@ -722,13 +731,13 @@ __device__ __forceinline__ void step_dot(const MvPhase& P, const TileList& T, in
 // memory), which keeps a single unpacked unit live.
 template <bool ONE>
 __device__ __forceinline__ void mv_tile(const MvPhase& P, const uint8_t* tb, const TileList& T, int t0,
-                                        const SmemMv& s, const XUnit& x0, float xscale) {
+                                        SmemMv& s, const XUnit& x0, float xscale, int cta) {
   constexpr int R = MvStep<ONE>::R;
   if (ONE) {
     for (int t = t0; t < T.total; t += R * CK_WARPS) {
       MvStep<true> w;
       step_unpack<true>(P, tb, T, t, w);
-      step_dot<true>(P, T, t, w, s, x0, xscale);
+      step_dot<true>(P, T, t, w, s, x0, xscale, cta);
     }
     return;
   }
@@ -755,11 +764,7 @@ __device__ __forceinline__ void mv_tile(const MvPhase& P, const uint8_t* tb, con
       }
     }
     acc = warp_sum(acc);
-    if (lane == 0) {
-      const int orow = pick3(pc, T.r00, T.r01, T.r02) + local;
-      const float v = xscale * acc;
-      S.out[orow] = S.add ? S.add[orow] + v : v;
-    }
+    if (lane == 0) mv_store(P, sg, pick3(pc, T.r00, T.r01, T.r02) + local, xscale * acc, s, cta);
   }
 }
 
@@ -863,10 +868,20 @@ __device__ __forceinline__ void mv_run_t(const MvPhase& P, SmemMv& s, Ring& R, i
   while (next_tile(P, cta, seg, row, T)) {
     if (!ring_wait(R, err, abort_flag)) { R.ok = 0; return; }
     if (first) stage_mark(tp, 2);
-    mv_tile<ONE>(P, ring_buf(R.consumed), T, warp, s, x0, xscale);
+    mv_tile<ONE>(P, ring_buf(R.consumed), T, warp, s, x0, xscale, cta);
     if (first) stage_mark(tp, 3);
     first = false;
     ring_release(R, cta);
+  }
+  if (P.epi) {
+    // fused SILU_MUL_WGSL (:3529-3547) / GELU_TANH_MUL_WGSL (:3568-3599) over
+    // this CTA's rows (the release above synchronised the staging rows)
+    int lo, hi;
+    seg_range(P.seg[0], cta, lo, hi);
+    for (int i = threadIdx.x; i < hi - lo; i += CK_THREADS) {
+      const float g = s.glu[0][i], u = s.glu[1][i];
+      P.glu_out[lo + i] = P.epi == EPI_SILU ? (g / (1.0f + expf(-g))) * u : gelu_tanh(g) * u;
+    }
   }
   stage_mark(tp, 4);
 }

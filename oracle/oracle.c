@@ -157,6 +157,7 @@ size_t or_row_bytes(int t, int k) { return (size_t)(k / or_block_weights(t)) * o
 /* Dequantize `n` rows of `k` weights. */
 void or_dequant(int t, const uint8_t* w, int k, int n, float* out) {
   size_t rb = or_row_bytes(t, k);
+#pragma omp parallel for schedule(static)
   for (int r = 0; r < n; r++)
     for (int c = 0; c < k; c++) out[(size_t)r * k + c] = weight_at(t, w + rb * r, (uint32_t)c);
 }
@@ -173,6 +174,8 @@ void or_embedding(int t, const uint8_t* table, int k, uint32_t token, float scal
  * `sum = sum + input[k] * w`, then a stride-64..1 tree. */
 void or_matvec(int t, const uint8_t* w, int k, int n, const float* x, float* y, int mode) {
   size_t rb = or_row_bytes(t, k);
+  /* rows are independent: spreading them over host threads changes no result */
+#pragma omp parallel for schedule(static)
   for (int r = 0; r < n; r++) {
     const uint8_t* row = w + rb * r;
     if (mode == OR_MODE_F64) {
@@ -308,6 +311,8 @@ void or_attention(const float* q, const float* kc, const float* vc, float* out, 
                   int kv_heads, int hd, int max_ctx, int pos, int window, float attn_scale, int mode) {
   int group = heads / kv_heads;
   uint32_t start = (window != 0 && (uint32_t)pos + 1u > (uint32_t)window) ? (uint32_t)pos + 1u - (uint32_t)window : 0u;
+  /* heads are independent (each owns its row of `scores`) */
+#pragma omp parallel for schedule(static)
   for (int h = 0; h < heads; h++) {
     int kvh = h / group;
     for (uint32_t t = start; t <= (uint32_t)pos; t++) {
