@@ -225,6 +225,9 @@ def main():
     ap.add_argument("--mode", type=int, default=0, help="0 megakernel, 1 per-phase CUDA graph")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-matvec", action="store_true")
+    ap.add_argument("--profile", type=int, default=0, metavar="N",
+                    help="profiling run for ncu: prefill the prompt (megakernel), decode N tokens in --mode, "
+                         "print nothing else")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -276,6 +279,16 @@ def main():
     if sampling:
         samp, _ = _lib.make_sampling(sampling["temperature"], sampling["topP"], sampling["topK"], 1.0,
                                      sampling["seed"], 0)
+    if args.profile:
+        eng.set_mode(0)
+        nid = eng.prefill(prompt, True, samp)
+        eng.set_mode(args.mode)
+        eng.enqueue_decode_steps(args.profile)
+        eng.sync()
+        print(json.dumps({"profile": args.config, "mode": args.mode, "tokens": args.profile,
+                          "position": eng.position}), flush=True)
+        loaded.engine.dispose()
+        return
     nid = eng.prefill(prompt, True, samp)
     ids0 = eng.decode(nid, 2, samp)           # stores the first id at the prompt end
     eng.truncate(prompt_len)
@@ -345,10 +358,15 @@ def main():
         peak, peak_kind = peaks()
         per_tok_s = (tot_ms / 1000.0) / (gen * args.steps)
         achieved = bytes_per_token / per_tok_s / 1e9
-        traffic = None
+        # DRAM bytes (read + write) of one launch of the dominant kernel, from the
+        # committed ncu capture of this workload (profiles/); null when absent
+        traffic, traffic_note = None, None
         try:
             with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
-                traffic = json.load(f).get(args.config)
+                t = json.load(f).get(args.config)
+            if t and args.mode == 0:
+                traffic = t["bytes_per_launch"]
+                traffic_note = f"ncu dram__bytes_read+write of one {t['kernel']} launch at position {t['position']}"
         except Exception:
             traffic = None
         cpu = None
@@ -378,7 +396,7 @@ def main():
                     "h2d_bytes_per_step": int(statistics.mean(x[0] for x in e2e_io)),
                     "d2h_bytes_per_step": int(statistics.mean(x[1] for x in e2e_io))},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "traffic": traffic,
+                         "frac": round(achieved / peak, 4), "traffic": traffic, "traffic_note": traffic_note,
                          "peak_source": peak_kind,
                          "bytes_per_token": round(bytes_per_token), "us_per_token": round(per_tok_s * 1e6, 2)},
             "cpu_baseline": cpu,
