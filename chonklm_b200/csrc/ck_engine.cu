@@ -64,9 +64,13 @@ struct ck_engine {
   // device state
   CkState* st = nullptr;
   CkDev D;
+  // inter-phase activations: 8-byte tagged words (value + tag, see ck_ops.cuh)
   float *resA = nullptr, *resB = nullptr, *tmp = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *attn = nullptr,
-        *g = nullptr, *u = nullptr, *part = nullptr;
-  unsigned* counters = nullptr;
+        *g = nullptr, *u = nullptr;
+  float* part = nullptr;
+  unsigned* counters = nullptr;   // [layers][kv_heads] finished attention splits
+  uint32_t epoch_steps = 1;       // mirror of CkState::epoch
+  std::vector<std::pair<void*, size_t>> tagged_bufs;
   float* inv_freq = nullptr;  // [layers][head_dim/2] RoPE inverse frequencies
   uint8_t* kv = nullptr;
   size_t kv_bytes = 0;
@@ -248,6 +252,48 @@ Pro glu_input(ck_engine* h, Phase& gateup, int epi) {
   return p;
 }
 
+// Inter-phase activations are tagged words; weights and logits are plain.
+bool tagged_buffer(const ck_engine* h, const void* p) {
+  return p && (p == h->resA || p == h->resB || p == h->tmp || p == h->q || p == h->k || p == h->v || p == h->attn ||
+               p == h->g || p == h->u);
+}
+
+// Walk a schedule in order: a read of a tagged buffer expects the tag of its
+// latest writer (phase index + 1), a write carries the writer's own tag.
+void assign_tags(ck_engine* h, std::vector<Phase>& ph) {
+  std::map<const void*, int> last;
+  auto rd = [&](const void* p) {
+    if (!tagged_buffer(h, p)) return 0;
+    auto it = last.find(p);
+    return it == last.end() ? 0 : it->second;
+  };
+  auto wr = [&](const void* p, int me) {
+    if (!tagged_buffer(h, p)) return 0;
+    last[p] = me;
+    return me;
+  };
+  for (size_t i = 0; i < ph.size(); i++) {
+    Phase& p = ph[i];
+    const int me = (int)i + 1;
+    if (p.kind == PH_EMBED) {
+      p.em.tout = wr(p.em.out, me);
+    } else if (p.kind == PH_MATVEC) {
+      Pro& r = p.mv.pro;
+      r.ta = rd(r.a);
+      r.tb = (r.kind == PRO_SILU || r.kind == PRO_GELU) ? rd(r.b) : 0;
+      r.trin = r.kind == PRO_GEMMA ? rd(r.rin) : 0;
+      for (int s = 0; s < p.mv.nseg; s++) p.mv.seg[s].tadd = rd(p.mv.seg[s].add);
+      if (r.kind == PRO_GEMMA) r.trout = wr(r.rout, me);
+      if (p.mv.epi) p.mv.tglu = wr(p.mv.glu_out, me);
+      else
+        for (int s = 0; s < p.mv.nseg; s++) p.mv.seg[s].tout = wr(p.mv.seg[s].out, me);
+    } else if (p.kind == PH_ATTN) {
+      p.at.tqkv = rd(p.at.q);
+      p.at.tout = wr(p.at.out, me);
+    }
+  }
+}
+
 void build_schedule(ck_engine* h, bool logits, std::vector<Phase>& out) {
   const ck_model_cfg& c = h->cfg;
   const int H = c.hidden, hd = c.head_dim, qd = c.heads * hd;
@@ -286,7 +332,7 @@ void build_schedule(ck_engine* h, bool logits, std::vector<Phase>& out) {
     a.at.vc = h->kv + (size_t)(2 * i + 1) * per;
     a.at.out = h->attn;
     a.at.part = h->part;
-    a.at.counter = h->counters;
+    a.at.counter = h->counters + (size_t)i * c.kv_heads;
     a.at.heads = c.heads; a.at.kvh = c.kv_heads; a.at.hd = hd; a.at.ctx = c.context_length;
     a.at.group = c.heads / c.kv_heads;
     a.at.window = (int)c.layer_window[i];
@@ -320,9 +366,11 @@ void build_schedule(ck_engine* h, bool logits, std::vector<Phase>& out) {
     Pro pf = !gemma ? pro_norm(cur, h->final_norm, c.norm_eps)
                     : pro_gemma(h->tmp, h->L[c.layers - 1].post_ffn, cur, other, h->final_norm, c.norm_eps);
     out.push_back(mk_mv(h, pf, H, {seg(h->head, h->D.logits, nullptr)}));
+    out.back().barrier_after = 1;   // argmax stage 1 reads all logits (plain floats)
     Phase a1;
     memset(&a1, 0, sizeof a1);
     a1.kind = PH_ARGMAX1;
+    a1.barrier_after = 1;           // select reads every chunk's candidate
     a1.grid = (c.vocab + 255) / 256;
     if (a1.grid > h->sms * 4) a1.grid = h->sms * 4;
     out.push_back(a1);
@@ -334,6 +382,7 @@ void build_schedule(ck_engine* h, bool logits, std::vector<Phase>& out) {
   f.need_logits = logits ? 1 : 0;
   out.push_back(f);
   for (size_t i = 0; i < out.size(); i++) out[i].index = (int)i;
+  assign_tags(h, out);
 }
 
 int enqueue_phases(ck_engine* h, bool logits, int mode, cudaStream_t s) {
@@ -371,7 +420,26 @@ int capture(ck_engine* h, bool logits, int mode, cudaGraphExec_t* out) {
   return CK_OK;
 }
 
+// Clear every tagged buffer and the attention counters and restart the
+// device step counter at 1, so no stored tag can match a later step: at
+// set-up, after a step gave up part-way, and before the 22-bit step field
+// of the tags would wrap.
+int epoch_restart(ck_engine* h) {
+  CKC(h, cudaStreamSynchronize(h->stream));
+  for (auto& b : h->tagged_bufs) CKC(h, cudaMemset(b.first, 0, b.second));
+  CKC(h, cudaMemset(h->counters, 0, (size_t)h->cfg.layers * h->cfg.kv_heads * 4));
+  const uint32_t one = 1;
+  CKC(h, cudaMemcpy(&h->st->epoch, &one, 4, cudaMemcpyHostToDevice));
+  h->epoch_steps = 1;
+  return CK_OK;
+}
+
 int launch_step(ck_engine* h, bool logits) {
+  if (h->epoch_steps >= (1u << 22) - 2) {
+    int rc = epoch_restart(h);
+    if (rc) return rc;
+  }
+  h->epoch_steps++;
   cudaGraphExec_t gx = logits ? h->gx_logits[h->mode] : h->gx_prefill[h->mode];
   if (gx) {
     CKC(h, cudaGraphLaunch(gx, h->stream));
@@ -424,6 +492,7 @@ int check_device(ck_engine* h) {
     cudaMemsetAsync(&h->st->err, 0, 4, h->stream);
     cudaMemsetAsync(&h->st->abort_flag, 0, 4, h->stream);
     cudaStreamSynchronize(h->stream);
+    if (bits & ~CK_DERR_TOKEN) epoch_restart(h);   // a step gave up part-way
     if (bits & CK_DERR_TOKEN) return h->fail(CK_EDEVICE, "token id outside embedding table");
     if (bits & CK_DERR_BARRIER) return h->fail(CK_EDEVICE, "device grid barrier timed out");
     return h->fail(CK_EDEVICE, "device error bits 0x%x", bits);
@@ -587,18 +656,19 @@ int ck_finalize(ck_engine* h) {
   if ((rc = dalloc(h, &h->D.cand_idx, (size_t)groups * 4))) return rc;
   CKC(h, cudaMemset(h->D.tokens, 0, (size_t)c.context_length * 4));
   CKC(h, cudaMemset(h->D.pen_mask, 0, (size_t)((c.vocab + 31) / 32) * 4));
-  if ((rc = dalloc(h, &h->resA, (size_t)H * 4))) return rc;
-  if ((rc = dalloc(h, &h->resB, (size_t)H * 4))) return rc;
-  if ((rc = dalloc(h, &h->tmp, (size_t)H * 4))) return rc;
-  if ((rc = dalloc(h, &h->q, (size_t)c.heads * hd * 4))) return rc;
-  if ((rc = dalloc(h, &h->k, (size_t)c.kv_heads * hd * 4))) return rc;
-  if ((rc = dalloc(h, &h->v, (size_t)c.kv_heads * hd * 4))) return rc;
-  if ((rc = dalloc(h, &h->attn, (size_t)c.heads * hd * 4))) return rc;
-  if ((rc = dalloc(h, &h->g, (size_t)c.intermediate * 4))) return rc;
-  if ((rc = dalloc(h, &h->u, (size_t)c.intermediate * 4))) return rc;
+  // tagged activations: 8 bytes per element, cleared so no tag matches a step
+  const size_t tagged_elems[9] = {(size_t)H, (size_t)H, (size_t)H, (size_t)c.heads * hd, (size_t)c.kv_heads * hd,
+                                  (size_t)c.kv_heads * hd, (size_t)c.heads * hd, (size_t)c.intermediate,
+                                  (size_t)c.intermediate};
+  float** tagged[9] = {&h->resA, &h->resB, &h->tmp, &h->q, &h->k, &h->v, &h->attn, &h->g, &h->u};
+  for (int i = 0; i < 9; i++) {
+    if ((rc = dalloc(h, tagged[i], tagged_elems[i] * 8))) return rc;
+    CKC(h, cudaMemset(*tagged[i], 0, tagged_elems[i] * 8));
+    h->tagged_bufs.push_back({*tagged[i], tagged_elems[i] * 8});
+  }
   if ((rc = dalloc(h, &h->part, (size_t)c.kv_heads * h->smax * G * (hd + 2) * 4))) return rc;
-  if ((rc = dalloc(h, &h->counters, (size_t)c.kv_heads * 4))) return rc;
-  CKC(h, cudaMemset(h->counters, 0, (size_t)c.kv_heads * 4));
+  if ((rc = dalloc(h, &h->counters, (size_t)c.layers * c.kv_heads * 4))) return rc;
+  CKC(h, cudaMemset(h->counters, 0, (size_t)c.layers * c.kv_heads * 4));
   if ((rc = dalloc(h, &h->inv_freq, (size_t)c.layers * (hd / 2) * 4))) return rc;
   for (int i = 0; i < c.layers; i++)
     k_inv_freq<<<1, 128>>>(h->inv_freq + (size_t)i * (hd / 2), c.layer_rope_theta[i], hd);
@@ -607,6 +677,7 @@ int ck_finalize(ck_engine* h) {
   if ((rc = dalloc(h, &h->kv, h->kv_bytes))) return rc;
   CKC(h, cudaMemset(h->kv, 0, h->kv_bytes));
 
+  if ((rc = epoch_restart(h))) return rc;
   h->Dlaunch = h->D;
   build_schedule(h, true, h->ph_logits);
   build_schedule(h, false, h->ph_prefill);

@@ -33,6 +33,7 @@ struct CkState {
   int pos;                  // position the next token is written to
   int err;                  // sticky CK_DERR_* bits
   uint32_t next_token;      // argmax / sampled id of the last logits step
+  uint32_t epoch;           // steps run since the tagged buffers were cleared (starts at 1)
   uint32_t draw;            // Philox draw index of the next sampled token
   int abort_flag;           // megakernel: a barrier gave up
   uint32_t bar;             // megakernel barrier arrivals (reset per launch)
@@ -47,7 +48,7 @@ struct CkState {
   int pen_count;            // explicit list length
   int sampling;             // needsSamplingReadback (sampling.ts:9-16)
   int chain;                // write next_token into tokens[pos+1]
-  int pad0;
+  int pad1;
   unsigned long long seed;  // Philox key
 };
 
@@ -84,6 +85,51 @@ __device__ __forceinline__ void stage_mark(unsigned long long* tp, int stage) {
   if (tp && threadIdx.x == 0) tp[stage] = (unsigned long long)clock64();
 }
 
+// ---------------------------------------------------------------------------
+// Tagged exchange between phases.  In the megakernel no grid barrier separates
+// most phases: every activation one phase hands to the next is stored as a
+// 64-bit word, value bits low and tag high, tag = epoch << 10 | producer phase
+// index, in one single-copy-atomic store.  A consumer reads exactly the words
+// it needs and re-reads any whose tag is not the one it expects.  Every
+// phase needs all (attention: its head's) outputs of the phase before it, so
+// no producer can overwrite a word another CTA has yet to read: a CTA with no
+// rows in a phase skips that phase's reads.  The epoch counts steps (the
+// step-end phase advances it), so words of the previous step never match.
+// A tag field of 0 in a descriptor means plain floats (standalone matvec).
+__device__ __forceinline__ uint32_t want_tag(uint32_t ep, int tag1) {
+  return tag1 ? ((ep << 10) | (uint32_t)(tag1 - 1)) : 0u;
+}
+__device__ __forceinline__ unsigned long long ld_word(const float* base, size_t i, int tag1) {
+  if (!tag1) return (unsigned long long)__float_as_uint(base[i]);
+  unsigned long long w;
+  asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(w) : "l"((const unsigned long long*)base + i) : "memory");
+  return w;
+}
+__device__ __forceinline__ void st_word(float* base, size_t i, float v, int tag1, uint32_t ep) {
+  if (!tag1) { base[i] = v; return; }
+  const unsigned long long w = ((unsigned long long)want_tag(ep, tag1) << 32) | __float_as_uint(v);
+  asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"((unsigned long long*)base + i), "l"(w) : "memory");
+}
+// The value of word w (element i), re-read until it carries `want`.  Bounded:
+// after ~2^22 reads it flags the step (the host reports a device timeout)
+// and returns what it has; it also stops once another CTA has given up.
+__device__ __forceinline__ float word_value(unsigned long long w, const float* base, size_t i, int tag1,
+                                            uint32_t want, int* err, int* abort_flag) {
+  if ((uint32_t)(w >> 32) != want) {
+    unsigned spins = 0;
+    do {
+      w = ld_word(base, i, tag1);
+      if (++spins > (1u << 22)) {
+        atomicOr(err, CK_DERR_BARRIER);
+        atomicExch(abort_flag, 1);
+        break;
+      }
+      if ((spins & 255u) == 0 && *(volatile int*)abort_flag) break;
+    } while ((uint32_t)(w >> 32) != want);
+  }
+  return __uint_as_float((uint32_t)w);
+}
+
 enum { PRO_COPY = 0, PRO_NORM = 1, PRO_SILU = 2, PRO_GELU = 3, PRO_GEMMA = 4 };
 enum { PH_EMBED = 0, PH_MATVEC = 1, PH_ATTN = 2, PH_ARGMAX1 = 3, PH_ARGMAX2 = 4, PH_SAMPLE = 5, PH_FINISH = 6,
        PH_SELECT = 7 };
@@ -97,6 +143,8 @@ struct Pro {
   const float* rin;         // GEMMA: residual in
   float* rout;              // GEMMA: residual out (written by CTA 0)
   float eps;
+  // tags (below) of a, b, rin as read and of rout as written; 0 = plain floats
+  int ta, tb, trin, trout;
 };
 
 struct MvSeg {
@@ -108,6 +156,7 @@ struct MvSeg {
   int per;                  // rows per CTA of the launch this descriptor is for
   int tile_rows;            // rows that fill an empty tile (CK_TILE_BYTES / row_bytes)
   uint32_t soff;            // byte offset of this segment's rows in a packed tile
+  int tout, tadd;           // tags of out as written and add as read (0 = plain)
 };
 
 enum { EPI_NONE = 0, EPI_SILU = 1, EPI_GELU = 2 };
@@ -119,6 +168,7 @@ struct MvPhase {
   int nseg;
   int packed;               // every CTA's rows of all segments fit one tile
   int epi;                  // EPI_SILU / EPI_GELU: segments 0, 1 are gate, up
+  int tglu;                 // tag of glu_out as written
   float* glu_out;           // with epi: act(gate) * up, the down projection's input
   MvSeg seg[3];
 };
@@ -130,9 +180,10 @@ struct AttnPhase {
   const float* inv_freq;    // [head_dim/2] theta^(-2d/head_dim) of this layer
   float* out;               // [heads * head_dim]
   float* part;              // split partials [kvh][smax][G][hd + 2]
-  unsigned* counter;        // [kvh] finished splits (last CTA merges, resets)
+  unsigned* counter;        // [kvh] finished splits of this layer (last CTA merges, resets)
   int heads, kvh, hd, ctx, window, interleaved, kv_f32, smax;
   int group;                // q heads per kv head (heads / kvh)
+  int tqkv, tout;           // tags of q/k/v as read and of out as written
   uint32_t theta;
   float eps, scale;
 };
@@ -143,12 +194,14 @@ struct EmbedPhase {
   float* out;
   float scale;
   int need_logits;
+  int tout;                 // tag of out as written
 };
 
 struct __align__(16) Phase {
   int kind;
   int grid;                 // CTAs for a standalone launch
   int index;                // position in its schedule (trace slots)
+  int barrier_after;        // megakernel: grid barrier before the next phase
   union {
     MvPhase mv;
     AttnPhase at;
@@ -258,7 +311,7 @@ __device__ __forceinline__ float gelu_tanh(float x) {
 //   GELU  GELU_TANH_MUL_WGSL (:3568-3599)
 //   GEMMA rmsNorm(post) -> ADD_CLAMP (:3510-3527) -> rmsNorm(pre), the gemma3
 //         sandwich of runToken (:1050-1064); CTA 0 stores the new residual.
-__device__ void build_x(const Pro& p, int k, SmemMv& s, int cta) {
+__device__ void build_x(const Pro& p, int k, SmemMv& s, int cta, uint32_t ep, int* err, int* abort_flag) {
   // Every global load of the prologue is issued in one round into registers
   // before anything is stored: interleaving them with the shared-memory
   // stores lets the compiler serialise each load behind the previous store.
@@ -267,15 +320,26 @@ __device__ void build_x(const Pro& p, int k, SmemMv& s, int cta) {
   const int kind = p.kind;
   float* xf = s.xf;
   float va[PER], vb[PER], vc[PER], vd[PER];
-  const float* pb = (kind == PRO_SILU || kind == PRO_GELU) ? p.b : p.w0;
+  const bool act = kind == PRO_SILU || kind == PRO_GELU;
+  const float* pb = act ? p.b : p.w0;
+  const int tb = act ? p.tb : 0, trin = kind == PRO_GEMMA ? p.trin : 0;
+  const uint32_t wa = want_tag(ep, p.ta), wb = want_tag(ep, tb), wr = want_tag(ep, trin);
+  unsigned long long xa[PER], xb[PER], xd[PER];
 #pragma unroll
   for (int j = 0; j < PER; j++) {
     const int i = tid + j * CK_THREADS;
     const bool ok = i < k;
-    va[j] = ok ? p.a[i] : 0.f;
-    vb[j] = (ok && kind != PRO_COPY) ? pb[i] : 0.f;
+    xa[j] = ok ? ld_word(p.a, i, p.ta) : ((unsigned long long)wa << 32);
+    xb[j] = (ok && kind != PRO_COPY) ? ld_word(pb, i, tb) : ((unsigned long long)wb << 32);
     vc[j] = (ok && kind == PRO_GEMMA) ? p.w1[i] : 0.f;
-    vd[j] = (ok && kind == PRO_GEMMA) ? p.rin[i] : 0.f;
+    xd[j] = (ok && kind == PRO_GEMMA) ? ld_word(p.rin, i, trin) : ((unsigned long long)wr << 32);
+  }
+#pragma unroll
+  for (int j = 0; j < PER; j++) {
+    const int i = tid + j * CK_THREADS;
+    va[j] = word_value(xa[j], p.a, i, p.ta, wa, err, abort_flag);
+    vb[j] = word_value(xb[j], pb, i, tb, wb, err, abort_flag);
+    vd[j] = word_value(xd[j], p.rin, i, trin, wr, err, abort_flag);
   }
   if (kind == PRO_COPY) {
 #pragma unroll
@@ -319,7 +383,7 @@ __device__ void build_x(const Pro& p, int k, SmemMv& s, int cta) {
       const float h = fminf(fmaxf(vd[j] + t, -65000.0f), 65000.0f);
       va[j] = h;
       if (i < k) {
-        if (cta == 0) p.rout[i] = h;
+        if (cta == 0) st_word(p.rout, i, h, p.trout, ep);
         ss2 += h * h;
       }
     }
@@ -396,7 +460,7 @@ __device__ __forceinline__ void load_xunit(const SmemMv& s, int c, XUnit& x) {
 // Dynamic shared memory: [tile buffer 0][tile buffer 1][3 mbarriers, 128 B][phase descriptors]
 #define CK_DYN_BARS (2 * CK_TILE_BYTES)
 #define CK_DYN_PHASES (2 * CK_TILE_BYTES + 128)
-#define CK_PHASE_SMEM_MAX (48 * 1024)
+#define CK_PHASE_SMEM_MAX (56 * 1024)   // 160 phases of 352 bytes (31 layers)
 #define CK_DYN_SMEM_MAX (CK_DYN_PHASES + CK_PHASE_SMEM_MAX)
 
 struct Cursor {
@@ -684,15 +748,24 @@ __device__ __forceinline__ void step_unpack(const MvPhase& P, const uint8_t* tb,
 
 // Store one output row: y = add + v, or, with a fused gate/up epilogue, the
 // CTA's staging row in shared memory.
-__device__ __forceinline__ void mv_store(const MvPhase& P, int sg, int orow, float v, SmemMv& s, int cta) {
+__device__ __forceinline__ void mv_store(const MvPhase& P, int sg, int orow, float v, SmemMv& s, int cta,
+                                         uint32_t ep, int* err, int* abort_flag) {
   const MvSeg& S = P.seg[sg];
-  if (P.epi) s.glu[sg][orow - cta * S.per] = v;
-  else S.out[orow] = S.add ? S.add[orow] + v : v;
+  if (P.epi) {
+    s.glu[sg][orow - cta * S.per] = v;
+  } else {
+    if (S.add) {
+      const uint32_t want = want_tag(ep, S.tadd);
+      v = word_value(ld_word(S.add, orow, S.tadd), S.add, orow, S.tadd, want, err, abort_flag) + v;
+    }
+    st_word(S.out, orow, v, S.tout, ep);
+  }
 }
 
 template <bool ONE>
 __device__ __forceinline__ void step_dot(const MvPhase& P, const TileList& T, int t, const MvStep<ONE>& w,
-                                         SmemMv& s, const XUnit& x0, float xscale, int cta) {
+                                         SmemMv& s, const XUnit& x0, float xscale, int cta, uint32_t ep, int* err,
+                                         int* abort_flag) {
   constexpr int R = MvStep<ONE>::R;
   const int lane = threadIdx.x & 31;
   const int U = P.seg[0].L.U;
@@ -722,7 +795,8 @@ __device__ __forceinline__ void step_dot(const MvPhase& P, const TileList& T, in
     for (int i = 0; i < R; i++) acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], o);
 #pragma unroll
   for (int i = 0; i < R; i++) {
-    if (lane == i && t + i * CK_WARPS < T.total) mv_store(P, w.sg[i], w.orow[i], xscale * acc[i], s, cta);
+    if (lane == i && t + i * CK_WARPS < T.total)
+      mv_store(P, w.sg[i], w.orow[i], xscale * acc[i], s, cta, ep, err, abort_flag);
   }
 }
 
@@ -731,13 +805,14 @@ __device__ __forceinline__ void step_dot(const MvPhase& P, const TileList& T, in
 // memory), which keeps a single unpacked unit live.
 template <bool ONE>
 __device__ __forceinline__ void mv_tile(const MvPhase& P, const uint8_t* tb, const TileList& T, int t0,
-                                        SmemMv& s, const XUnit& x0, float xscale, int cta) {
+                                        SmemMv& s, const XUnit& x0, float xscale, int cta, uint32_t ep, int* err,
+                                        int* abort_flag) {
   constexpr int R = MvStep<ONE>::R;
   if (ONE) {
     for (int t = t0; t < T.total; t += R * CK_WARPS) {
       MvStep<true> w;
       step_unpack<true>(P, tb, T, t, w);
-      step_dot<true>(P, T, t, w, s, x0, xscale, cta);
+      step_dot<true>(P, T, t, w, s, x0, xscale, cta, ep, err, abort_flag);
     }
     return;
   }
@@ -764,23 +839,34 @@ __device__ __forceinline__ void mv_tile(const MvPhase& P, const uint8_t* tb, con
       }
     }
     acc = warp_sum(acc);
-    if (lane == 0) mv_store(P, sg, pick3(pc, T.r00, T.r01, T.r02) + local, xscale * acc, s, cta);
+    if (lane == 0) mv_store(P, sg, pick3(pc, T.r00, T.r01, T.r02) + local, xscale * acc, s, cta, ep, err, abort_flag);
   }
 }
 
 // Prologue loads (fused path): element 32 g + lane of every group g of this
 // warp, issued before anything waits on them.
 template <int GPW>
-__device__ __forceinline__ void prologue_load(const Pro& p, int k, float (&va)[GPW], float (&vb)[GPW]) {
+__device__ __forceinline__ void prologue_load(const Pro& p, int k, float (&va)[GPW], float (&vb)[GPW], uint32_t ep,
+                                              int* err, int* abort_flag) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int U = k >> 5, kind = p.kind;
-  const float* pb = (kind == PRO_SILU || kind == PRO_GELU) ? p.b : p.w0;
+  const bool act = kind == PRO_SILU || kind == PRO_GELU;   // b is an activation, else a weight
+  const float* pb = act ? p.b : p.w0;
+  const int tb = act ? p.tb : 0;
+  const uint32_t wa = want_tag(ep, p.ta), wb = want_tag(ep, tb);
+  unsigned long long xa[GPW], xb[GPW];
 #pragma unroll
   for (int j = 0; j < GPW; j++) {
     const int g = warp + j * CK_WARPS;
     const int i = 32 * g + lane;
-    va[j] = g < U ? p.a[i] : 0.f;
-    vb[j] = (g < U && kind != PRO_COPY) ? pb[i] : 0.f;
+    xa[j] = g < U ? ld_word(p.a, i, p.ta) : ((unsigned long long)wa << 32);
+    xb[j] = (g < U && kind != PRO_COPY) ? ld_word(pb, i, tb) : ((unsigned long long)wb << 32);
+  }
+#pragma unroll
+  for (int j = 0; j < GPW; j++) {
+    const int i = 32 * (warp + j * CK_WARPS) + lane;
+    va[j] = word_value(xa[j], p.a, i, p.ta, wa, err, abort_flag);
+    vb[j] = word_value(xb[j], pb, i, tb, wb, err, abort_flag);
   }
 }
 
@@ -846,33 +932,36 @@ __device__ float prologue_quant(const Pro& p, int k, const float (&va)[GPW], con
 // GPW); ONE (k <= 1024) keeps the lane's x unit in registers.
 template <int GPW>
 __device__ __forceinline__ void mv_run_t(const MvPhase& P, SmemMv& s, Ring& R, int cta, int* err, int* abort_flag,
-                                         unsigned long long* tp) {
+                                         unsigned long long* tp, uint32_t ep) {
   constexpr bool ONE = GPW <= 2;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int seg = 0, row = -1;
+  TileList T;
+  // a CTA without rows in this phase reads nothing (its reads could race the
+  // next writer of the input, which does not wait for this CTA)
+  if (!next_tile(P, cta, seg, row, T)) return;
   stage_mark(tp, 0);
   float xscale = 1.0f;
   if (P.pro.kind == PRO_GEMMA) {
-    build_x(P.pro, P.k, s, cta);
+    build_x(P.pro, P.k, s, cta, ep, err, abort_flag);
     quant_x(P.k, s);
   } else {
     float va[GPW], vb[GPW];
-    prologue_load<GPW>(P.pro, P.k, va, vb);
+    prologue_load<GPW>(P.pro, P.k, va, vb, ep, err, abort_flag);
     xscale = prologue_quant<GPW>(P.pro, P.k, va, vb, s);
   }
   stage_mark(tp, 1);
   XUnit x0;
   if (ONE && lane < (P.k >> 5)) load_xunit(s, lane, x0);
-  int seg = 0, row = -1;
-  TileList T;
   bool first = true;
-  while (next_tile(P, cta, seg, row, T)) {
+  do {
     if (!ring_wait(R, err, abort_flag)) { R.ok = 0; return; }
     if (first) stage_mark(tp, 2);
-    mv_tile<ONE>(P, ring_buf(R.consumed), T, warp, s, x0, xscale, cta);
+    mv_tile<ONE>(P, ring_buf(R.consumed), T, warp, s, x0, xscale, cta, ep, err, abort_flag);
     if (first) stage_mark(tp, 3);
     first = false;
     ring_release(R, cta);
-  }
+  } while (next_tile(P, cta, seg, row, T));
   if (P.epi) {
     // fused SILU_MUL_WGSL (:3529-3547) / GELU_TANH_MUL_WGSL (:3568-3599) over
     // this CTA's rows (the release above synchronised the staging rows)
@@ -880,30 +969,31 @@ __device__ __forceinline__ void mv_run_t(const MvPhase& P, SmemMv& s, Ring& R, i
     seg_range(P.seg[0], cta, lo, hi);
     for (int i = threadIdx.x; i < hi - lo; i += CK_THREADS) {
       const float g = s.glu[0][i], u = s.glu[1][i];
-      P.glu_out[lo + i] = P.epi == EPI_SILU ? (g / (1.0f + expf(-g))) * u : gelu_tanh(g) * u;
+      st_word(P.glu_out, lo + i, P.epi == EPI_SILU ? (g / (1.0f + expf(-g))) * u : gelu_tanh(g) * u, P.tglu, ep);
     }
   }
   stage_mark(tp, 4);
 }
 
 __device__ __forceinline__ void mv_run(const MvPhase& P, SmemMv& s, Ring& R, int cta, int* err, int* abort_flag,
-                                       unsigned long long* tp) {
+                                       unsigned long long* tp, uint32_t ep) {
   const int U = P.k >> 5;
-  if (U <= 2 * CK_WARPS) mv_run_t<2>(P, s, R, cta, err, abort_flag, tp);
-  else if (U <= 4 * CK_WARPS) mv_run_t<4>(P, s, R, cta, err, abort_flag, tp);
-  else mv_run_t<CK_KMAX / 32 / CK_WARPS>(P, s, R, cta, err, abort_flag, tp);
+  if (U <= 2 * CK_WARPS) mv_run_t<2>(P, s, R, cta, err, abort_flag, tp, ep);
+  else if (U <= 4 * CK_WARPS) mv_run_t<4>(P, s, R, cta, err, abort_flag, tp, ep);
+  else mv_run_t<CK_KMAX / 32 / CK_WARPS>(P, s, R, cta, err, abort_flag, tp, ep);
 }
 
 __device__ __forceinline__ void phase_matvec(const MvPhase& P, Smem& sm, Ring& R, int cta, int* err,
-                                             int* abort_flag, unsigned long long* tp = nullptr) {
-  mv_run(P, sm.mv, R, cta, err, abort_flag, tp);
+                                             int* abort_flag, unsigned long long* tp, uint32_t ep) {
+  mv_run(P, sm.mv, R, cta, err, abort_flag, tp, ep);
 }
 
 // ---------------------------------------------------------------------------
 // Embedding (GGUF_*_EMBEDDING_WGSL, :2615-2866): row tokens[pos] of the
 // (tied) table dequantized in WGSL order, times EMBEDDING_SCALE.  Also marks
 // the repetition-penalty id set when this step computes logits.
-__device__ __forceinline__ void phase_embed(const EmbedPhase& P, const CkDev& D, int cta, int ncta, int pos) {
+__device__ __forceinline__ void phase_embed(const EmbedPhase& P, const CkDev& D, int cta, int ncta, int pos,
+                                            uint32_t ep) {
   const CkState* st = D.st;
   uint32_t token = D.tokens[pos];
   if (token >= (uint32_t)D.vocab) {
@@ -912,7 +1002,7 @@ __device__ __forceinline__ void phase_embed(const EmbedPhase& P, const CkDev& D,
   }
   const uint8_t* row = P.w + (size_t)token * P.L.row_bytes;
   for (int i = cta * CK_THREADS + threadIdx.x; i < P.L.k; i += ncta * CK_THREADS)
-    P.out[i] = __fmul_rn(dequant_at(row, P.L, i), P.scale);
+    st_word(P.out, i, __fmul_rn(dequant_at(row, P.L, i), P.scale), P.tout, ep);
   if (P.need_logits && st->pen_d != 1.0) {
     int cnt = st->pen_src == 0 ? pos + 1 : st->pen_count;
     const uint32_t* ids = st->pen_src == 0 ? D.tokens : D.pen_list;
@@ -1035,7 +1125,7 @@ __device__ __forceinline__ void softmax_pair(const float (&q)[E], const KvRow<E,
 // per head for the weights, then each output element's S accumulator values
 // split over P adjacent lanes, eight loads in flight per lane.
 template <int E>
-__device__ __forceinline__ void attn_merge(const AttnPhase& P, SmemAt& s, int kvh, int S) {
+__device__ __forceinline__ void attn_merge(const AttnPhase& P, SmemAt& s, int kvh, int S, uint32_t ep) {
   constexpr int hd = 32 * E;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int G = P.group, NE = G * hd;
@@ -1085,14 +1175,14 @@ __device__ __forceinline__ void attn_merge(const AttnPhase& P, SmemAt& s, int kv
       }
     }
     for (int o = 1; o < Pw; o <<= 1) A += __shfl_xor_sync(0xffffffffu, A, o);
-    if (ok && part == 0) P.out[(size_t)(kvh * G + gg) * hd + d] = A / sm_L[gg];
+    if (ok && part == 0) st_word(P.out, (size_t)(kvh * G + gg) * hd + d, A / sm_L[gg], P.tout, ep);
   }
   if (tid == 0) P.counter[kvh] = 0u;
 }
 
 template <int E, bool F32>
 __device__ __forceinline__ void attn_unit(const AttnPhase& P, SmemAt& s, int kvh, int split, int pos,
-                                          unsigned long long* tp) {
+                                          unsigned long long* tp, uint32_t ep, int* err, int* abort_flag) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   constexpr int hd = 32 * E;        // head_dim: one lane holds E elements of a row
   const int G = P.group;
@@ -1124,18 +1214,22 @@ __device__ __forceinline__ void attn_unit(const AttnPhase& P, SmemAt& s, int kvh
     }
   }
   float invf = 0.f, qv0 = 0.f, qv1 = 0.f, kk = 0.f, vv = 0.f, wq = 0.f, wk = 0.f;
-  const float* qsrc = P.q + (size_t)kvh * G * hd;
+  const uint32_t want = want_tag(ep, P.tqkv);
+  const unsigned long long none = (unsigned long long)want << 32;
+  const size_t q0 = (size_t)kvh * G * hd, kv0 = (size_t)kvh * hd;
+  const unsigned long long xq0 = tid < G * hd ? ld_word(P.q, q0 + tid, P.tqkv) : none;
+  const unsigned long long xq1 = tid + CK_THREADS < G * hd ? ld_word(P.q, q0 + tid + CK_THREADS, P.tqkv) : none;
+  const unsigned long long xk = (owner && tid < hd) ? ld_word(P.k, kv0 + tid, P.tqkv) : none;
+  const unsigned long long xv = (owner && tid < hd) ? ld_word(P.v, kv0 + tid, P.tqkv) : none;
   if (tid < (hd >> 1)) invf = P.inv_freq[tid];
-  if (tid < G * hd) qv0 = qsrc[tid];
-  if (tid + CK_THREADS < G * hd) qv1 = qsrc[tid + CK_THREADS];
   if (tid < hd) {
-    if (owner) {
-      kk = P.k[(size_t)kvh * hd + tid];
-      vv = P.v[(size_t)kvh * hd + tid];
-      if (P.kw) wk = P.kw[tid];
-    }
+    if (owner && P.kw) wk = P.kw[tid];
     if (P.qw) wq = P.qw[tid];
   }
+  qv0 = word_value(xq0, P.q, q0 + tid, P.tqkv, want, err, abort_flag);
+  qv1 = word_value(xq1, P.q, q0 + tid + CK_THREADS, P.tqkv, want, err, abort_flag);
+  kk = word_value(xk, P.k, kv0 + tid, P.tqkv, want, err, abort_flag);
+  vv = word_value(xv, P.v, kv0 + tid, P.tqkv, want, err, abort_flag);
   if (tid < (hd >> 1)) {
     // angle = pos * theta^(-2d/hd) (rope_angle, :2885-2888); the power is the
     // per-layer table built at load time with the same powf
@@ -1258,7 +1352,7 @@ __device__ __forceinline__ void attn_unit(const AttnPhase& P, SmemAt& s, int kvh
         L += s.wl[w] * f;
         A += s.wacc[w * CK_HDMAX + d] * f;
       }
-      P.out[(size_t)(kvh * G + gg) * hd + d] = A / L;
+      st_word(P.out, (size_t)(kvh * G + gg) * hd + d, A / L, P.tout, ep);
     }
     stage_mark(tp, 3);
     return;
@@ -1295,12 +1389,14 @@ __device__ __forceinline__ void attn_unit(const AttnPhase& P, SmemAt& s, int kvh
   __syncthreads();
   stage_mark(tp, 5);
   if (!s.last) return;
-  attn_merge<E>(P, s, kvh, S);
+  attn_merge<E>(P, s, kvh, S, ep);
   stage_mark(tp, 6);
 }
 
 __device__ __forceinline__ void phase_attn(const AttnPhase& P, Smem& sm, const CkDev& D, int cta, int ncta, int pos,
-                                           unsigned long long* tp = nullptr) {
+                                           unsigned long long* tp, uint32_t ep) {
+  int* err = &D.st->err;
+  int* ab = &D.st->abort_flag;
   // split-major: the active split 0 units of every kv head land on
   // different CTAs even when the context needs one split only
   int units = P.kvh * P.smax;
@@ -1308,13 +1404,13 @@ __device__ __forceinline__ void phase_attn(const AttnPhase& P, Smem& sm, const C
     int kvh = u % P.kvh, split = u / P.kvh;
     unsigned long long* up = (tp && u == cta) ? tp : nullptr;
     if (P.kv_f32) {
-      if (P.hd == 64) attn_unit<2, true>(P, sm.at, kvh, split, pos, up);
-      else if (P.hd == 128) attn_unit<4, true>(P, sm.at, kvh, split, pos, up);
-      else attn_unit<8, true>(P, sm.at, kvh, split, pos, up);
+      if (P.hd == 64) attn_unit<2, true>(P, sm.at, kvh, split, pos, up, ep, err, ab);
+      else if (P.hd == 128) attn_unit<4, true>(P, sm.at, kvh, split, pos, up, ep, err, ab);
+      else attn_unit<8, true>(P, sm.at, kvh, split, pos, up, ep, err, ab);
     } else {
-      if (P.hd == 64) attn_unit<2, false>(P, sm.at, kvh, split, pos, up);
-      else if (P.hd == 128) attn_unit<4, false>(P, sm.at, kvh, split, pos, up);
-      else attn_unit<8, false>(P, sm.at, kvh, split, pos, up);
+      if (P.hd == 64) attn_unit<2, false>(P, sm.at, kvh, split, pos, up, ep, err, ab);
+      else if (P.hd == 128) attn_unit<4, false>(P, sm.at, kvh, split, pos, up, ep, err, ab);
+      else attn_unit<8, false>(P, sm.at, kvh, split, pos, up, ep, err, ab);
     }
     __syncthreads();
   }
@@ -1491,7 +1587,7 @@ __device__ __forceinline__ void phase_sample(const CkDev& D, Smem& smu, int cta)
 }
 
 // End of step: clear the penalty set, chain the produced id, advance pos.
-__device__ __forceinline__ void phase_finish(int need_logits, const CkDev& D, int cta) {
+__device__ __forceinline__ void phase_finish(int need_logits, const CkDev& D, int cta, uint32_t ep) {
   if (cta != 0) return;
   CkState* st = D.st;
   int pos = st->pos;
@@ -1510,36 +1606,37 @@ __device__ __forceinline__ void phase_finish(int need_logits, const CkDev& D, in
       if (st->sampling) st->draw += 1;
     }
     st->pos = pos + 1;
+    st->epoch = ep + 1;       // tags of the next step differ from this step's
   }
 }
 
 // argmax stage 2 -> sampling -> end of step, on CTA 0 in one phase.
-__device__ __forceinline__ void phase_select(int need_logits, const CkDev& D, Smem& sm, int cta) {
+__device__ __forceinline__ void phase_select(int need_logits, const CkDev& D, Smem& sm, int cta, uint32_t ep) {
   if (cta != 0) return;
   phase_argmax2(D, sm, 0);
   __syncthreads();
   phase_sample(D, sm, 0);
   __syncthreads();
-  phase_finish(need_logits, D, 0);
+  phase_finish(need_logits, D, 0, ep);
 }
 
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void run_phase(const Phase* ph, int i, Smem& sm, Ring& R, const CkDev& D, int cta,
-                                          int ncta, int pos) {
+                                          int ncta, int pos, uint32_t ep) {
   const Phase& p = ph[i];
   unsigned long long* tp =
       !D.trace ? nullptr
       : (i == 2 && cta < 1024) ? D.trace + CK_TRACE_CTA_BASE + cta * 16 + 8
       : (cta == 0 && i < 512) ? D.trace + CK_TRACE_STAGE_BASE + i * 8 : nullptr;
   switch (p.kind) {
-    case PH_EMBED: phase_embed(p.em, D, cta, ncta, pos); break;
-    case PH_MATVEC: phase_matvec(p.mv, sm, R, cta, &D.st->err, &D.st->abort_flag, tp); break;
-    case PH_ATTN: phase_attn(p.at, sm, D, cta, ncta, pos, tp); break;
+    case PH_EMBED: phase_embed(p.em, D, cta, ncta, pos, ep); break;
+    case PH_MATVEC: phase_matvec(p.mv, sm, R, cta, &D.st->err, &D.st->abort_flag, tp, ep); break;
+    case PH_ATTN: phase_attn(p.at, sm, D, cta, ncta, pos, tp, ep); break;
     case PH_ARGMAX1: phase_argmax1(D, sm, cta, ncta); break;
     case PH_ARGMAX2: phase_argmax2(D, sm, cta); break;
     case PH_SAMPLE: phase_sample(D, sm, cta); break;
-    case PH_FINISH: phase_finish(p.need_logits, D, cta); break;
-    case PH_SELECT: phase_select(p.need_logits, D, sm, cta); break;
+    case PH_FINISH: phase_finish(p.need_logits, D, cta, ep); break;
+    case PH_SELECT: phase_select(p.need_logits, D, sm, cta, ep); break;
   }
 }
 
@@ -1558,23 +1655,26 @@ __global__ void __launch_bounds__(CK_THREADS, 1) k_mv(const Phase* __restrict__ 
   if (tr) tr[1] = gtimer();
   unsigned long long* tp = (D.trace && blockIdx.x == 0 && sph->index < 512)
                                ? D.trace + CK_TRACE_STAGE_BASE + sph->index * 8 : nullptr;
-  phase_matvec(sph->mv, sm, R, blockIdx.x, &D.st->err, &D.st->abort_flag, tp);
+  phase_matvec(sph->mv, sm, R, blockIdx.x, &D.st->err, &D.st->abort_flag, tp, D.st->epoch);
   if (tr) tr[2] = gtimer();
 }
 __global__ void __launch_bounds__(CK_THREADS, 1) k_attn(const Phase* __restrict__ ph, CkDev D) {
   __shared__ Smem sm;
-  phase_attn(ph->at, sm, D, blockIdx.x, gridDim.x, D.st->pos);
+  phase_attn(ph->at, sm, D, blockIdx.x, gridDim.x, D.st->pos, nullptr, D.st->epoch);
 }
 __global__ void __launch_bounds__(CK_THREADS, 1) k_misc(const Phase* __restrict__ ph, CkDev D) {
   __shared__ Smem sm;
   const Phase& p = *ph;
+  // every CTA reads the epoch before CTA 0's step end can advance it: the
+  // step-end phases run on a one-CTA grid
+  const uint32_t ep = D.st->epoch;
   switch (p.kind) {
-    case PH_EMBED: phase_embed(p.em, D, blockIdx.x, gridDim.x, D.st->pos); break;
+    case PH_EMBED: phase_embed(p.em, D, blockIdx.x, gridDim.x, D.st->pos, ep); break;
     case PH_ARGMAX1: phase_argmax1(D, sm, blockIdx.x, gridDim.x); break;
     case PH_ARGMAX2: phase_argmax2(D, sm, blockIdx.x); break;
     case PH_SAMPLE: phase_sample(D, sm, blockIdx.x); break;
-    case PH_FINISH: phase_finish(p.need_logits, D, blockIdx.x); break;
-    case PH_SELECT: phase_select(p.need_logits, D, sm, blockIdx.x); break;
+    case PH_FINISH: phase_finish(p.need_logits, D, blockIdx.x, ep); break;
+    case PH_SELECT: phase_select(p.need_logits, D, sm, blockIdx.x, ep); break;
   }
 }
 
@@ -1611,10 +1711,15 @@ __device__ __forceinline__ bool grid_sync(CkState* st, unsigned target) {
   return s_ok != 0;
 }
 
-// Whole step in one cooperative launch (megakernel mode).
+// Whole step in one cooperative launch (megakernel mode).  Phases hand data
+// over as tagged words, so a CTA moves to its next phase as soon as its own
+// work is done; a grid barrier remains only where a phase is marked
+// barrier_after (the LM head before argmax stage 1, stage 1 before select),
+// whose outputs are plain.
 __global__ void __launch_bounds__(CK_THREADS, 1) k_mega(const Phase* __restrict__ ph, int nph, CkDev D) {
   __shared__ Smem sm;
-  const int pos = D.st->pos;   // constant for the whole step (phase_finish runs last)
+  const int pos = D.st->pos;         // constant for the whole step (phase_finish runs last)
+  const uint32_t ep = D.st->epoch;   // read before any CTA can reach the step end
   Ring R;
   const Phase* sph = launch_start(R, ph, nph, blockIdx.x, &D.st->err, &D.st->abort_flag);
   if (!sph) return;
@@ -1626,11 +1731,11 @@ __global__ void __launch_bounds__(CK_THREADS, 1) k_mega(const Phase* __restrict_
 #pragma unroll 1
   for (int i = 0; i < nph; i++) {
     if (tr && 2 * i + 1 < CK_TRACE_MV_BASE) D.trace[2 * i] = gtimer();
-    run_phase(sph, i, sm, R, D, blockIdx.x, gridDim.x, pos);
+    run_phase(sph, i, sm, R, D, blockIdx.x, gridDim.x, pos, ep);
     if (tr && 2 * i + 1 < CK_TRACE_MV_BASE) D.trace[2 * i + 1] = gtimer();
     if (ct && i >= 1 && i <= 4) ct[i - 1] = gtimer();
     if (!R.ok) return;
-    if (i + 1 < nph) {
+    if (i + 1 < nph && sph[i].barrier_after) {
       target += gridDim.x;
       if (!grid_sync(D.st, target)) return;
     }
