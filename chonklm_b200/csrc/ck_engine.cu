@@ -68,7 +68,6 @@ struct ck_engine {
   float *resA = nullptr, *resB = nullptr, *tmp = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *attn = nullptr,
         *g = nullptr, *u = nullptr;
   float* part = nullptr;
-  unsigned* counters = nullptr;   // [layers][kv_heads] finished attention splits
   uint32_t epoch_steps = 1;       // mirror of CkState::epoch
   std::vector<std::pair<void*, size_t>> tagged_bufs;
   float* inv_freq = nullptr;  // [layers][head_dim/2] RoPE inverse frequencies
@@ -332,7 +331,6 @@ void build_schedule(ck_engine* h, bool logits, std::vector<Phase>& out) {
     a.at.vc = h->kv + (size_t)(2 * i + 1) * per;
     a.at.out = h->attn;
     a.at.part = h->part;
-    a.at.counter = h->counters + (size_t)i * c.kv_heads;
     a.at.heads = c.heads; a.at.kvh = c.kv_heads; a.at.hd = hd; a.at.ctx = c.context_length;
     a.at.group = c.heads / c.kv_heads;
     a.at.window = (int)c.layer_window[i];
@@ -420,14 +418,13 @@ int capture(ck_engine* h, bool logits, int mode, cudaGraphExec_t* out) {
   return CK_OK;
 }
 
-// Clear every tagged buffer and the attention counters and restart the
+// Clear every tagged buffer and restart the
 // device step counter at 1, so no stored tag can match a later step: at
 // set-up, after a step gave up part-way, and before the 22-bit step field
 // of the tags would wrap.
 int epoch_restart(ck_engine* h) {
   CKC(h, cudaStreamSynchronize(h->stream));
   for (auto& b : h->tagged_bufs) CKC(h, cudaMemset(b.first, 0, b.second));
-  CKC(h, cudaMemset(h->counters, 0, (size_t)h->cfg.layers * h->cfg.kv_heads * 4));
   const uint32_t one = 1;
   CKC(h, cudaMemcpy(&h->st->epoch, &one, 4, cudaMemcpyHostToDevice));
   h->epoch_steps = 1;
@@ -638,7 +635,9 @@ int ck_finalize(ck_engine* h) {
   int rc;
   const int H = c.hidden, hd = c.head_dim;
   int G = c.heads / c.kv_heads;
-  h->smax = (2 * h->sms + c.kv_heads - 1) / c.kv_heads;
+  // at most one attention unit per CTA: a CTA that ran two units in turn
+  // would finish last and hold up the merge
+  h->smax = h->sms / c.kv_heads;
   if (h->smax > 64) h->smax = 64;
   if (h->smax < 1) h->smax = 1;
   if ((rc = dalloc(h, &h->st, sizeof(CkState)))) return rc;
@@ -666,9 +665,11 @@ int ck_finalize(ck_engine* h) {
     CKC(h, cudaMemset(*tagged[i], 0, tagged_elems[i] * 8));
     h->tagged_bufs.push_back({*tagged[i], tagged_elems[i] * 8});
   }
-  if ((rc = dalloc(h, &h->part, (size_t)c.kv_heads * h->smax * G * (hd + 2) * 4))) return rc;
-  if ((rc = dalloc(h, &h->counters, (size_t)c.layers * c.kv_heads * 4))) return rc;
-  CKC(h, cudaMemset(h->counters, 0, (size_t)c.layers * c.kv_heads * 4));
+  // attention split partials, tagged words
+  const size_t part_bytes = (size_t)c.kv_heads * h->smax * G * (hd + 2) * 8;
+  if ((rc = dalloc(h, &h->part, part_bytes))) return rc;
+  CKC(h, cudaMemset(h->part, 0, part_bytes));
+  h->tagged_bufs.push_back({h->part, part_bytes});
   if ((rc = dalloc(h, &h->inv_freq, (size_t)c.layers * (hd / 2) * 4))) return rc;
   for (int i = 0; i < c.layers; i++)
     k_inv_freq<<<1, 128>>>(h->inv_freq + (size_t)i * (hd / 2), c.layer_rope_theta[i], hd);

@@ -130,6 +130,33 @@ __device__ __forceinline__ float word_value(unsigned long long w, const float* b
   return __uint_as_float((uint32_t)w);
 }
 
+// Bring a batch of words up to date: every round re-reads all words whose
+// tag is not yet want[j], with the reads of the round in flight together, so
+// the batch costs one round trip after its last producer's store lands
+// (polling the words one after another would cost one each).  reread(j)
+// issues the read of word j.  Bounded like word_value.
+template <int N, typename Reread>
+__device__ __forceinline__ void settle(unsigned long long (&w)[N], const uint32_t (&want)[N], Reread reread,
+                                       int* err, int* abort_flag) {
+  unsigned spins = 0;
+  for (;;) {
+    bool stale = false;
+#pragma unroll
+    for (int j = 0; j < N; j++) stale |= (uint32_t)(w[j] >> 32) != want[j];
+    if (!stale) return;
+    if (++spins > (1u << 22)) {
+      atomicOr(err, CK_DERR_BARRIER);
+      atomicExch(abort_flag, 1);
+      return;
+    }
+    if ((spins & 255u) == 0 && *(volatile int*)abort_flag) return;
+#pragma unroll
+    for (int j = 0; j < N; j++)
+      if ((uint32_t)(w[j] >> 32) != want[j]) w[j] = reread(j);
+  }
+}
+__device__ __forceinline__ float word_float(unsigned long long w) { return __uint_as_float((uint32_t)w); }
+
 enum { PRO_COPY = 0, PRO_NORM = 1, PRO_SILU = 2, PRO_GELU = 3, PRO_GEMMA = 4 };
 enum { PH_EMBED = 0, PH_MATVEC = 1, PH_ATTN = 2, PH_ARGMAX1 = 3, PH_ARGMAX2 = 4, PH_SAMPLE = 5, PH_FINISH = 6,
        PH_SELECT = 7 };
@@ -179,8 +206,7 @@ struct AttnPhase {
   void *kc, *vc;            // this layer's cache [kv_head][ctx][head_dim]
   const float* inv_freq;    // [head_dim/2] theta^(-2d/head_dim) of this layer
   float* out;               // [heads * head_dim]
-  float* part;              // split partials [kvh][smax][G][hd + 2]
-  unsigned* counter;        // [kvh] finished splits of this layer (last CTA merges, resets)
+  float* part;              // split partials [kvh][smax][G][hd + 2], tagged words
   int heads, kvh, hd, ctx, window, interleaved, kv_f32, smax;
   int group;                // q heads per kv head (heads / kvh)
   int tqkv, tout;           // tags of q/k/v as read and of out as written
@@ -250,9 +276,10 @@ struct SmemAt {
   float kst[CK_HDMAX];             // the new k row after norm + rope
   float wm[CK_WARPS];
   float wl[CK_WARPS];
+  float wf[CK_WARPS];              // each warp's weight exp(m_w - M) in its head's merge
+  float hm[CK_GMAX], hl[CK_GMAX];  // per head: merged max and sum of this split
   float2 cs[CK_HDMAX / 2];
   float inv[CK_GMAX + 1];
-  int last;
 };
 struct SmemSm {
   double val[CK_SAMPLE_MAX];
@@ -324,22 +351,29 @@ __device__ void build_x(const Pro& p, int k, SmemMv& s, int cta, uint32_t ep, in
   const float* pb = act ? p.b : p.w0;
   const int tb = act ? p.tb : 0, trin = kind == PRO_GEMMA ? p.trin : 0;
   const uint32_t wa = want_tag(ep, p.ta), wb = want_tag(ep, tb), wr = want_tag(ep, trin);
-  unsigned long long xa[PER], xb[PER], xd[PER];
+  unsigned long long x[3 * PER];        // a, b, rin words
+  uint32_t want[3 * PER];
 #pragma unroll
   for (int j = 0; j < PER; j++) {
     const int i = tid + j * CK_THREADS;
     const bool ok = i < k;
-    xa[j] = ok ? ld_word(p.a, i, p.ta) : ((unsigned long long)wa << 32);
-    xb[j] = (ok && kind != PRO_COPY) ? ld_word(pb, i, tb) : ((unsigned long long)wb << 32);
+    x[j] = ok ? ld_word(p.a, i, p.ta) : ((unsigned long long)wa << 32);
+    x[PER + j] = (ok && kind != PRO_COPY) ? ld_word(pb, i, tb) : ((unsigned long long)wb << 32);
     vc[j] = (ok && kind == PRO_GEMMA) ? p.w1[i] : 0.f;
-    xd[j] = (ok && kind == PRO_GEMMA) ? ld_word(p.rin, i, trin) : ((unsigned long long)wr << 32);
+    x[2 * PER + j] = (ok && kind == PRO_GEMMA) ? ld_word(p.rin, i, trin) : ((unsigned long long)wr << 32);
+    want[j] = wa;
+    want[PER + j] = wb;
+    want[2 * PER + j] = wr;
   }
+  settle(x, want, [&](int j) {
+    const int i = tid + (j % PER) * CK_THREADS;
+    return j < PER ? ld_word(p.a, i, p.ta) : j < 2 * PER ? ld_word(pb, i, tb) : ld_word(p.rin, i, trin);
+  }, err, abort_flag);
 #pragma unroll
   for (int j = 0; j < PER; j++) {
-    const int i = tid + j * CK_THREADS;
-    va[j] = word_value(xa[j], p.a, i, p.ta, wa, err, abort_flag);
-    vb[j] = word_value(xb[j], pb, i, tb, wb, err, abort_flag);
-    vd[j] = word_value(xd[j], p.rin, i, trin, wr, err, abort_flag);
+    va[j] = word_float(x[j]);
+    vb[j] = word_float(x[PER + j]);
+    vd[j] = word_float(x[2 * PER + j]);
   }
   if (kind == PRO_COPY) {
 #pragma unroll
@@ -854,19 +888,25 @@ __device__ __forceinline__ void prologue_load(const Pro& p, int k, float (&va)[G
   const float* pb = act ? p.b : p.w0;
   const int tb = act ? p.tb : 0;
   const uint32_t wa = want_tag(ep, p.ta), wb = want_tag(ep, tb);
-  unsigned long long xa[GPW], xb[GPW];
+  unsigned long long x[2 * GPW];       // a words, then b words
+  uint32_t want[2 * GPW];
 #pragma unroll
   for (int j = 0; j < GPW; j++) {
     const int g = warp + j * CK_WARPS;
     const int i = 32 * g + lane;
-    xa[j] = g < U ? ld_word(p.a, i, p.ta) : ((unsigned long long)wa << 32);
-    xb[j] = (g < U && kind != PRO_COPY) ? ld_word(pb, i, tb) : ((unsigned long long)wb << 32);
+    x[j] = g < U ? ld_word(p.a, i, p.ta) : ((unsigned long long)wa << 32);
+    x[GPW + j] = (g < U && kind != PRO_COPY) ? ld_word(pb, i, tb) : ((unsigned long long)wb << 32);
+    want[j] = wa;
+    want[GPW + j] = wb;
   }
+  settle(x, want, [&](int j) {
+    const int i = 32 * (warp + (j % GPW) * CK_WARPS) + lane;
+    return j < GPW ? ld_word(p.a, i, p.ta) : ld_word(pb, i, tb);
+  }, err, abort_flag);
 #pragma unroll
   for (int j = 0; j < GPW; j++) {
-    const int i = 32 * (warp + j * CK_WARPS) + lane;
-    va[j] = word_value(xa[j], p.a, i, p.ta, wa, err, abort_flag);
-    vb[j] = word_value(xb[j], pb, i, tb, wb, err, abort_flag);
+    va[j] = word_float(x[j]);
+    vb[j] = word_float(x[GPW + j]);
   }
 }
 
@@ -1097,6 +1137,20 @@ __device__ __forceinline__ float kv_round(float x) {
   return F32 ? x : __half2float(__float2half_rn(x));
 }
 
+// Cache rows of positions t and t + wpg (zero rows past tend).
+template <int E, bool F32>
+__device__ __forceinline__ void kv_load_pair(const AttnPhase& P, size_t kvbase, int t, int tend, int wpg,
+                                             KvRow<E, F32>& k0, KvRow<E, F32>& v0, KvRow<E, F32>& k1,
+                                             KvRow<E, F32>& v1) {
+  constexpr int hd = 32 * E;
+  kv_zero(k0); kv_zero(v0); kv_zero(k1); kv_zero(v1);
+  if (t < tend) { kv_load(P.kc, kvbase + (size_t)t * hd, k0); kv_load(P.vc, kvbase + (size_t)t * hd, v0); }
+  if (t + wpg < tend) {
+    kv_load(P.kc, kvbase + (size_t)(t + wpg) * hd, k1);
+    kv_load(P.vc, kvbase + (size_t)(t + wpg) * hd, v1);
+  }
+}
+
 // One online-softmax step over two positions of a warp (the second may be
 // absent: score -inf and a zero row add nothing).
 template <int E, bool F32>
@@ -1125,18 +1179,40 @@ __device__ __forceinline__ void softmax_pair(const float (&q)[E], const KvRow<E,
 // per head for the weights, then each output element's S accumulator values
 // split over P adjacent lanes, eight loads in flight per lane.
 template <int E>
-__device__ __forceinline__ void attn_merge(const AttnPhase& P, SmemAt& s, int kvh, int S, uint32_t ep) {
+__device__ __forceinline__ void attn_merge(const AttnPhase& P, SmemAt& s, int kvh, int S, uint32_t ep, int* err,
+                                           int* abort_flag) {
   constexpr int hd = 32 * E;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int G = P.group, NE = G * hd;
-  const float* pk = P.part + (size_t)kvh * P.smax * G * (hd + 2);
+  const float* pk = P.part + (size_t)kvh * P.smax * G * (hd + 2) * 2;   // tagged words: 2 floats each
+  const uint32_t want = want_tag(ep, P.tout);
+  const unsigned long long none = (unsigned long long)want << 32;
   float* sm_m = s.wacc;                 // [S * G] split maxima, then weights
   float* sm_l = s.wacc + 1024;          // [S * G] split sums
   float* sm_L = s.wacc + 2048;          // [G] merged sums
-  for (int i = tid; i < S * G; i += CK_THREADS) {
-    const float* pp = pk + (size_t)i * (hd + 2);     // i = split * G + head
-    sm_m[i] = __ldcg(pp);
-    sm_l[i] = __ldcg(pp + 1);
+  int Pw = 1;                                        // lanes per element (power of two)
+  while (Pw < 32 && 2 * Pw * NE <= CK_THREADS) Pw *= 2;
+  const int part = tid & (Pw - 1), slots = CK_THREADS / Pw;
+  const int passes = (NE + slots - 1) / slots;
+  // the first eight accumulators of this lane's first element are requested
+  // together with the split maxima and sums (one round trip, not two)
+  unsigned long long x[8];
+  {
+    const int e = tid / Pw;
+    const int gg = e < NE ? e / hd : 0, d = e % hd;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      const int sp = part + j * Pw;
+      x[j] = (e < NE && sp < S) ? ld_word(pk, ((size_t)sp * G + gg) * (hd + 2) + 2 + d, P.tout) : none;
+    }
+  }
+  for (int i = tid; i < S * G; i += CK_THREADS) {   // one pass: S * G <= 64 * 8
+    const size_t o = (size_t)i * (hd + 2);          // i = split * G + head
+    unsigned long long ml[2] = {ld_word(pk, o, P.tout), ld_word(pk, o + 1, P.tout)};
+    const uint32_t w2[2] = {want, want};
+    settle(ml, w2, [&](int j) { return ld_word(pk, o + j, P.tout); }, err, abort_flag);
+    sm_m[i] = word_float(ml[0]);
+    sm_l[i] = word_float(ml[1]);
   }
   __syncthreads();
   for (int gg = warp; gg < G; gg += CK_WARPS) {
@@ -1153,31 +1229,32 @@ __device__ __forceinline__ void attn_merge(const AttnPhase& P, SmemAt& s, int kv
     if (lane == 0) sm_L[gg] = L;
   }
   __syncthreads();
-  int Pw = 1;                                        // lanes per element (power of two)
-  while (Pw < 32 && 2 * Pw * NE <= CK_THREADS) Pw *= 2;
-  const int part = tid & (Pw - 1);
-  for (int e = tid / Pw; e < (CK_THREADS / Pw) * ((NE + CK_THREADS / Pw - 1) / (CK_THREADS / Pw));
-       e += CK_THREADS / Pw) {
+  for (int ps = 0; ps < passes; ps++) {
+    const int e = tid / Pw + ps * slots;
     const bool ok = e < NE;
     const int gg = ok ? e / hd : 0, d = e % hd;
     float A = 0.f;
     for (int sp0 = part; sp0 < S; sp0 += 8 * Pw) {
-      float v[8];
+      if (ps > 0 || sp0 != part) {
 #pragma unroll
-      for (int j = 0; j < 8; j++) {
-        const int sp = sp0 + j * Pw;
-        v[j] = (ok && sp < S) ? __ldcg(pk + ((size_t)sp * G + gg) * (hd + 2) + 2 + d) : 0.f;
+        for (int j = 0; j < 8; j++) {
+          const int sp = sp0 + j * Pw;
+          x[j] = (ok && sp < S) ? ld_word(pk, ((size_t)sp * G + gg) * (hd + 2) + 2 + d, P.tout) : none;
+        }
       }
+      const uint32_t w8[8] = {want, want, want, want, want, want, want, want};
+      settle(x, w8, [&](int j) {
+        return ld_word(pk, ((size_t)(sp0 + j * Pw) * G + gg) * (hd + 2) + 2 + d, P.tout);
+      }, err, abort_flag);
 #pragma unroll
       for (int j = 0; j < 8; j++) {
         const int sp = sp0 + j * Pw;
-        if (ok && sp < S) A += v[j] * sm_m[sp * G + gg];
+        if (ok && sp < S) A += word_float(x[j]) * sm_m[sp * G + gg];
       }
     }
     for (int o = 1; o < Pw; o <<= 1) A += __shfl_xor_sync(0xffffffffu, A, o);
     if (ok && part == 0) st_word(P.out, (size_t)(kvh * G + gg) * hd + d, A / sm_L[gg], P.tout, ep);
   }
-  if (tid == 0) P.counter[kvh] = 0u;
 }
 
 template <int E, bool F32>
@@ -1204,32 +1281,41 @@ __device__ __forceinline__ void attn_unit(const AttnPhase& P, SmemAt& s, int kvh
   stage_mark(tp, 0);
   const size_t kvbase = (size_t)kvh * P.ctx * hd + lane * E;
   int t = t0 + sub;
-  KvRow<E, F32> ka, va, kb, vb;      // the warp's first two positions
+  // KV rows are in flight two position pairs ahead of the math (one pair
+  // ahead for 256-wide rows, none for 256-wide fp32 rows: register budget);
+  // the first pairs load under the q/k/v wait and the QK-norm / RoPE below
+  constexpr int DEPTH = (E <= 4 && !(F32 && E == 4)) ? 2 : (F32 && E == 8) ? 0 : 1;
+  KvRow<E, F32> ka, va, kb, vb, kc, vc, kd, vd;
   kv_zero(ka); kv_zero(va); kv_zero(kb); kv_zero(vb);
+  kv_zero(kc); kv_zero(vc); kv_zero(kd); kv_zero(vd);
   if (g < G) {
-    if (t < tend) { kv_load(P.kc, kvbase + (size_t)t * hd, ka); kv_load(P.vc, kvbase + (size_t)t * hd, va); }
-    if (t + wpg < tend) {
-      kv_load(P.kc, kvbase + (size_t)(t + wpg) * hd, kb);
-      kv_load(P.vc, kvbase + (size_t)(t + wpg) * hd, vb);
-    }
+    kv_load_pair<E, F32>(P, kvbase, t, tend, wpg, ka, va, kb, vb);
+    if (DEPTH == 2) kv_load_pair<E, F32>(P, kvbase, t + 2 * wpg, tend, wpg, kc, vc, kd, vd);
   }
   float invf = 0.f, qv0 = 0.f, qv1 = 0.f, kk = 0.f, vv = 0.f, wq = 0.f, wk = 0.f;
   const uint32_t want = want_tag(ep, P.tqkv);
   const unsigned long long none = (unsigned long long)want << 32;
   const size_t q0 = (size_t)kvh * G * hd, kv0 = (size_t)kvh * hd;
-  const unsigned long long xq0 = tid < G * hd ? ld_word(P.q, q0 + tid, P.tqkv) : none;
-  const unsigned long long xq1 = tid + CK_THREADS < G * hd ? ld_word(P.q, q0 + tid + CK_THREADS, P.tqkv) : none;
-  const unsigned long long xk = (owner && tid < hd) ? ld_word(P.k, kv0 + tid, P.tqkv) : none;
-  const unsigned long long xv = (owner && tid < hd) ? ld_word(P.v, kv0 + tid, P.tqkv) : none;
+  unsigned long long xw[4];   // q (two), k, v
+  xw[0] = tid < G * hd ? ld_word(P.q, q0 + tid, P.tqkv) : none;
+  xw[1] = tid + CK_THREADS < G * hd ? ld_word(P.q, q0 + tid + CK_THREADS, P.tqkv) : none;
+  xw[2] = (owner && tid < hd) ? ld_word(P.k, kv0 + tid, P.tqkv) : none;
+  xw[3] = (owner && tid < hd) ? ld_word(P.v, kv0 + tid, P.tqkv) : none;
   if (tid < (hd >> 1)) invf = P.inv_freq[tid];
   if (tid < hd) {
     if (owner && P.kw) wk = P.kw[tid];
     if (P.qw) wq = P.qw[tid];
   }
-  qv0 = word_value(xq0, P.q, q0 + tid, P.tqkv, want, err, abort_flag);
-  qv1 = word_value(xq1, P.q, q0 + tid + CK_THREADS, P.tqkv, want, err, abort_flag);
-  kk = word_value(xk, P.k, kv0 + tid, P.tqkv, want, err, abort_flag);
-  vv = word_value(xv, P.v, kv0 + tid, P.tqkv, want, err, abort_flag);
+  const uint32_t wants[4] = {want, want, want, want};
+  settle(xw, wants, [&](int j) {
+    return j == 0 ? ld_word(P.q, q0 + tid, P.tqkv)
+         : j == 1 ? ld_word(P.q, q0 + tid + CK_THREADS, P.tqkv)
+         : j == 2 ? ld_word(P.k, kv0 + tid, P.tqkv) : ld_word(P.v, kv0 + tid, P.tqkv);
+  }, err, abort_flag);
+  qv0 = word_float(xw[0]);
+  qv1 = word_float(xw[1]);
+  kk = word_float(xw[2]);
+  vv = word_float(xw[3]);
   if (tid < (hd >> 1)) {
     // angle = pos * theta^(-2d/hd) (rope_angle, :2885-2888); the power is the
     // per-layer table built at load time with the same powf
@@ -1290,31 +1376,19 @@ __device__ __forceinline__ void attn_unit(const AttnPhase& P, SmemAt& s, int kvh
     acc[e] = 0.f;
   }
   if (g < G) {
-    // two positions per step, the next two loads in flight during the step
-    // (except for 256-wide fp32 rows, whose second pair would not fit the
-    // register budget: those load after the step)
-    constexpr bool PIPE = !(F32 && E == 8);
+    // two positions per step
     for (; t < tend; t += 2 * wpg) {
-      const int tn = t + 2 * wpg;
       KvRow<E, F32> nka, nva, nkb, nvb;
-      if (PIPE) {
-        kv_zero(nka); kv_zero(nva); kv_zero(nkb); kv_zero(nvb);
-        if (tn < tend) { kv_load(P.kc, kvbase + (size_t)tn * hd, nka); kv_load(P.vc, kvbase + (size_t)tn * hd, nva); }
-        if (tn + wpg < tend) {
-          kv_load(P.kc, kvbase + (size_t)(tn + wpg) * hd, nkb);
-          kv_load(P.vc, kvbase + (size_t)(tn + wpg) * hd, nvb);
-        }
-      }
+      if (DEPTH == 2) kv_load_pair<E, F32>(P, kvbase, t + 4 * wpg, tend, wpg, nka, nva, nkb, nvb);
+      if (DEPTH == 1) kv_load_pair<E, F32>(P, kvbase, t + 2 * wpg, tend, wpg, nka, nva, nkb, nvb);
       softmax_pair<E, F32>(q, ka, va, kb, vb, t + wpg < tend, P.scale, m, l, acc);
-      if (PIPE) {
+      if (DEPTH == 2) {
+        ka = kc; va = vc; kb = kd; vb = vd;
+        kc = nka; vc = nva; kd = nkb; vd = nvb;
+      } else if (DEPTH == 1) {
         ka = nka; va = nva; kb = nkb; vb = nvb;
       } else {
-        kv_zero(ka); kv_zero(va); kv_zero(kb); kv_zero(vb);
-        if (tn < tend) { kv_load(P.kc, kvbase + (size_t)tn * hd, ka); kv_load(P.vc, kvbase + (size_t)tn * hd, va); }
-        if (tn + wpg < tend) {
-          kv_load(P.kc, kvbase + (size_t)(tn + wpg) * hd, kb);
-          kv_load(P.vc, kvbase + (size_t)(tn + wpg) * hd, vb);
-        }
+        kv_load_pair<E, F32>(P, kvbase, t + 2 * wpg, tend, wpg, ka, va, kb, vb);
       }
     }
     if (owner && sub == 0) {   // position pos, as the cache now holds it
@@ -1339,58 +1413,77 @@ __device__ __forceinline__ void attn_unit(const AttnPhase& P, SmemAt& s, int kvh
 #pragma unroll
   for (int e = 0; e < E; e++) s.wacc[warp * CK_HDMAX + lane * E + e] = acc[e];
   __syncthreads();
+  // per head: M = max over its warps, each warp's weight exp(m_w - M), L
+  if (tid < G) {
+    float M = -INFINITY;
+    for (int w = tid * wpg; w < tid * wpg + wpg; w++) M = fmaxf(M, s.wm[w]);
+    float L = 0.f;
+    for (int w = tid * wpg; w < tid * wpg + wpg; w++) {
+      const float f = s.wm[w] == -INFINITY ? 0.f : expf(s.wm[w] - M);
+      s.wf[w] = f;
+      L += s.wl[w] * f;
+    }
+    s.hm[tid] = M;
+    s.hl[tid] = L;
+  }
+  __syncthreads();
   if (S == 1) {   // one split covers the context: no partials, no merge
     for (int i = tid; i < G * hd; i += CK_THREADS) {
-      int gg = i / hd, d = i % hd;
-      float M = -INFINITY;
-      for (int w = gg * wpg; w < gg * wpg + wpg; w++) M = fmaxf(M, s.wm[w]);
-      float L = 0.f, A = 0.f;
-      for (int w = gg * wpg; w < gg * wpg + wpg; w++) {
-        float wm = s.wm[w];
-        if (wm == -INFINITY) continue;
-        float f = expf(wm - M);
-        L += s.wl[w] * f;
-        A += s.wacc[w * CK_HDMAX + d] * f;
-      }
-      st_word(P.out, (size_t)(kvh * G + gg) * hd + d, A / L, P.tout, ep);
+      const int gg = i / hd, d = i % hd;
+      float A = 0.f;
+      for (int w = gg * wpg; w < gg * wpg + wpg; w++) A += s.wacc[w * CK_HDMAX + d] * s.wf[w];
+      st_word(P.out, (size_t)(kvh * G + gg) * hd + d, A / s.hl[gg], P.tout, ep);
     }
     stage_mark(tp, 3);
     return;
   }
-  float* part = P.part + ((size_t)kvh * P.smax + split) * G * (hd + 2);
+  // partials (m, l, acc) of this split as tagged words
+  float* part = P.part + ((size_t)kvh * P.smax + split) * G * (hd + 2) * 2;
   for (int i = tid; i < G * hd; i += CK_THREADS) {
-    int gg = i / hd, d = i % hd;
-    float M = -INFINITY;
-    for (int w = gg * wpg; w < gg * wpg + wpg; w++) M = fmaxf(M, s.wm[w]);
-    float L = 0.f, A = 0.f;
-    for (int w = gg * wpg; w < gg * wpg + wpg; w++) {
-      float wm = s.wm[w];
-      if (wm == -INFINITY) continue;
-      float f = expf(wm - M);
-      L += s.wl[w] * f;
-      A += s.wacc[w * CK_HDMAX + d] * f;
-    }
-    part[gg * (hd + 2) + 2 + d] = A;
+    const int gg = i / hd, d = i % hd;
+    float A = 0.f;
+    for (int w = gg * wpg; w < gg * wpg + wpg; w++) A += s.wacc[w * CK_HDMAX + d] * s.wf[w];
+    st_word(part, gg * (hd + 2) + 2 + d, A, P.tout, ep);
     if (d == 0) {
-      part[gg * (hd + 2)] = M;
-      part[gg * (hd + 2) + 1] = L;
+      st_word(part, gg * (hd + 2), s.hm[gg], P.tout, ep);
+      st_word(part, gg * (hd + 2) + 1, s.hl[gg], P.tout, ep);
     }
   }
   stage_mark(tp, 4);
-  // --- last split to finish merges all splits --------------------------------
-  // (acq_rel: this CTA's partials are published before the count; the last
-  // CTA's read of the count orders its reads of the other partials after it)
+  // --- the split holding pos merges all splits of this kv head ---------------
+  if (!owner) return;
   __syncthreads();
-  if (tid == 0) {
-    unsigned prev;
-    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(P.counter + kvh) : "memory");
-    s.last = (prev == (unsigned)(S - 1));
-  }
-  __syncthreads();
-  stage_mark(tp, 5);
-  if (!s.last) return;
-  attn_merge<E>(P, s, kvh, S, ep);
+  attn_merge<E>(P, s, kvh, S, ep, err, abort_flag);
   stage_mark(tp, 6);
+}
+
+// Bulk prefetch into L2 (no shared memory): addr and bytes multiples of 16.
+__device__ __forceinline__ void prefetch_l2(const void* addr, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(addr), "r"(bytes) : "memory");
+}
+
+// Issued one phase early (at the start of the layer's QKV phase): this CTA's
+// attention unit's cache rows [t0, tend) of K and V move into L2 while the
+// projections run, so the unit's first reads do not go to HBM.
+__device__ __forceinline__ void attn_prefetch(const AttnPhase& P, int cta, int ncta, int pos) {
+  if (threadIdx.x != 0) return;
+  const int start = (P.window != 0 && pos + 1 > P.window) ? pos + 1 - P.window : 0;
+  const int npos = pos - start + 1;
+  int chunk = (npos + P.smax - 1) / P.smax;
+  if (chunk < CK_MIN_SPLIT) chunk = CK_MIN_SPLIT;
+  const int S = (npos + chunk - 1) / chunk;
+  const size_t elem = P.kv_f32 ? 4 : 2;
+  for (int u = cta; u < P.kvh * P.smax; u += ncta) {
+    const int kvh = u % P.kvh, split = u / P.kvh;
+    if (split >= S) continue;
+    const int t0 = start + split * chunk;
+    const int tend = split == S - 1 ? pos : min(t0 + chunk, pos + 1);
+    if (tend <= t0) continue;
+    const size_t off = ((size_t)kvh * P.ctx + t0) * P.hd * elem;
+    const uint32_t bytes = (uint32_t)((size_t)(tend - t0) * P.hd * elem);
+    prefetch_l2((const uint8_t*)P.kc + off, bytes);
+    prefetch_l2((const uint8_t*)P.vc + off, bytes);
+  }
 }
 
 __device__ __forceinline__ void phase_attn(const AttnPhase& P, Smem& sm, const CkDev& D, int cta, int ncta, int pos,
@@ -1628,6 +1721,7 @@ __device__ __forceinline__ void run_phase(const Phase* ph, int i, Smem& sm, Ring
       !D.trace ? nullptr
       : (i == 2 && cta < 1024) ? D.trace + CK_TRACE_CTA_BASE + cta * 16 + 8
       : (cta == 0 && i < 512) ? D.trace + CK_TRACE_STAGE_BASE + i * 8 : nullptr;
+  if (p.kind == PH_MATVEC && ph[i + 1].kind == PH_ATTN) attn_prefetch(ph[i + 1].at, cta, ncta, pos);
   switch (p.kind) {
     case PH_EMBED: phase_embed(p.em, D, cta, ncta, pos, ep); break;
     case PH_MATVEC: phase_matvec(p.mv, sm, R, cta, &D.st->err, &D.st->abort_flag, tp, ep); break;
