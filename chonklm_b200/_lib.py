@@ -9,7 +9,7 @@ from __future__ import annotations
 import ctypes
 import os
 import threading
-from typing import Optional, Sequence, Tuple
+from typing import List, Optional, Sequence, Tuple
 
 import numpy as np
 
@@ -107,6 +107,14 @@ def lib():
             L.ck_matvec_noalloc.argtypes = [I, P, S, I, I, P, P, P]
             L.ck_trace.argtypes = [P, I]
             L.ck_trace_read.argtypes = [P, P, S]
+            L.ck_batch_create.argtypes = [P, I, I, pp(P)]
+            L.ck_batch_add_seq.argtypes = [P, pp(U), I, I, pp(U), I, pp(I)]
+            L.ck_batch_step.argtypes = [P, pp(I)]
+            L.ck_batch_collect.argtypes = [P, I, pp(U), I, pp(I), pp(I)]
+            L.ck_batch_stats.argtypes = [P, pp(ctypes.c_uint64), pp(ctypes.c_uint64), pp(ctypes.c_uint64)]
+            L.ck_batch_last_error.argtypes = [P]
+            L.ck_batch_last_error.restype = ctypes.c_char_p
+            L.ck_batch_destroy.argtypes = [P]
             _lib = L
     return _lib
 
@@ -245,6 +253,63 @@ class Engine:
         if getattr(self, "h", None):
             self._L.ck_destroy(self.h)
             self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def _check_batch(rc: int, b) -> None:
+    if rc == CK_OK:
+        return
+    msg = (lib().ck_batch_last_error(b) or b"").decode("utf-8", "replace")
+    raise CkError(rc, msg)
+
+
+class Batch:
+    """Batched decode over an Engine's weights (ck_batch_*): sequences are
+    added, stepped together one position per step, and collected."""
+
+    def __init__(self, engine: "Engine", max_seqs: int, kv_blocks: int = 0):
+        self._L = lib()
+        self.engine = engine   # keeps the weights alive
+        b = ctypes.c_void_p()
+        _check(self._L.ck_batch_create(engine.h, int(max_seqs), int(kv_blocks), ctypes.byref(b)), engine.h)
+        self.b = b
+
+    def add(self, prompt: Sequence[int], max_new: int, eos_ids: Sequence[int] = ()) -> int:
+        arr = np.ascontiguousarray(np.asarray(prompt, dtype=np.uint32))
+        eos = np.ascontiguousarray(np.asarray(list(eos_ids) or [0], dtype=np.uint32))
+        sid = ctypes.c_int(0)
+        _check_batch(self._L.ck_batch_add_seq(self.b, _u32p(arr), int(arr.size), int(max_new), _u32p(eos),
+                                              len(eos_ids), ctypes.byref(sid)), self.b)
+        return sid.value
+
+    def step(self) -> int:
+        n = ctypes.c_int(0)
+        _check_batch(self._L.ck_batch_step(self.b, ctypes.byref(n)), self.b)
+        return n.value
+
+    def collect(self, seq_id: int, cap: int = 1 << 16) -> Tuple[List[int], bool]:
+        """Ids so far and whether the sequence finished (a finished result is
+        released by this call)."""
+        out = np.zeros(max(cap, 1), dtype=np.uint32)
+        n, done = ctypes.c_int(0), ctypes.c_int(0)
+        _check_batch(self._L.ck_batch_collect(self.b, int(seq_id), _u32p(out), out.size, ctypes.byref(n),
+                                              ctypes.byref(done)), self.b)
+        return out[:min(n.value, out.size)].tolist(), bool(done.value)
+
+    def stats(self) -> Tuple[int, int, int]:
+        a, b, c = ctypes.c_uint64(0), ctypes.c_uint64(0), ctypes.c_uint64(0)
+        _check_batch(self._L.ck_batch_stats(self.b, ctypes.byref(a), ctypes.byref(b), ctypes.byref(c)), self.b)
+        return a.value, b.value, c.value
+
+    def close(self) -> None:
+        if getattr(self, "b", None):
+            self._L.ck_batch_destroy(self.b)
+            self.b = None
 
     def __del__(self):
         try:

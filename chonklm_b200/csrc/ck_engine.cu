@@ -1214,3 +1214,5 @@ extern "C" int ck_matvec_noalloc(int ggml_type, const void* w_dev, size_t nbytes
   return CK_OK;
 }
 
+// Batched decode: kernels and scheduler over this engine's weights.
+#include "ck_batch.cuh"

@@ -31,7 +31,8 @@ extern "C" {
 #define CK_ESTATE -3      /* call not valid in the engine's current state       */
 #define CK_ECONTEXT -4    /* context exhausted (llama-wgsl-runtime.ts:1030-1033) */
 #define CK_EDEVICE -5     /* device-side check failed (bad token id, timeout)   */
-#define CK_ENOMEM -6      /* device allocation failed                           */
+#define CK_ENOMEM -6      /* device allocation failed / KV pool exhausted        */
+#define CK_EBUSY -7       /* batch: every sequence slot is in use               */
 
 /* GGML tensor types accepted for weights (gguf.ts:5-14). */
 #define CK_GGML_F32 0
@@ -172,6 +173,36 @@ int ck_bench_matvec(int ggml_type, const void* bytes, size_t nbytes, int k, int 
  * overlap on the GPU race. */
 int ck_matvec_noalloc(int ggml_type, const void* w_dev, size_t nbytes, int k, int n, const float* x_dev,
                       float* y_dev, void* stream);
+
+/* ---- batched decode (continuous batching) ----
+ * No counterpart in the reference, whose engine decodes one sequence
+ * (llama-wgsl-runtime.ts:619-1150): several sequences share one engine's
+ * weights and advance together, one position per step each (a sequence
+ * still in its prompt feeds its next prompt token, the others their last
+ * generated id), so every sequence gets exactly the ids generateLlamaWgsl
+ * (:242-314) would give it with greedy decoding.  Sequences may be added
+ * between steps; a finished sequence frees its slot and KV blocks at once.
+ * llama / qwen3 architectures; paged fp16 KV cache (16-position blocks).
+ * Not thread-safe per batch; the engine must not run single-sequence steps
+ * while a batch step is in flight. */
+typedef struct ck_batch ck_batch;
+/* max_seqs concurrent sequences; kv_blocks 16-position blocks of KV pool
+ * (0 = enough for every slot at the full context length). */
+int ck_batch_create(ck_engine* h, int max_seqs, int kv_blocks, ck_batch** out);
+/* Queue a sequence: prompt of n >= 1 ids, up to max_new >= 1 generated ids
+ * (capped at the context left, as generateLlamaWgsl does), stopping after
+ * an id in eos_ids (which is kept).  CK_EBUSY when every slot is taken,
+ * CK_ENOMEM when the KV pool cannot hold it. */
+int ck_batch_add_seq(ck_batch* b, const uint32_t* prompt, int n, int max_new, const uint32_t* eos_ids, int n_eos,
+                     int* seq_id);
+/* One step of every queued sequence; *n_active = sequences still running. */
+int ck_batch_step(ck_batch* b, int* n_active);
+/* Ids generated so far (done = 0) or the final ids of a finished sequence
+ * (done = 1; the result is released).  Copies min(n, cap) ids. */
+int ck_batch_collect(ck_batch* b, int seq_id, uint32_t* out_ids, int cap, int* n_out, int* done);
+int ck_batch_stats(ck_batch* b, uint64_t* steps, uint64_t* tokens_fed, uint64_t* tokens_generated);
+const char* ck_batch_last_error(ck_batch* b);
+int ck_batch_destroy(ck_batch* b);
 
 /* sizeof(ck_model_cfg) and sizeof(ck_sampling) as compiled, so bindings can
  * check their struct mirrors; needs no GPU. */
