@@ -107,6 +107,7 @@ def lib():
             L.ck_matvec_noalloc.argtypes = [I, P, S, I, I, P, P, P]
             L.ck_trace.argtypes = [P, I]
             L.ck_trace_read.argtypes = [P, P, S]
+            L.ck_matmul.argtypes = [I, P, S, I, I, P, I, P, I]
             L.ck_batch_create.argtypes = [P, I, I, pp(P)]
             L.ck_batch_add_seq.argtypes = [P, pp(U), I, I, pp(U), I, pp(I)]
             L.ck_batch_step.argtypes = [P, pp(I)]
@@ -330,6 +331,16 @@ def matvec(ggml_type: int, data: bytes, k: int, n: int, x: np.ndarray, device: i
     xx = np.ascontiguousarray(x, dtype=np.float32)
     y = np.empty(n, dtype=np.float32)
     _check(lib().ck_matvec(ggml_type, buf.ctypes.data, buf.nbytes, k, n, xx.ctypes.data, y.ctypes.data, device))
+    return y
+
+
+def matmul(ggml_type: int, data: bytes, k: int, n: int, x: np.ndarray, device: int = 0) -> np.ndarray:
+    """Y = X W^T for T rows of x (the batched path's tensor-core GEMM)."""
+    buf = np.ascontiguousarray(np.frombuffer(data, dtype=np.uint8))
+    xx = np.ascontiguousarray(np.asarray(x, dtype=np.float32))
+    T = xx.shape[0]
+    y = np.empty((T, n), dtype=np.float32)
+    _check(lib().ck_matmul(ggml_type, buf.ctypes.data, buf.nbytes, k, n, xx.ctypes.data, T, y.ctypes.data, device))
     return y
 
 

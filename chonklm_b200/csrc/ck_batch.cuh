@@ -35,11 +35,9 @@ struct BStep {
   int max_blocks;
 };
 
-struct BXq {             // per-token quantized x (layout of the single-sequence prologue)
-  int8_t* xh;            // [max_seqs][k]
-  int8_t* xl;
-  float* sx;             // [max_seqs][k/32]
-  int* s16;              // [max_seqs][k/16]
+struct BXh {             // per-token matmul input x = hi + lo (two fp16 parts)
+  __half* hi;            // [max_seqs][k]
+  __half* lo;
   float* xs;             // [max_seqs] output scale (RMS of NORM, else 1)
 };
 
@@ -95,169 +93,243 @@ __global__ void __launch_bounds__(256) k_bembed(const uint8_t* w, Lay L, float s
   for (int i = threadIdx.x; i < H; i += blockDim.x) x[(size_t)t * H + i] = __fmul_rn(dequant_at(row, L, i), scale);
 }
 
-// Per-token prologue + quantization (one CTA per active entry): the forms of
-// build_quant prologue kinds COPY / NORM / SILU of the single-sequence path,
-// with every global load of the CTA issued before any math.
-__global__ void __launch_bounds__(CK_THREADS) k_bprep(BPrep p, BStep st, BXq q) {
-  constexpr int GPW = CK_KMAX / 32 / CK_WARPS;
+// Per-token prologue (one CTA per active entry): the COPY / NORM / SILU forms
+// of the single-sequence prologue, x written as two fp16 parts for the
+// tensor-core GEMM.  NORM's RMS scale is applied to the matmul output, as in
+// the single-sequence path.
+__global__ void __launch_bounds__(CK_THREADS) k_bprep(BPrep p, BStep st, BXh q) {
+  constexpr int PER = CK_KMAX / CK_THREADS;
   const int t = blockIdx.x;
   if (t >= *st.nact) return;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int k = p.k, U = k >> 5;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int k = p.k;
   const float* a = p.a + (size_t)t * p.lda;
   const float* b = p.kind == BP_SILU ? p.b + (size_t)t * p.lda : p.w;
   __shared__ float red[CK_WARPS];
-  float va[GPW], vb[GPW];
+  float va[PER], vb[PER];
 #pragma unroll
-  for (int j = 0; j < GPW; j++) {
-    const int g = warp + j * CK_WARPS, i = 32 * g + lane;
-    va[j] = g < U ? a[i] : 0.f;
-    vb[j] = (g < U && p.kind != BP_COPY) ? b[i] : 0.f;
+  for (int j = 0; j < PER; j++) {
+    const int i = tid + j * CK_THREADS;
+    va[j] = i < k ? a[i] : 0.f;
+    vb[j] = (i < k && p.kind != BP_COPY) ? b[i] : 0.f;
   }
   float ss = 0.f;
 #pragma unroll
-  for (int j = 0; j < GPW; j++) {
-    const int g = warp + j * CK_WARPS;
+  for (int j = 0; j < PER; j++) {
+    const int i = tid + j * CK_THREADS;
     float v = va[j];
     if (p.kind == BP_NORM) { ss += va[j] * va[j]; v = va[j] * vb[j]; }
     else if (p.kind == BP_SILU) v = (va[j] / (1.0f + expf(-va[j]))) * vb[j];
-    const float amax = warp_max(fabsf(v));
-    const bool fin = amax <= 3.0e38f;
-    const float step = amax * (1.0f / 32639.0f);
-    const float inv = (step > 0.f && fin) ? 32639.0f / amax : 0.f;
-    const int X = max(-32639, min(32639, __float2int_rn(v * inv)));
-    const int h = (X + 128) >> 8;
-    int sum = X;
-#pragma unroll
-    for (int o = 8; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-    if (g < U) {
-      q.xh[(size_t)t * k + 32 * g + lane] = (int8_t)h;
-      q.xl[(size_t)t * k + 32 * g + lane] = (int8_t)(X - 256 * h);
-      if (lane == 0) q.sx[(size_t)t * U + g] = fin ? step : __int_as_float(0x7fc00000);
-      if ((lane & 15) == 0) q.s16[(size_t)t * 2 * U + 2 * g + (lane >> 4)] = sum;
+    if (i < k) {
+      const __half h = __float2half_rn(v);
+      q.hi[(size_t)t * k + i] = h;
+      q.lo[(size_t)t * k + i] = __float2half_rn(v - __half2float(h));
     }
   }
   if (p.kind == BP_NORM) {
     ss = warp_sum(ss);
     if (lane == 0) red[warp] = ss;
     __syncthreads();
-    if (threadIdx.x == 0) {
+    if (tid == 0) {
       float tot = 0.f;
       for (int w = 0; w < CK_WARPS; w++) tot += red[w];
       q.xs[t] = rms_inv(tot, k, p.eps);
     }
-  } else if (threadIdx.x == 0) {
+  } else if (tid == 0) {
     q.xs[t] = 1.0f;
   }
 }
 
-// Sum over the 32 lanes of each of N per-lane values, scattered: lane l ends
-// with the total of value (l % N).  N = 32 takes 31 shuffles.
-template <int N>
-__device__ __forceinline__ float reduce_scatter(float (&v)[N]) {
-  const int lane = threadIdx.x & 31;
-#pragma unroll
-  for (int n = N; n > 1; n >>= 1) {
-    const int o = n >> 1;
-    const bool upper = (lane & o) != 0;
-#pragma unroll
-    for (int i = 0; i < o; i++) {
-      const float send = upper ? v[i] : v[i + o];
-      const float keep = upper ? v[i + o] : v[i];
-      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+// ---------------------------------------------------------------------------
+// Tensor-core GEMM (tcgen05) for the batched matmuls.
+//
+// D[128 weight rows x N tokens] accumulates in tensor memory (fp32) over the
+// K dimension in chunks of 64: for each chunk every thread dequantizes one
+// 32-weight unit of one row to fp32, splits it into two fp16 values
+// (hi = fp16(w), lo = fp16(w - hi)) and stores both into shared memory in
+// the K-major canonical layout (8-row x 16-byte core matrices: the two 16-byte
+// K halves of a 16-wide step 128 bytes apart, 8-row groups 256 bytes apart);
+// x arrives already split the same way from the prologue kernel.  One thread
+// issues three MMAs per 16-wide step (w_hi x_hi + w_hi x_lo + w_lo x_hi), so
+// the products carry ~22 significant bits (fp16 alone would give ~4e-4
+// relative error per dot), and commits them to the stage's mbarrier; the next
+// chunk is dequantized into the other stage meanwhile.  At the end the
+// accumulator is read back (tcgen05.ld, 32 rows per warp quarter) and the
+// epilogue scales by the token's prologue scale and adds the residual.
+#define TC_ROWS 128
+#define TC_NT 128            // tokens per CTA tile (columns of the accumulator)
+#define TC_KC 64             // K per stage
+#define TC_THREADS 256
+#define TC_A_BYTES (TC_ROWS * TC_KC * 2)    // one fp16 weight tile (16 KB)
+#define TC_B_BYTES (TC_NT * TC_KC * 2)      // one fp16 token tile (16 KB)
+#define TC_STAGE (2 * TC_A_BYTES + 2 * TC_B_BYTES)
+#define TC_SMEM (2 * TC_STAGE + 64)
+
+__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+         ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);   // version 1, no swizzle
+}
+// byte offset of (row, k) in a K-major tile of `rows` rows and TC_KC columns
+__device__ __forceinline__ uint32_t kmaj_off(int row, int k, int rows) {
+  return (uint32_t)((k >> 4) * rows * 32 + (row >> 3) * 256 + ((k >> 3) & 1) * 128 + (row & 7) * 16 + (k & 7) * 2);
+}
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* err) {
+  unsigned spins = 0;
+  while (!mbar_try_wait(bar, parity)) {
+    if (++spins > (1u << 22)) {
+      atomicOr(err, CK_DERR_BARRIER);
+      return false;
     }
   }
-  float r = v[0];
-#pragma unroll
-  for (int o = N; o < 32; o <<= 1) r += __shfl_xor_sync(0xffffffffu, r, o);
-  return r;
+  return true;
 }
 
-__host__ __device__ inline int bgemm_tt(int k) { return k <= 1536 ? 32 : 16; }
-__host__ __device__ inline size_t bgemm_smem(int k) {
-  return (size_t)bgemm_tt(k) * (2 * (size_t)k + 4 * (size_t)(k / 32) + 4 * (size_t)(k / 16));
-}
-
-// Y = W X over the step's tokens for up to three weight matrices sharing x.
-// CTA = 16 rows of one segment (a warp per row) x one tile of TT tokens
-// (blockIdx.y): the tile's quantized x is staged in shared memory and every
-// warp dots its row's units, unpacked once, with each token of the tile.
-template <int TT>
-__global__ void __launch_bounds__(CK_THREADS, 1) k_bgemm(BGemm G, BStep st, BXq q) {
-  extern __shared__ __align__(16) uint8_t bsm[];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+__global__ void __launch_bounds__(TC_THREADS, 1) k_bgemm_tc(BGemm G, BStep st, BXh xh, int* err) {
+  extern __shared__ __align__(1024) uint8_t tsm[];
+  __shared__ uint32_t s_tmem;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int T = *st.nact;
+  const int t0 = blockIdx.y * TC_NT;
+  if (t0 >= T) return;                          // before any TMEM is held
+  const int nt = min(TC_NT, T - t0);
+  const int N = (nt + 15) & ~15;                // MMA N: a multiple of 16
   int si = 0;
   while (si + 1 < G.nseg && (int)blockIdx.x >= G.tile0[si + 1]) si++;
   const BSeg& S = G.seg[si];
-  const int row = ((int)blockIdx.x - G.tile0[si]) * CK_WARPS + warp;
-  const bool has = row < S.n;
-  const int k = G.k, U = k >> 5, upl = (U + 31) >> 5;
-  U8 u[3];
-  if (has) {
-    const uint8_t* wrow = S.w + (size_t)row * S.L.row_bytes;
+  const int r0 = ((int)blockIdx.x - G.tile0[si]) * TC_ROWS;
+  const int k = G.k, U = k >> 5, nchunk = (k + TC_KC - 1) / TC_KC;
+  uint64_t* bars = (uint64_t*)(tsm + 2 * TC_STAGE);
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
+                 "r"(TC_NT));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  if (tid == 0) {
+    mbar_init(bars, 1);
+    mbar_init(bars + 1, 1);
+    mbar_fence_init();
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;");
+  const uint32_t tmem = s_tmem;
+  // instruction descriptor: fp32 D, fp16 A and B, both K-major, M = 128, N
+  const uint32_t idesc = (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(TC_ROWS >> 4) << 24);
+  bool ok = true;
+  for (int c = 0; c < nchunk && ok; c++) {
+    const int stg = c & 1;
+    uint8_t* base = tsm + stg * TC_STAGE;
+    uint8_t* a_hi = base;
+    uint8_t* a_lo = base + TC_A_BYTES;
+    uint8_t* b_hi = base + 2 * TC_A_BYTES;
+    uint8_t* b_lo = b_hi + TC_B_BYTES;
+    if (c >= 2) ok = mbar_wait_bounded(bars + stg, ((c >> 1) - 1) & 1, err);   // MMAs of chunk c-2 done
+    if (!ok) break;
+    // weights: thread -> (row, unit) of this chunk
+    {
+      const int row = tid >> 1, uu = tid & 1;
+      const int unit = c * 2 + uu;
+      const int grow = r0 + row;
+      float w[32];
+      if (grow < S.n && unit < U) {
+        U8 u;
+        unpack_unit<true>(S.L.type, S.w + (size_t)grow * S.L.row_bytes, S.L, unit, u);
 #pragma unroll
-    for (int j = 0; j < 3; j++) {
-      const int c = lane + 32 * j;
-      if (j < upl && c < U) unpack_unit<true>(S.L.type, wrow, S.L, c, u[j]);
+        for (int i = 0; i < 32; i++) {
+          // byte codes are signed (Q8_0 stores int8; the other types' codes are < 64)
+          const int code = (int)(int8_t)((u.q[i >> 2] >> (8 * (i & 3))) & 0xFF);
+          w[i] = (i < 16 ? u.a0 : u.a1) * (float)(code + u.ko) + u.b;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; i++) w[i] = 0.f;
+      }
+#pragma unroll
+      for (int cc = 0; cc < 4; cc++) {      // 8 weights = one 16-byte row of a core matrix
+        __align__(16) __half hv[8], lv[8];
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+          const float x = w[8 * cc + e];
+          hv[e] = __float2half_rn(x);
+          lv[e] = __float2half_rn(x - __half2float(hv[e]));
+        }
+        const uint32_t off = kmaj_off(row, 32 * uu + 8 * cc, TC_ROWS);
+        *(int4*)(a_hi + off) = *(const int4*)hv;
+        *(int4*)(a_lo + off) = *(const int4*)lv;
+      }
+    }
+    // tokens: 16-byte pieces of x_hi / x_lo
+    for (int i = tid; i < TC_NT * (TC_KC / 8); i += TC_THREADS) {
+      const int n = i >> 3, piece = i & 7;
+      const int kk = c * TC_KC + 8 * piece;
+      int4 vh = make_int4(0, 0, 0, 0), vl = make_int4(0, 0, 0, 0);
+      if (n < nt && kk < k) {
+        vh = *(const int4*)(xh.hi + (size_t)(t0 + n) * k + kk);
+        vl = *(const int4*)(xh.lo + (size_t)(t0 + n) * k + kk);
+      }
+      const uint32_t off = kmaj_off(n, 8 * piece, TC_NT);
+      *(int4*)(b_hi + off) = vh;
+      *(int4*)(b_lo + off) = vl;
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // generic-proxy stores -> tensor core
+    __syncthreads();
+    if (tid == 0) {
+      asm volatile("tcgen05.fence::after_thread_sync;");
+#pragma unroll
+      for (int kk = 0; kk < TC_KC / 16; kk++) {
+        const uint64_t da_hi = umma_desc(smem_u32(a_hi) + kk * TC_ROWS * 32, 128, 256);
+        const uint64_t da_lo = umma_desc(smem_u32(a_lo) + kk * TC_ROWS * 32, 128, 256);
+        const uint64_t db_hi = umma_desc(smem_u32(b_hi) + kk * TC_NT * 32, 128, 256);
+        const uint64_t db_lo = umma_desc(smem_u32(b_lo) + kk * TC_NT * 32, 128, 256);
+        const uint32_t acc0 = (c > 0 || kk > 0) ? 1u : 0u;
+        asm volatile("{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+                     " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n"
+                     ::"r"(tmem), "l"(da_hi), "l"(db_hi), "r"(idesc), "r"(acc0));
+        asm volatile("{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+                     " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n"
+                     ::"r"(tmem), "l"(da_hi), "l"(db_lo), "r"(idesc), "r"(1u));
+        asm volatile("{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+                     " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n"
+                     ::"r"(tmem), "l"(da_lo), "l"(db_hi), "r"(idesc), "r"(1u));
+      }
+      asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                       smem_u32(bars + stg))
+                   : "memory");
     }
   }
-  int8_t* sxh = (int8_t*)bsm;
-  int8_t* sxl = sxh + TT * k;
-  float* ssx = (float*)(sxl + TT * k);
-  int* ss16 = (int*)(ssx + TT * U);
-  const int T = *st.nact;
-  const int t0 = blockIdx.y * TT;
-  if (t0 >= T) return;
-  {
-    const int nt = min(TT, T - t0);
-    // stage the tile: xh, xl rows are contiguous per token and the tile's
-    // tokens are consecutive, so each array is one contiguous span
-    {
-      const int4* gh = (const int4*)(q.xh + (size_t)t0 * k);
-      const int4* gl = (const int4*)(q.xl + (size_t)t0 * k);
-      const int nv = nt * k / 16;
-      for (int i = threadIdx.x; i < nv; i += CK_THREADS) {
-        ((int4*)sxh)[i] = gh[i];
-        ((int4*)sxl)[i] = gl[i];
-      }
-      for (int i = threadIdx.x; i < nt * U; i += CK_THREADS) ssx[i] = q.sx[(size_t)t0 * U + i];
-      for (int i = threadIdx.x; i < nt * 2 * U; i += CK_THREADS) ss16[i] = q.s16[(size_t)t0 * 2 * U + i];
-    }
-    __syncthreads();
-    if (!has) return;
-    float v[TT];
+  // the last commit covers every earlier MMA
+  const int last = nchunk - 1;
+  if (!mbar_wait_bounded(bars + (last & 1), (last >> 1) & 1, err)) ok = false;
+  asm volatile("tcgen05.fence::after_thread_sync;");
+  if (ok) {
+    // warp w reads accumulator lanes 32*(w%4).. (rows) and half the columns
+    const int q4 = warp & 3, half = warp >> 2;
+    const int row = r0 + 32 * q4 + lane;
+    for (int col = half * (TC_NT / 2); col < (half + 1) * (TC_NT / 2); col += 16) {
+      uint32_t r[16];
+      const uint32_t taddr = tmem + ((uint32_t)(32 * q4) << 16) + (uint32_t)col;
+      asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+                   : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+                     "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+                     "=r"(r[15])
+                   : "r"(taddr));
+      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+      if (row < S.n) {
 #pragma unroll
-    for (int i = 0; i < TT; i++) {
-      v[i] = 0.f;
-      if (i < nt) {
-#pragma unroll
-        for (int j = 0; j < 3; j++) {
-          const int c = lane + 32 * j;
-          if (j < upl && c < U) {
-            XUnit x;
-            const int4* h = (const int4*)(sxh + i * k) + 2 * c;
-            const int4* l = (const int4*)(sxl + i * k) + 2 * c;
-            const int4 h0 = h[0], h1 = h[1], l0 = l[0], l1 = l[1];
-            x.h[0] = h0.x; x.h[1] = h0.y; x.h[2] = h0.z; x.h[3] = h0.w;
-            x.h[4] = h1.x; x.h[5] = h1.y; x.h[6] = h1.z; x.h[7] = h1.w;
-            x.l[0] = l0.x; x.l[1] = l0.y; x.l[2] = l0.z; x.l[3] = l0.w;
-            x.l[4] = l1.x; x.l[5] = l1.y; x.l[6] = l1.z; x.l[7] = l1.w;
-            x.sx = ssx[i * U + c];
-            x.sa = ss16[i * 2 * U + 2 * c];
-            x.sb = ss16[i * 2 * U + 2 * c + 1];
-            v[i] += unit_dot8(u[j], x);
+        for (int j = 0; j < 16; j++) {
+          const int n = col + j;
+          if (n < nt) {
+            const size_t o = (size_t)(t0 + n) * S.ldo + row;
+            const float y = xh.xs[t0 + n] * __uint_as_float(r[j]);
+            S.out[o] = S.add ? S.add[o] + y : y;
           }
         }
       }
     }
-    const float tot = reduce_scatter<TT>(v);
-    const int i = lane % TT;
-    if (lane < TT && i < nt) {
-      const size_t o = (size_t)(t0 + i) * S.ldo + row;
-      const float y = q.xs[t0 + i] * tot;
-      S.out[o] = S.add ? S.add[o] + y : y;
-    }
   }
+  asm volatile("tcgen05.fence::before_thread_sync;");
+  __syncthreads();
+  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TC_NT));
 }
 
 // Attention for one (active entry, kv head): QK-norm + RoPE + K/V store at
@@ -424,7 +496,7 @@ struct ck_batch {
   uint32_t* d_ids = nullptr;
   float *x = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *ao = nullptr, *g = nullptr, *u = nullptr,
         *logits = nullptr;
-  BXq xq{};
+  BXh xh{};
   uint8_t* pin = nullptr;     // pinned staging: tok | slot | pos | nact | ids | err
   std::vector<BSeq> seqs;     // one per slot
   std::vector<int> free_blocks;
@@ -484,14 +556,11 @@ int bgemm_launch(ck_batch* b, cudaStream_t s, int k, std::initializer_list<BSeg>
   for (const BSeg& x : segs) {
     G.tile0[G.nseg] = tiles;
     G.seg[G.nseg++] = x;
-    tiles += (x.n + CK_WARPS - 1) / CK_WARPS;
+    tiles += (x.n + TC_ROWS - 1) / TC_ROWS;
   }
   G.tile0[G.nseg] = tiles;
-  const size_t smem = bgemm_smem(k);
-  const int tt = bgemm_tt(k);
-  const dim3 grid(tiles, (b->max_seqs + tt - 1) / tt);   // token tiles past T return at once
-  if (tt == 32) k_bgemm<32><<<grid, CK_THREADS, smem, s>>>(G, bstep(b), b->xq);
-  else k_bgemm<16><<<grid, CK_THREADS, smem, s>>>(G, bstep(b), b->xq);
+  const dim3 grid(tiles, (b->max_seqs + TC_NT - 1) / TC_NT);   // token tiles past T return at once
+  k_bgemm_tc<<<grid, TC_THREADS, TC_SMEM, s>>>(G, bstep(b), b->xh, b->d_err);
   return CK_OK;
 }
 
@@ -510,7 +579,7 @@ void bprep(ck_batch* b, cudaStream_t s, int kind, const float* a, const float* b
            int lda) {
   BPrep p;
   p.kind = kind; p.a = a; p.b = bb; p.w = w; p.eps = eps; p.k = k; p.lda = lda;
-  k_bprep<<<b->max_seqs, CK_THREADS, 0, s>>>(p, bstep(b), b->xq);
+  k_bprep<<<b->max_seqs, CK_THREADS, 0, s>>>(p, bstep(b), b->xh);
 }
 
 // The whole step on stream s (captured once into a graph).
@@ -567,8 +636,8 @@ int ck_batch_create(ck_engine* h, int max_seqs, int kv_blocks, ck_batch** out) {
   if (max_seqs < 1 || max_seqs > 1024) return h->fail(CK_EINVAL, "max_seqs %d outside [1, 1024]", max_seqs);
   const int max_blocks = (c.context_length + CK_BLK - 1) / CK_BLK;
   if (max_blocks > 256) return h->fail(CK_EINVAL, "batched decode handles contexts up to %d", 256 * CK_BLK);
-  if (bgemm_smem(c.intermediate) > CK_DYN_SMEM_MAX || bgemm_smem(c.heads * c.head_dim) > CK_DYN_SMEM_MAX)
-    return h->fail(CK_EINVAL, "batched decode: matmul input too wide");
+  if (c.hidden % 32 || c.intermediate % 32 || c.hidden > CK_KMAX || c.intermediate > CK_KMAX)
+    return h->fail(CK_EINVAL, "batched decode: matmul widths must be multiples of 32 up to %d", CK_KMAX);
   ck_batch* b = new ck_batch();
   b->h = h;
   b->max_seqs = max_seqs;
@@ -597,16 +666,14 @@ int ck_batch_create(ck_engine* h, int max_seqs, int kv_blocks, ck_batch** out) {
       (rc = balloc(b, &b->k, S * kvd * 4)) || (rc = balloc(b, &b->v, S * kvd * 4)) ||
       (rc = balloc(b, &b->ao, S * qd * 4)) || (rc = balloc(b, &b->g, S * I * 4)) ||
       (rc = balloc(b, &b->u, S * I * 4)) || (rc = balloc(b, &b->logits, S * c.vocab * 4)) ||
-      (rc = balloc(b, &b->xq.xh, S * CK_KMAX)) || (rc = balloc(b, &b->xq.xl, S * CK_KMAX)) ||
-      (rc = balloc(b, &b->xq.sx, S * (CK_KMAX / 32) * 4)) || (rc = balloc(b, &b->xq.s16, S * (CK_KMAX / 16) * 4)) ||
-      (rc = balloc(b, &b->xq.xs, S * 4)))
+      (rc = balloc(b, &b->xh.hi, S * CK_KMAX * 2)) || (rc = balloc(b, &b->xh.lo, S * CK_KMAX * 2)) ||
+      (rc = balloc(b, &b->xh.xs, S * 4)))
     return bail(rc);
   if (cudaMemset(b->d_err, 0, 16) != cudaSuccess || cudaMemset(b->d_nact, 0, 16) != cudaSuccess ||
       cudaMemset(b->d_btab, 0, S * max_blocks * 4) != cudaSuccess)
     return bail(b->fail(CK_ECUDA, "memset"));
   if (cudaMallocHost(&b->pin, S * 16 + 64) != cudaSuccess) return bail(b->fail(CK_ENOMEM, "pinned staging"));
-  if (cudaFuncSetAttribute(k_bgemm<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, CK_DYN_SMEM_MAX) != cudaSuccess ||
-      cudaFuncSetAttribute(k_bgemm<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, CK_DYN_SMEM_MAX) != cudaSuccess)
+  if (cudaFuncSetAttribute(k_bgemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM) != cudaSuccess)
     return bail(b->fail(CK_ECUDA, "matmul shared memory"));
   b->seqs.resize(max_seqs);
   b->btab.assign(S * max_blocks, 0);
@@ -696,8 +763,10 @@ int ck_batch_step(ck_batch* b, int* n_active) {
   CKB(b, cudaMemcpyAsync(perr, b->d_err, 4, cudaMemcpyDeviceToHost, s));
   CKB(b, cudaStreamSynchronize(s));
   if (*perr) {
+    const int bits = *perr;
     cudaMemset(b->d_err, 0, 4);
-    return b->fail(CK_EDEVICE, "token id outside embedding table");
+    if (bits & CK_DERR_TOKEN) return b->fail(CK_EDEVICE, "token id outside embedding table");
+    return b->fail(CK_EDEVICE, "batched step: a device wait timed out (bits 0x%x)", bits);
   }
   b->steps++;
   b->fed += T;
@@ -755,6 +824,58 @@ int ck_batch_stats(ck_batch* b, uint64_t* steps, uint64_t* tokens_fed, uint64_t*
 }
 
 const char* ck_batch_last_error(ck_batch* b) { return b ? b->err.c_str() : g_err.c_str(); }
+
+// Y[T x n] = X[T x k] W^T through the batched path's prologue and
+// tensor-core GEMM (parity helper: x host fp32 [T][k], y host fp32 [T][n]).
+int ck_matmul(int ggml_type, const void* bytes, size_t nbytes, int k, int n, const float* x, int T, float* y,
+              int device) {
+  if (!bytes || !x || !y || T < 1 || T > 1024 || k % 32 || k > CK_KMAX)
+    return set_global(CK_EINVAL, "ck_matmul: bad argument");
+  ck_engine* h;
+  int rc = make_tmp(device, &h);
+  if (rc) return rc;
+  Weight w;
+  float *dx = nullptr, *dy = nullptr, *xs = nullptr;
+  __half *hi = nullptr, *lo = nullptr;
+  int *nact = nullptr, *err = nullptr;
+  auto done = [&](int code) {
+    std::string m = h->err;
+    free_tmp(h);
+    return code ? set_global(code, "ck_matmul: %s", m.c_str()) : CK_OK;
+  };
+  if ((rc = prep_weight(h, ggml_type, bytes, nbytes, k, n, w)) || (rc = dalloc(h, &dx, (size_t)T * k * 4)) ||
+      (rc = dalloc(h, &dy, (size_t)T * n * 4)) || (rc = dalloc(h, &xs, (size_t)T * 4)) ||
+      (rc = dalloc(h, &hi, (size_t)T * k * 2)) || (rc = dalloc(h, &lo, (size_t)T * k * 2)) ||
+      (rc = dalloc(h, &nact, 16)) || (rc = dalloc(h, &err, 16)))
+    return done(rc);
+  cudaMemcpy(dx, x, (size_t)T * k * 4, cudaMemcpyHostToDevice);
+  cudaMemcpy(nact, &T, 4, cudaMemcpyHostToDevice);
+  cudaMemset(err, 0, 16);
+  BStep st;
+  memset(&st, 0, sizeof st);
+  st.nact = nact;
+  BXh xh;
+  xh.hi = hi; xh.lo = lo; xh.xs = xs;
+  BPrep p;
+  p.kind = BP_COPY; p.a = dx; p.b = nullptr; p.w = nullptr; p.eps = 0.f; p.k = k; p.lda = k;
+  k_bprep<<<T, CK_THREADS, 0, h->own>>>(p, st, xh);
+  BGemm G;
+  memset(&G, 0, sizeof G);
+  G.k = k;
+  G.nseg = 1;
+  G.seg[0] = bseg(w, dy, nullptr, n);
+  G.tile0[1] = (n + TC_ROWS - 1) / TC_ROWS;
+  cudaFuncSetAttribute(k_bgemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM);
+  k_bgemm_tc<<<dim3(G.tile0[1], (T + TC_NT - 1) / TC_NT), TC_THREADS, TC_SMEM, h->own>>>(G, st, xh, err);
+  cudaError_t e = cudaGetLastError();
+  int herr = 0;
+  if (e == cudaSuccess) e = cudaMemcpyAsync(y, dy, (size_t)T * n * 4, cudaMemcpyDeviceToHost, h->own);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(&herr, err, 4, cudaMemcpyDeviceToHost, h->own);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(h->own);
+  if (e != cudaSuccess) return done(h->fail(CK_ECUDA, "%s", cudaGetErrorString(e)));
+  if (herr) return done(h->fail(CK_EDEVICE, "device wait timed out"));
+  return done(CK_OK);
+}
 
 int ck_batch_destroy(ck_batch* b) {
   if (!b) return CK_OK;

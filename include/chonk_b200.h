@@ -153,6 +153,10 @@ int ck_dequant(int ggml_type, const void* bytes, size_t nbytes, int k, int n, fl
 /* y = W x through the production matvec kernel (x host fp32[k], y fp32[n]). */
 int ck_matvec(int ggml_type, const void* bytes, size_t nbytes, int k, int n, const float* x, float* y,
               int device);
+/* Y[T x n] = X[T x k] W^T through the batched path (its prologue and the
+ * tcgen05 tensor-core GEMM): x host fp32 [T][k], y host fp32 [T][n]. */
+int ck_matmul(int ggml_type, const void* bytes, size_t nbytes, int k, int n, const float* x, int T, float* y,
+              int device);
 /* Time `reps` launches of the matvec kernel on an n x k weight resident on
  * the device; writes mean microseconds per launch (CUDA events). */
 int ck_bench_matvec(int ggml_type, const void* bytes, size_t nbytes, int k, int n, int reps, double* us_per,

@@ -47,6 +47,29 @@ def _run(batch, pending, max_steps=2000):
     return [ids[j] for j in range(len(pending))]
 
 
+MATMUL_TOL = 2e-5   # relative: x and w each split into two fp16 parts (~22 bits), fp32 accumulation
+
+
+@pytest.mark.parametrize("t,k,n,T", [(12, 1024, 300, 1), (14, 512, 129, 37), (8, 576, 260, 130), (6, 576, 200, 16),
+                                     (7, 64, 130, 5)])
+def test_tensor_core_matmul(t, k, n, T):
+    """The batched path's tcgen05 GEMM (prologue split of x + dequant split of
+    W, three MMAs per step) against fp64 over the oracle's dequantized
+    weights: single token, partial and multiple 128-token tiles, partial
+    128-row tiles, every block type."""
+    import torch
+    from chonklm_b200 import _lib
+    from chonklm_b200.quant import quantize
+    g = torch.Generator().manual_seed(t * 1000 + k + T)
+    data = quantize(torch.randn(n, k, generator=g) * 0.02, t)
+    x = (np.random.default_rng(T).standard_normal((T, k)) * 3).astype(np.float32)
+    y = _lib.matmul(t, data, k, n, x)
+    w = oracle.dequant(t, np.frombuffer(data, dtype=np.uint8), k, n).astype(np.float64)
+    ref = x.astype(np.float64) @ w.T
+    err = np.abs(y - ref).max() / np.abs(ref).max()
+    assert err < MATMUL_TOL, err
+
+
 @pytest.mark.parametrize("arch", ["llama", "qwen3"])
 def test_batch_matches_oracle_greedy(tiny_dir, arch):
     from chonklm_b200 import _lib
