@@ -44,6 +44,11 @@ CONFIGS = {
 }
 MAX_CONTEXT = {"qwen3-0.6b": 2048, "qwen3-0.6b-q8": 2048, "smollm2-135m": 512, "gemma3-270m": 512}
 METRIC = "Q4_K_M bs=1 decode tok/s + matvec HBM GB/s vs B200 peak"
+# 256 independent sequences, 128-token prompt + 256 greedy
+# tokens each, continuous batching over a paged fp16 KV cache, sequences
+# sharded across the GPUs (sequence i on rank i mod N), no collective.
+BATCHED = {"spec": "smollm2-135m", "seqs": 256, "prompt": 128, "generated": 256, "max_context": 512}
+BATCHED_METRIC = "batched decode aggregate tok/s (256 sequences, continuous batching)"
 
 
 def log(*a):
@@ -215,13 +220,55 @@ def matvec_report(path, peak):
     return out
 
 
+def run_batched(rank: int, world: int, barrier, local: int, warmup: int, max_steps: int = 0):
+    """Config 5 on this rank's share of the sequences: every step advances
+    each running sequence one position (ck_batch_step, host-synchronised);
+    returns (generated tokens, seconds, steps, tokens fed)."""
+    import numpy as np
+    from chonklm_b200 import _lib
+    from chonklm_b200.registry import ModelDef
+    from chonklm_b200.runtime import loadLlamaWgslModel
+    from chonklm_b200.synth import SPECS
+    B = BATCHED
+    S = SPECS[B["spec"]]
+    path = model_file(B["spec"], rank, world, barrier)
+    loaded = loadLlamaWgslModel(ModelDef(id="batched", label="batched", vocab=S.vocab, maxContext=B["max_context"],
+                                         gguf=path, eosIds=[]), device=local)
+    eng = loaded.engine.dev
+    mine = [i for i in range(B["seqs"]) if i % world == rank]
+    prompts = {i: np.random.default_rng(1 + i).integers(0, S.vocab, size=B["prompt"]).tolist() for i in mine}
+    # warm-up: the same shapes on a throw-away batch (kernel loading, graph capture)
+    wb = _lib.Batch(eng, max_seqs=len(mine))
+    for i in mine:
+        wb.add(prompts[i], B["generated"])
+    for _ in range(warmup):
+        wb.step()
+    wb.close()
+    b = _lib.Batch(eng, max_seqs=len(mine))
+    for i in mine:
+        b.add(prompts[i], B["generated"])
+    barrier()
+    t0 = time.perf_counter()
+    n = 0
+    while b.step() > 0:
+        n += 1
+        if max_steps and n >= max_steps:   # profiling runs stop early
+            break
+    dt = time.perf_counter() - t0
+    steps, fed, gen = b.stats()
+    b.close()
+    loaded.engine.dispose()
+    return gen, dt, steps, fed
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", default="qwen3-0.6b-q4_k_m", choices=list(CONFIGS))
+    ap.add_argument("--config", default="qwen3-0.6b-q4_k_m", choices=list(CONFIGS) + ["smollm2-135m-batched"])
+    ap.add_argument("--no-batched", action="store_true", help="skip the batched (config 5) summary")
     ap.add_argument("--mode", type=int, default=0, help="0 megakernel, 1 per-phase CUDA graph")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-matvec", action="store_true")
@@ -249,8 +296,45 @@ def main():
             dist.barrier()
 
     if args.impl == "reference":
-        run_reference(args, args.config, rank, world, barrier)
+        if args.config == "smollm2-135m-batched":
+            if rank == 0:
+                print(json.dumps({"impl": "reference", "unavailable":
+                                  "the reference decodes one sequence per engine (no batched path) and its "
+                                  "WebGPU runtime is unavailable on this box"}), flush=True)
+        else:
+            run_reference(args, args.config, rank, world, barrier)
         if dist is not None:
+            dist.destroy_process_group()
+        return
+
+    if args.config == "smollm2-135m-batched":
+        torch.cuda.set_device(local)
+        gen, dt, steps, fed = run_batched(rank, world, barrier, local, args.warmup, args.profile)
+        vals = torch.tensor([dt, float(gen)], dtype=torch.float64, device="cuda")
+        if dist is not None:
+            t = vals[:1].clone()
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            g = vals[1:].clone()
+            dist.all_reduce(g, op=dist.ReduceOp.SUM)
+            vals = torch.cat([t, g])
+        max_s, total_gen = float(vals[0]), float(vals[1])
+        if rank == 0:
+            B = BATCHED
+            print(json.dumps({
+                "metric": BATCHED_METRIC, "value": round(total_gen / max_s, 1), "unit": "tok/s", "n_gpus": world,
+                "steps": int(steps), "warmup": args.warmup, "ms_per_step": round(1000 * max_s / max(steps, 1), 4),
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp16x2/fp32-tcgen05",
+                "data": "synthetic",
+                "config": {"workload": "smollm2-135m-batched", "sequences": B["seqs"], "prompt": B["prompt"],
+                           "generated": B["generated"], "kv_cache": "paged fp16, 16-position blocks",
+                           "parallelism": f"sequences sharded over {world} GPU(s), no collective",
+                           "timing": "wall clock over host-synchronised steps (each step: ids up, next ids down)"},
+                "e2e": {"value": round(total_gen / max_s, 1), "unit": "tok/s",
+                        "h2d_bytes_per_step": int(12 * B["seqs"] / world + 4),
+                        "d2h_bytes_per_step": int(4 * B["seqs"] / world + 4)},
+                "tokens_fed": int(fed), "tokens_generated": int(total_gen)}), flush=True)
+        if dist is not None:
+            dist.barrier()
             dist.destroy_process_group()
         return
 
@@ -375,6 +459,15 @@ def main():
                 cpu = cpu_baseline_sample(path, S.vocab, MAX_CONTEXT[spec])
             except Exception as e:  # reported, not fatal
                 cpu = {"value": None, "error": str(e)}
+        batched = None
+        if world == 1 and not args.no_batched:
+            try:
+                gen_b, dt_b, steps_b, fed_b = run_batched(0, 1, lambda: None, local, 3)
+                batched = {"metric": BATCHED_METRIC, "value": round(gen_b / dt_b, 1), "unit": "tok/s",
+                           "ms_per_step": round(1000 * dt_b / max(steps_b, 1), 3), "steps": steps_b,
+                           "config": "smollm2-135m-batched (BASELINE configs[4]) on 1 GPU"}
+            except Exception as e:
+                batched = {"error": str(e)}
         mv = None
         if not args.no_matvec:
             try:
@@ -401,6 +494,7 @@ def main():
                          "bytes_per_token": round(bytes_per_token), "us_per_token": round(per_tok_s * 1e6, 2)},
             "cpu_baseline": cpu,
             "matvec": mv,
+            "batched": batched,
             "clocks": clk.summary(),
             "gpu_launches": int(launches_per_token * gen * args.steps),
             "decode_ids_head": ids0[:2],
