@@ -36,8 +36,7 @@ struct BStep {
 };
 
 struct BXh {             // per-token matmul input x = hi + lo (two fp16 parts)
-  __half* hi;            // [max_seqs][k]
-  __half* lo;
+  __half* xt;            // operand tiles of the step's tokens (tc_index layout)
   float* xs;             // [max_seqs] output scale (RMS of NORM, else 1)
 };
 
@@ -53,7 +52,8 @@ struct BPrep {
 };
 
 struct BSeg {
-  const uint8_t* w;
+  const uint8_t* w;      // device-layout weight rows (the single-sequence matvec's copy)
+  const __half* wt;      // the same weights as fp16 operand tiles (tc_format)
   Lay L;
   int n;
   float* out;            // out[t * ldo + row]
@@ -93,16 +93,105 @@ __global__ void __launch_bounds__(256) k_bembed(const uint8_t* w, Lay L, float s
   for (int i = threadIdx.x; i < H; i += blockDim.x) x[(size_t)t * H + i] = __fmul_rn(dequant_at(row, L, i), scale);
 }
 
+// ---------------------------------------------------------------------------
+// Tensor-core GEMM (tcgen05) for the batched matmuls.
+//
+// Operands are fp16 "operand tiles": 128 rows x 64 columns in the K-major
+// canonical shared-memory layout (8-row x 16-byte core matrices; the two
+// 16-byte K halves of a 16-wide step 128 bytes apart, 8-row groups 256 bytes
+// apart, 16-wide steps 4 KB apart), 16 KB each, stored [row tile][K chunk]
+// [hi|lo] so a CTA moves every tile with one bulk copy.  A value v is kept
+// as two fp16 parts hi = fp16(v), lo = fp16(v - hi) (~22 significant bits):
+// the weights are dequantized into tiles once, when a batch is created
+// (k_tc_format: 4 bytes per weight), and the prologue kernel writes x the
+// same way.  D[128 weight rows x N tokens] accumulates in tensor memory
+// (fp32): one thread keeps TC_STAGES chunks of four tiles in flight
+// (cp.async.bulk completing on the stage's mbarrier), issues three MMAs per
+// 16-wide step (w_hi x_hi + w_hi x_lo + w_lo x_hi; fp16 alone measured
+// 3.8e-4 relative error per dot, bf16 3.3e-3) and commits them to the
+// stage's release barrier; the accumulator is read back (tcgen05.ld, 32 rows
+// per warp quarter) for the epilogue (prologue scale, residual add).
+#define TC_ROWS 128
+#define TC_NT 128            // tokens per CTA tile (columns of the accumulator)
+#define TC_KC 64             // K per chunk
+#define TC_THREADS 256
+#define TC_STAGES 3
+#define TC_TILE 16384        // bytes of one operand tile
+#define TC_SMEM (TC_STAGES * 4 * TC_TILE + 128)
+
+__host__ __device__ inline int tc_nch(int k) { return (k + TC_KC - 1) / TC_KC; }
+__host__ __device__ inline size_t tc_bytes(int rows, int k) {
+  return (size_t)((rows + TC_ROWS - 1) / TC_ROWS) * tc_nch(k) * 2 * TC_TILE;
+}
+// byte offset of (row, k) inside one tile
+__device__ __forceinline__ uint32_t kmaj_off(int row, int k) {
+  return (uint32_t)((k >> 4) * TC_ROWS * 32 + (row >> 3) * 256 + ((k >> 3) & 1) * 128 + (row & 7) * 16 + (k & 7) * 2);
+}
+// half-element index of (row r, column e) in a tiled matrix, part 0 = hi, 1 = lo
+__device__ __forceinline__ size_t tc_index(int r, int e, int nch, int part) {
+  const size_t tile = ((size_t)(r >> 7) * nch + (e >> 6)) * 2 + part;
+  return tile * (TC_TILE / 2) + kmaj_off(r & 127, e & 63) / 2;
+}
+__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+         ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);   // version 1, no swizzle
+}
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* err) {
+  unsigned spins = 0;
+  while (!mbar_try_wait(bar, parity)) {
+    if (++spins > (1u << 22)) {
+      atomicOr(err, CK_DERR_BARRIER);
+      return false;
+    }
+  }
+  return true;
+}
+
+// Dequantize n x k weights into operand tiles (grid: row tiles x K chunks;
+// a thread per 32-weight unit of the chunk).  Rows past n and columns past k
+// are zero.
+__global__ void __launch_bounds__(256) k_tc_format(const uint8_t* w, Lay L, int n, int k, __half* out) {
+  const int row = blockIdx.x * TC_ROWS + (threadIdx.x >> 1), uu = threadIdx.x & 1;
+  const int c = blockIdx.y, unit = c * 2 + uu, nch = gridDim.y;
+  float wv[32];
+  if (row < n && unit < (k >> 5)) {
+    U8 u;
+    unpack_unit<true>(L.type, w + (size_t)row * L.row_bytes, L, unit, u);
+#pragma unroll
+    for (int i = 0; i < 32; i++) {
+      // byte codes are signed (Q8_0 stores int8; the other types' codes are < 64)
+      const int code = (int)(int8_t)((u.q[i >> 2] >> (8 * (i & 3))) & 0xFF);
+      wv[i] = (i < 16 ? u.a0 : u.a1) * (float)(code + u.ko) + u.b;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; i++) wv[i] = 0.f;
+  }
+#pragma unroll
+  for (int cc = 0; cc < 4; cc++) {
+    __align__(16) __half hv[8], lv[8];
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+      const float x = wv[8 * cc + e];
+      hv[e] = __float2half_rn(x);
+      lv[e] = __float2half_rn(x - __half2float(hv[e]));
+    }
+    const int col = c * TC_KC + 32 * uu + 8 * cc;
+    *(int4*)(out + tc_index(row, col, nch, 0)) = *(const int4*)hv;
+    *(int4*)(out + tc_index(row, col, nch, 1)) = *(const int4*)lv;
+  }
+}
+
 // Per-token prologue (one CTA per active entry): the COPY / NORM / SILU forms
-// of the single-sequence prologue, x written as two fp16 parts for the
-// tensor-core GEMM.  NORM's RMS scale is applied to the matmul output, as in
+// of the single-sequence prologue, x written as two fp16 parts into the
+// operand tiles of the tensor-core GEMM.  NORM's RMS scale is applied to the matmul output, as in
 // the single-sequence path.
 __global__ void __launch_bounds__(CK_THREADS) k_bprep(BPrep p, BStep st, BXh q) {
   constexpr int PER = CK_KMAX / CK_THREADS;
   const int t = blockIdx.x;
   if (t >= *st.nact) return;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int k = p.k;
+  const int k = p.k, nch = tc_nch(k);
   const float* a = p.a + (size_t)t * p.lda;
   const float* b = p.kind == BP_SILU ? p.b + (size_t)t * p.lda : p.w;
   __shared__ float red[CK_WARPS];
@@ -122,9 +211,14 @@ __global__ void __launch_bounds__(CK_THREADS) k_bprep(BPrep p, BStep st, BXh q) 
     else if (p.kind == BP_SILU) v = (va[j] / (1.0f + expf(-va[j]))) * vb[j];
     if (i < k) {
       const __half h = __float2half_rn(v);
-      q.hi[(size_t)t * k + i] = h;
-      q.lo[(size_t)t * k + i] = __float2half_rn(v - __half2float(h));
+      q.xt[tc_index(t, i, nch, 0)] = h;
+      q.xt[tc_index(t, i, nch, 1)] = __float2half_rn(v - __half2float(h));
     }
+  }
+  // columns past k in the last chunk meet zero weights: keep them finite
+  for (int i = k + tid; i < nch * TC_KC; i += CK_THREADS) {
+    q.xt[tc_index(t, i, nch, 0)] = __float2half_rn(0.f);
+    q.xt[tc_index(t, i, nch, 1)] = __float2half_rn(0.f);
   }
   if (p.kind == BP_NORM) {
     ss = warp_sum(ss);
@@ -140,50 +234,6 @@ __global__ void __launch_bounds__(CK_THREADS) k_bprep(BPrep p, BStep st, BXh q) 
   }
 }
 
-// ---------------------------------------------------------------------------
-// Tensor-core GEMM (tcgen05) for the batched matmuls.
-//
-// D[128 weight rows x N tokens] accumulates in tensor memory (fp32) over the
-// K dimension in chunks of 64: for each chunk every thread dequantizes one
-// 32-weight unit of one row to fp32, splits it into two fp16 values
-// (hi = fp16(w), lo = fp16(w - hi)) and stores both into shared memory in
-// the K-major canonical layout (8-row x 16-byte core matrices: the two 16-byte
-// K halves of a 16-wide step 128 bytes apart, 8-row groups 256 bytes apart);
-// x arrives already split the same way from the prologue kernel.  One thread
-// issues three MMAs per 16-wide step (w_hi x_hi + w_hi x_lo + w_lo x_hi), so
-// the products carry ~22 significant bits (fp16 alone would give ~4e-4
-// relative error per dot), and commits them to the stage's mbarrier; the next
-// chunk is dequantized into the other stage meanwhile.  At the end the
-// accumulator is read back (tcgen05.ld, 32 rows per warp quarter) and the
-// epilogue scales by the token's prologue scale and adds the residual.
-#define TC_ROWS 128
-#define TC_NT 128            // tokens per CTA tile (columns of the accumulator)
-#define TC_KC 64             // K per stage
-#define TC_THREADS 256
-#define TC_A_BYTES (TC_ROWS * TC_KC * 2)    // one fp16 weight tile (16 KB)
-#define TC_B_BYTES (TC_NT * TC_KC * 2)      // one fp16 token tile (16 KB)
-#define TC_STAGE (2 * TC_A_BYTES + 2 * TC_B_BYTES)
-#define TC_SMEM (2 * TC_STAGE + 64)
-
-__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
-  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
-         ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);   // version 1, no swizzle
-}
-// byte offset of (row, k) in a K-major tile of `rows` rows and TC_KC columns
-__device__ __forceinline__ uint32_t kmaj_off(int row, int k, int rows) {
-  return (uint32_t)((k >> 4) * rows * 32 + (row >> 3) * 256 + ((k >> 3) & 1) * 128 + (row & 7) * 16 + (k & 7) * 2);
-}
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* err) {
-  unsigned spins = 0;
-  while (!mbar_try_wait(bar, parity)) {
-    if (++spins > (1u << 22)) {
-      atomicOr(err, CK_DERR_BARRIER);
-      return false;
-    }
-  }
-  return true;
-}
-
 __global__ void __launch_bounds__(TC_THREADS, 1) k_bgemm_tc(BGemm G, BStep st, BXh xh, int* err) {
   extern __shared__ __align__(1024) uint8_t tsm[];
   __shared__ uint32_t s_tmem;
@@ -196,91 +246,53 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_bgemm_tc(BGemm G, BStep st, B
   int si = 0;
   while (si + 1 < G.nseg && (int)blockIdx.x >= G.tile0[si + 1]) si++;
   const BSeg& S = G.seg[si];
-  const int r0 = ((int)blockIdx.x - G.tile0[si]) * TC_ROWS;
-  const int k = G.k, U = k >> 5, nchunk = (k + TC_KC - 1) / TC_KC;
-  uint64_t* bars = (uint64_t*)(tsm + 2 * TC_STAGE);
+  const int rt = (int)blockIdx.x - G.tile0[si], r0 = rt * TC_ROWS;
+  const int nch = tc_nch(G.k);
+  uint64_t* full = (uint64_t*)(tsm + TC_STAGES * 4 * TC_TILE);
+  uint64_t* empty = full + TC_STAGES;
+  uint64_t* done = empty + TC_STAGES;
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
                  "r"(TC_NT));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   if (tid == 0) {
-    mbar_init(bars, 1);
-    mbar_init(bars + 1, 1);
+    for (int i = 0; i < 2 * TC_STAGES + 1; i++) mbar_init(full + i, 1);
     mbar_fence_init();
   }
   asm volatile("tcgen05.fence::before_thread_sync;");
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;");
   const uint32_t tmem = s_tmem;
-  // instruction descriptor: fp32 D, fp16 A and B, both K-major, M = 128, N
-  const uint32_t idesc = (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(TC_ROWS >> 4) << 24);
   bool ok = true;
-  for (int c = 0; c < nchunk && ok; c++) {
-    const int stg = c & 1;
-    uint8_t* base = tsm + stg * TC_STAGE;
-    uint8_t* a_hi = base;
-    uint8_t* a_lo = base + TC_A_BYTES;
-    uint8_t* b_hi = base + 2 * TC_A_BYTES;
-    uint8_t* b_lo = b_hi + TC_B_BYTES;
-    if (c >= 2) ok = mbar_wait_bounded(bars + stg, ((c >> 1) - 1) & 1, err);   // MMAs of chunk c-2 done
-    if (!ok) break;
-    // weights: thread -> (row, unit) of this chunk
-    {
-      const int row = tid >> 1, uu = tid & 1;
-      const int unit = c * 2 + uu;
-      const int grow = r0 + row;
-      float w[32];
-      if (grow < S.n && unit < U) {
-        U8 u;
-        unpack_unit<true>(S.L.type, S.w + (size_t)grow * S.L.row_bytes, S.L, unit, u);
-#pragma unroll
-        for (int i = 0; i < 32; i++) {
-          // byte codes are signed (Q8_0 stores int8; the other types' codes are < 64)
-          const int code = (int)(int8_t)((u.q[i >> 2] >> (8 * (i & 3))) & 0xFF);
-          w[i] = (i < 16 ? u.a0 : u.a1) * (float)(code + u.ko) + u.b;
-        }
-      } else {
-#pragma unroll
-        for (int i = 0; i < 32; i++) w[i] = 0.f;
-      }
-#pragma unroll
-      for (int cc = 0; cc < 4; cc++) {      // 8 weights = one 16-byte row of a core matrix
-        __align__(16) __half hv[8], lv[8];
-#pragma unroll
-        for (int e = 0; e < 8; e++) {
-          const float x = w[8 * cc + e];
-          hv[e] = __float2half_rn(x);
-          lv[e] = __float2half_rn(x - __half2float(hv[e]));
-        }
-        const uint32_t off = kmaj_off(row, 32 * uu + 8 * cc, TC_ROWS);
-        *(int4*)(a_hi + off) = *(const int4*)hv;
-        *(int4*)(a_lo + off) = *(const int4*)lv;
-      }
-    }
-    // tokens: 16-byte pieces of x_hi / x_lo
-    for (int i = tid; i < TC_NT * (TC_KC / 8); i += TC_THREADS) {
-      const int n = i >> 3, piece = i & 7;
-      const int kk = c * TC_KC + 8 * piece;
-      int4 vh = make_int4(0, 0, 0, 0), vl = make_int4(0, 0, 0, 0);
-      if (n < nt && kk < k) {
-        vh = *(const int4*)(xh.hi + (size_t)(t0 + n) * k + kk);
-        vl = *(const int4*)(xh.lo + (size_t)(t0 + n) * k + kk);
-      }
-      const uint32_t off = kmaj_off(n, 8 * piece, TC_NT);
-      *(int4*)(b_hi + off) = vh;
-      *(int4*)(b_lo + off) = vl;
-    }
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // generic-proxy stores -> tensor core
-    __syncthreads();
-    if (tid == 0) {
+  if (tid == 0) {
+    // instruction descriptor: fp32 D, fp16 A and B, both K-major, M = 128, N
+    const uint32_t idesc = (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(TC_ROWS >> 4) << 24);
+    const uint8_t* a_src = (const uint8_t*)S.wt + (size_t)rt * nch * 2 * TC_TILE;
+    const uint8_t* b_src = (const uint8_t*)xh.xt + (size_t)blockIdx.y * nch * 2 * TC_TILE;
+    auto issue = [&](int c) {
+      const int sg = c % TC_STAGES;
+      uint8_t* dst = tsm + sg * 4 * TC_TILE;
+      mbar_expect_tx(full + sg, 4 * TC_TILE);
+      bulk_g2s(dst, a_src + (size_t)c * 2 * TC_TILE, TC_TILE, full + sg);
+      bulk_g2s(dst + TC_TILE, a_src + ((size_t)c * 2 + 1) * TC_TILE, TC_TILE, full + sg);
+      bulk_g2s(dst + 2 * TC_TILE, b_src + (size_t)c * 2 * TC_TILE, TC_TILE, full + sg);
+      bulk_g2s(dst + 3 * TC_TILE, b_src + ((size_t)c * 2 + 1) * TC_TILE, TC_TILE, full + sg);
+    };
+    int issued = 0;
+    for (; issued < TC_STAGES && issued < nch; issued++) issue(issued);
+    int c = 0;
+    for (; c < nch; c++) {
+      const int sg = c % TC_STAGES;
+      if (!mbar_wait_bounded(full + sg, (c / TC_STAGES) & 1, err)) { ok = false; break; }
       asm volatile("tcgen05.fence::after_thread_sync;");
+      const uint32_t base = smem_u32(tsm + sg * 4 * TC_TILE);
 #pragma unroll
       for (int kk = 0; kk < TC_KC / 16; kk++) {
-        const uint64_t da_hi = umma_desc(smem_u32(a_hi) + kk * TC_ROWS * 32, 128, 256);
-        const uint64_t da_lo = umma_desc(smem_u32(a_lo) + kk * TC_ROWS * 32, 128, 256);
-        const uint64_t db_hi = umma_desc(smem_u32(b_hi) + kk * TC_NT * 32, 128, 256);
-        const uint64_t db_lo = umma_desc(smem_u32(b_lo) + kk * TC_NT * 32, 128, 256);
+        const uint64_t da_hi = umma_desc(base + kk * TC_ROWS * 32, 128, 256);
+        const uint64_t da_lo = umma_desc(base + TC_TILE + kk * TC_ROWS * 32, 128, 256);
+        const uint64_t db_hi = umma_desc(base + 2 * TC_TILE + kk * TC_ROWS * 32, 128, 256);
+        const uint64_t db_lo = umma_desc(base + 3 * TC_TILE + kk * TC_ROWS * 32, 128, 256);
         const uint32_t acc0 = (c > 0 || kk > 0) ? 1u : 0u;
         asm volatile("{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
                      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n"
@@ -293,19 +305,32 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_bgemm_tc(BGemm G, BStep st, B
                      ::"r"(tmem), "l"(da_lo), "l"(db_hi), "r"(idesc), "r"(1u));
       }
       asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                       smem_u32(bars + stg))
+                       smem_u32(empty + sg))
                    : "memory");
+      if (issued < nch) {   // refill this stage once its MMAs have read it
+        if (!mbar_wait_bounded(empty + sg, (c / TC_STAGES) & 1, err)) { ok = false; c++; break; }
+        issue(issued++);
+      }
     }
+    if (!ok) {   // copies still in flight must land before the CTA's shared memory is released
+      for (int j = c; j < issued; j++) mbar_wait_bounded(full + j % TC_STAGES, (j / TC_STAGES) & 1, err);
+    }
+    // one more commit: arrives once every MMA issued above has completed
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                     smem_u32(done))
+                 : "memory");
   }
-  // the last commit covers every earlier MMA
-  const int last = nchunk - 1;
-  if (!mbar_wait_bounded(bars + (last & 1), (last >> 1) & 1, err)) ok = false;
+  __syncthreads();
+  if (!mbar_wait_bounded(done, 0, err)) ok = false;
   asm volatile("tcgen05.fence::after_thread_sync;");
-  if (ok) {
+  __shared__ int s_ok;
+  if (tid == 0) s_ok = ok ? 1 : 0;
+  __syncthreads();
+  if (s_ok) {
     // warp w reads accumulator lanes 32*(w%4).. (rows) and half the columns
     const int q4 = warp & 3, half = warp >> 2;
     const int row = r0 + 32 * q4 + lane;
-    for (int col = half * (TC_NT / 2); col < (half + 1) * (TC_NT / 2); col += 16) {
+    for (int col = half * (TC_NT / 2); col < (half + 1) * (TC_NT / 2) && col < nt; col += 16) {
       uint32_t r[16];
       const uint32_t taddr = tmem + ((uint32_t)(32 * q4) << 16) + (uint32_t)col;
       asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
@@ -497,6 +522,7 @@ struct ck_batch {
   float *x = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *ao = nullptr, *g = nullptr, *u = nullptr,
         *logits = nullptr;
   BXh xh{};
+  std::vector<__half*> wt;    // operand tiles per weight: layer-major q k v o gate up down, then the head
   uint8_t* pin = nullptr;     // pinned staging: tok | slot | pos | nact | ids | err
   std::vector<BSeq> seqs;     // one per slot
   std::vector<int> free_blocks;
@@ -564,9 +590,10 @@ int bgemm_launch(ck_batch* b, cudaStream_t s, int k, std::initializer_list<BSeg>
   return CK_OK;
 }
 
-BSeg bseg(const Weight& w, float* out, const float* add, int ldo) {
+BSeg bseg(const Weight& w, const __half* wt, float* out, const float* add, int ldo) {
   BSeg s;
   s.w = w.dev;
+  s.wt = wt;
   s.L = w.L;
   s.n = w.n;
   s.out = out;
@@ -591,8 +618,10 @@ int batch_enqueue(ck_batch* b, cudaStream_t s) {
   k_bembed<<<b->max_seqs, 256, 0, s>>>(h->emb.dev, h->emb.L, c.embedding_scale, bstep(b), b->x, H, c.vocab, b->d_err);
   for (int i = 0; i < c.layers; i++) {
     const LayerW& W = h->L[i];
+    __half* const* wt = &b->wt[(size_t)7 * i];
     bprep(b, s, BP_NORM, b->x, nullptr, W.attn_norm, c.norm_eps, H, H);
-    bgemm_launch(b, s, H, {bseg(W.q, b->q, nullptr, qd), bseg(W.k, b->k, nullptr, kvd), bseg(W.v, b->v, nullptr, kvd)});
+    bgemm_launch(b, s, H, {bseg(W.q, wt[0], b->q, nullptr, qd), bseg(W.k, wt[1], b->k, nullptr, kvd),
+                           bseg(W.v, wt[2], b->v, nullptr, kvd)});
     BAttn a;
     a.q = b->q; a.k = b->k; a.v = b->v;
     a.qw = c.qk_norm ? W.q_norm : nullptr;
@@ -610,14 +639,14 @@ int batch_enqueue(ck_batch* b, cudaStream_t s) {
     else if (hd == 128) k_battn<4><<<grid, CK_THREADS, 0, s>>>(a, bstep(b));
     else k_battn<8><<<grid, CK_THREADS, 0, s>>>(a, bstep(b));
     bprep(b, s, BP_COPY, b->ao, nullptr, nullptr, 0.f, qd, qd);
-    bgemm_launch(b, s, qd, {bseg(W.o, b->x, b->x, H)});
+    bgemm_launch(b, s, qd, {bseg(W.o, wt[3], b->x, b->x, H)});
     bprep(b, s, BP_NORM, b->x, nullptr, W.post_norm, c.norm_eps, H, H);
-    bgemm_launch(b, s, H, {bseg(W.gate, b->g, nullptr, I), bseg(W.up, b->u, nullptr, I)});
+    bgemm_launch(b, s, H, {bseg(W.gate, wt[4], b->g, nullptr, I), bseg(W.up, wt[5], b->u, nullptr, I)});
     bprep(b, s, BP_SILU, b->g, b->u, nullptr, 0.f, I, I);
-    bgemm_launch(b, s, I, {bseg(W.down, b->x, b->x, H)});
+    bgemm_launch(b, s, I, {bseg(W.down, wt[6], b->x, b->x, H)});
   }
   bprep(b, s, BP_NORM, b->x, nullptr, h->final_norm, c.norm_eps, H, H);
-  bgemm_launch(b, s, H, {bseg(h->head, b->logits, nullptr, c.vocab)});
+  bgemm_launch(b, s, H, {bseg(h->head, b->wt[(size_t)7 * c.layers], b->logits, nullptr, c.vocab)});
   k_bargmax<<<b->max_seqs, CK_THREADS, 0, s>>>(b->logits, c.vocab, bstep(b), b->d_ids);
   CKB(b, cudaGetLastError());
   return CK_OK;
@@ -666,9 +695,26 @@ int ck_batch_create(ck_engine* h, int max_seqs, int kv_blocks, ck_batch** out) {
       (rc = balloc(b, &b->k, S * kvd * 4)) || (rc = balloc(b, &b->v, S * kvd * 4)) ||
       (rc = balloc(b, &b->ao, S * qd * 4)) || (rc = balloc(b, &b->g, S * I * 4)) ||
       (rc = balloc(b, &b->u, S * I * 4)) || (rc = balloc(b, &b->logits, S * c.vocab * 4)) ||
-      (rc = balloc(b, &b->xh.hi, S * CK_KMAX * 2)) || (rc = balloc(b, &b->xh.lo, S * CK_KMAX * 2)) ||
-      (rc = balloc(b, &b->xh.xs, S * 4)))
+      (rc = balloc(b, &b->xh.xt, tc_bytes(max_seqs, CK_KMAX))) || (rc = balloc(b, &b->xh.xs, S * 4)))
     return bail(rc);
+  // every weight as operand tiles (dequantized once: 4 bytes per weight)
+  {
+    std::vector<const Weight*> ws;
+    for (int i = 0; i < c.layers; i++) {
+      const LayerW& W = h->L[i];
+      for (const Weight* w : {&W.q, &W.k, &W.v, &W.o, &W.gate, &W.up, &W.down}) ws.push_back(w);
+    }
+    ws.push_back(&h->head);
+    for (const Weight* w : ws) {
+      __half* t = nullptr;
+      const int kk = w->L.k;
+      if ((rc = balloc(b, &t, tc_bytes(w->n, kk)))) return bail(rc);
+      k_tc_format<<<dim3((w->n + TC_ROWS - 1) / TC_ROWS, tc_nch(kk)), 256, 0, b->stream>>>(w->dev, w->L, w->n, kk, t);
+      b->wt.push_back(t);
+    }
+    if (cudaGetLastError() != cudaSuccess || cudaStreamSynchronize(b->stream) != cudaSuccess)
+      return bail(b->fail(CK_ECUDA, "weight tiles"));
+  }
   if (cudaMemset(b->d_err, 0, 16) != cudaSuccess || cudaMemset(b->d_nact, 0, 16) != cudaSuccess ||
       cudaMemset(b->d_btab, 0, S * max_blocks * 4) != cudaSuccess)
     return bail(b->fail(CK_ECUDA, "memset"));
@@ -836,7 +882,7 @@ int ck_matmul(int ggml_type, const void* bytes, size_t nbytes, int k, int n, con
   if (rc) return rc;
   Weight w;
   float *dx = nullptr, *dy = nullptr, *xs = nullptr;
-  __half *hi = nullptr, *lo = nullptr;
+  __half *wt = nullptr, *xt = nullptr;
   int *nact = nullptr, *err = nullptr;
   auto done = [&](int code) {
     std::string m = h->err;
@@ -845,17 +891,19 @@ int ck_matmul(int ggml_type, const void* bytes, size_t nbytes, int k, int n, con
   };
   if ((rc = prep_weight(h, ggml_type, bytes, nbytes, k, n, w)) || (rc = dalloc(h, &dx, (size_t)T * k * 4)) ||
       (rc = dalloc(h, &dy, (size_t)T * n * 4)) || (rc = dalloc(h, &xs, (size_t)T * 4)) ||
-      (rc = dalloc(h, &hi, (size_t)T * k * 2)) || (rc = dalloc(h, &lo, (size_t)T * k * 2)) ||
+      (rc = dalloc(h, &wt, tc_bytes(n, k))) || (rc = dalloc(h, &xt, tc_bytes(T, k))) ||
       (rc = dalloc(h, &nact, 16)) || (rc = dalloc(h, &err, 16)))
     return done(rc);
   cudaMemcpy(dx, x, (size_t)T * k * 4, cudaMemcpyHostToDevice);
   cudaMemcpy(nact, &T, 4, cudaMemcpyHostToDevice);
   cudaMemset(err, 0, 16);
+  k_tc_format<<<dim3((n + TC_ROWS - 1) / TC_ROWS, tc_nch(k)), 256, 0, h->own>>>(w.dev, w.L, n, k, wt);
   BStep st;
   memset(&st, 0, sizeof st);
   st.nact = nact;
   BXh xh;
-  xh.hi = hi; xh.lo = lo; xh.xs = xs;
+  xh.xt = xt;
+  xh.xs = xs;
   BPrep p;
   p.kind = BP_COPY; p.a = dx; p.b = nullptr; p.w = nullptr; p.eps = 0.f; p.k = k; p.lda = k;
   k_bprep<<<T, CK_THREADS, 0, h->own>>>(p, st, xh);
@@ -863,7 +911,7 @@ int ck_matmul(int ggml_type, const void* bytes, size_t nbytes, int k, int n, con
   memset(&G, 0, sizeof G);
   G.k = k;
   G.nseg = 1;
-  G.seg[0] = bseg(w, dy, nullptr, n);
+  G.seg[0] = bseg(w, wt, dy, nullptr, n);
   G.tile0[1] = (n + TC_ROWS - 1) / TC_ROWS;
   cudaFuncSetAttribute(k_bgemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM);
   k_bgemm_tc<<<dim3(G.tile0[1], (T + TC_NT - 1) / TC_NT), TC_THREADS, TC_SMEM, h->own>>>(G, st, xh, err);
