@@ -65,7 +65,8 @@ struct BGemm {
   BSeg seg[3];
   int nseg;
   int k;
-  int tile0[4];          // first 16-row tile of each segment; tile0[nseg] = total
+  int tile0[4];          // first 128-row tile of each segment; tile0[nseg] = total
+  int splits;            // K slices per row tile (the cluster size, <= 8 and <= the K chunks)
 };
 
 struct BAttn {
@@ -234,20 +235,49 @@ __global__ void __launch_bounds__(CK_THREADS) k_bprep(BPrep p, BStep st, BXh q) 
   }
 }
 
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ float4 ld_dsmem4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
+  return v;
+}
+
+// One CTA = one 128-row tile x one 128-token tile x one K slice.  A row
+// tile's G.splits K slices form one thread-block cluster (cluster rank =
+// slice): each slice accumulates its chunks in its own tensor memory, copies
+// the accumulator to shared memory, and after a cluster barrier every CTA
+// sums one column range of the tile over all slices in rank order (read
+// through distributed shared memory, so the result does not depend on
+// timing) and writes it with the epilogue.
 __global__ void __launch_bounds__(TC_THREADS, 1) k_bgemm_tc(BGemm G, BStep st, BXh xh, int* err) {
   extern __shared__ __align__(1024) uint8_t tsm[];
   __shared__ uint32_t s_tmem;
+  __shared__ int s_ok;
+  __shared__ float s_xs[TC_NT];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int T = *st.nact;
   const int t0 = blockIdx.y * TC_NT;
-  if (t0 >= T) return;                          // before any TMEM is held
+  if (t0 >= T) return;                          // the whole cluster (same blockIdx.y), before any TMEM is held
   const int nt = min(TC_NT, T - t0);
   const int N = (nt + 15) & ~15;                // MMA N: a multiple of 16
-  int si = 0;
-  while (si + 1 < G.nseg && (int)blockIdx.x >= G.tile0[si + 1]) si++;
-  const BSeg& S = G.seg[si];
-  const int rt = (int)blockIdx.x - G.tile0[si], r0 = rt * TC_ROWS;
+  const int S = G.splits, ks = (int)blockIdx.x % S, tile = (int)blockIdx.x / S;
+  // the row tile's segment: its fields read into registers with constant
+  // parameter indices (a dynamically indexed parameter is read through a
+  // generic address, again after every asm statement that clobbers memory)
+  const int si = (G.nseg > 1 && tile >= G.tile0[1]) + (G.nseg > 2 && tile >= G.tile0[2]);
+  const __half* s_wt;
+  const float* s_add;
+  float* s_out;
+  int s_n, s_ldo;
+#define TC_PICK(I) \
+  { s_wt = G.seg[I].wt; s_add = G.seg[I].add; s_out = G.seg[I].out; s_n = G.seg[I].n; s_ldo = G.seg[I].ldo; }
+  if (si == 0) TC_PICK(0) else if (si == 1) TC_PICK(1) else TC_PICK(2)
+#undef TC_PICK
+  const int rt = tile - G.tile0[si], r0 = rt * TC_ROWS;
   const int nch = tc_nch(G.k);
+  const int c_lo = ks * nch / S, c_hi = (ks + 1) * nch / S;   // splits <= chunks: never empty
   uint64_t* full = (uint64_t*)(tsm + TC_STAGES * 4 * TC_TILE);
   uint64_t* empty = full + TC_STAGES;
   uint64_t* done = empty + TC_STAGES;
@@ -268,10 +298,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_bgemm_tc(BGemm G, BStep st, B
   if (tid == 0) {
     // instruction descriptor: fp32 D, fp16 A and B, both K-major, M = 128, N
     const uint32_t idesc = (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(TC_ROWS >> 4) << 24);
-    const uint8_t* a_src = (const uint8_t*)S.wt + (size_t)rt * nch * 2 * TC_TILE;
+    const uint8_t* a_src = (const uint8_t*)s_wt + (size_t)rt * nch * 2 * TC_TILE;
     const uint8_t* b_src = (const uint8_t*)xh.xt + (size_t)blockIdx.y * nch * 2 * TC_TILE;
     auto issue = [&](int c) {
-      const int sg = c % TC_STAGES;
+      const int sg = (c - c_lo) % TC_STAGES;
       uint8_t* dst = tsm + sg * 4 * TC_TILE;
       mbar_expect_tx(full + sg, 4 * TC_TILE);
       bulk_g2s(dst, a_src + (size_t)c * 2 * TC_TILE, TC_TILE, full + sg);
@@ -279,12 +309,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_bgemm_tc(BGemm G, BStep st, B
       bulk_g2s(dst + 2 * TC_TILE, b_src + (size_t)c * 2 * TC_TILE, TC_TILE, full + sg);
       bulk_g2s(dst + 3 * TC_TILE, b_src + ((size_t)c * 2 + 1) * TC_TILE, TC_TILE, full + sg);
     };
-    int issued = 0;
-    for (; issued < TC_STAGES && issued < nch; issued++) issue(issued);
-    int c = 0;
-    for (; c < nch; c++) {
-      const int sg = c % TC_STAGES;
-      if (!mbar_wait_bounded(full + sg, (c / TC_STAGES) & 1, err)) { ok = false; break; }
+    int issued = c_lo;
+    for (; issued < c_lo + TC_STAGES && issued < c_hi; issued++) issue(issued);
+    int c = c_lo;
+    for (; c < c_hi; c++) {
+      const int j = c - c_lo, sg = j % TC_STAGES;
+      if (!mbar_wait_bounded(full + sg, (j / TC_STAGES) & 1, err)) { ok = false; break; }
       asm volatile("tcgen05.fence::after_thread_sync;");
       const uint32_t base = smem_u32(tsm + sg * 4 * TC_TILE);
 #pragma unroll
@@ -293,7 +323,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_bgemm_tc(BGemm G, BStep st, B
         const uint64_t da_lo = umma_desc(base + TC_TILE + kk * TC_ROWS * 32, 128, 256);
         const uint64_t db_hi = umma_desc(base + 2 * TC_TILE + kk * TC_ROWS * 32, 128, 256);
         const uint64_t db_lo = umma_desc(base + 3 * TC_TILE + kk * TC_ROWS * 32, 128, 256);
-        const uint32_t acc0 = (c > 0 || kk > 0) ? 1u : 0u;
+        const uint32_t acc0 = (j > 0 || kk > 0) ? 1u : 0u;
         asm volatile("{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
                      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n"
                      ::"r"(tmem), "l"(da_hi), "l"(db_hi), "r"(idesc), "r"(acc0));
@@ -307,30 +337,64 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_bgemm_tc(BGemm G, BStep st, B
       asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                        smem_u32(empty + sg))
                    : "memory");
-      if (issued < nch) {   // refill this stage once its MMAs have read it
-        if (!mbar_wait_bounded(empty + sg, (c / TC_STAGES) & 1, err)) { ok = false; c++; break; }
+      if (issued < c_hi) {   // refill this stage once its MMAs have read it
+        if (!mbar_wait_bounded(empty + sg, (j / TC_STAGES) & 1, err)) { ok = false; c++; break; }
         issue(issued++);
       }
     }
-    if (!ok) {   // copies still in flight must land before the CTA's shared memory is released
-      for (int j = c; j < issued; j++) mbar_wait_bounded(full + j % TC_STAGES, (j / TC_STAGES) & 1, err);
+    if (!ok) {   // copies still in flight must land before the CTA's shared memory is reused
+      for (int i = c; i < issued; i++) mbar_wait_bounded(full + (i - c_lo) % TC_STAGES, ((i - c_lo) / TC_STAGES) & 1, err);
     }
     // one more commit: arrives once every MMA issued above has completed
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                      smem_u32(done))
                  : "memory");
   }
+  // while thread 0 runs the K loop: the tokens' output scales
+  if (tid >= TC_THREADS - TC_NT) {
+    const int n = tid - (TC_THREADS - TC_NT);
+    s_xs[n] = n < nt ? xh.xs[t0 + n] : 0.f;
+  }
   __syncthreads();
   if (!mbar_wait_bounded(done, 0, err)) ok = false;
   asm volatile("tcgen05.fence::after_thread_sync;");
-  __shared__ int s_ok;
   if (tid == 0) s_ok = ok ? 1 : 0;
   __syncthreads();
-  if (s_ok) {
-    // warp w reads accumulator lanes 32*(w%4).. (rows) and half the columns
-    const int q4 = warp & 3, half = warp >> 2;
-    const int row = r0 + 32 * q4 + lane;
-    for (int col = half * (TC_NT / 2); col < (half + 1) * (TC_NT / 2) && col < nt; col += 16) {
+  // warp w holds accumulator lanes (rows) 32*(w%4).. and half the columns
+  const int q4 = warp & 3, half = warp >> 2, rl = 32 * q4 + lane, row = r0 + rl;
+  const int cend = min((half + 1) * (TC_NT / 2), nt);
+  if (S == 1) {
+    // straight from the accumulator: 16 columns (tokens) per tcgen05.ld
+    for (int col = half * (TC_NT / 2); col < cend; col += 16) {
+      uint32_t r[16];
+      const uint32_t taddr = tmem + ((uint32_t)(32 * q4) << 16) + (uint32_t)col;
+      asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+                   : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+                     "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+                     "=r"(r[15])
+                   : "r"(taddr));
+      const int m = min(16, cend - col);
+      float av[16];
+      if (s_add && row < s_n) {   // every residual value before any store (out may alias add)
+        const float* ap = s_add + (size_t)(t0 + col) * s_ldo + row;
+#pragma unroll
+        for (int j = 0; j < 16; j++) av[j] = j < m ? ap[(size_t)j * s_ldo] : 0.f;
+      } else {
+#pragma unroll
+        for (int j = 0; j < 16; j++) av[j] = 0.f;
+      }
+      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+      if (s_ok && row < s_n) {
+        float* op = s_out + (size_t)(t0 + col) * s_ldo + row;
+#pragma unroll
+        for (int j = 0; j < 16; j++)
+          if (j < m) op[(size_t)j * s_ldo] = av[j] + s_xs[col + j] * __uint_as_float(r[j]);
+      }
+    }
+  } else {
+    // accumulator -> ex[column][row] (fp32, over the drained stage buffers)
+    float* ex = (float*)tsm;
+    for (int col = half * (TC_NT / 2); col < cend; col += 16) {
       uint32_t r[16];
       const uint32_t taddr = tmem + ((uint32_t)(32 * q4) << 16) + (uint32_t)col;
       asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
@@ -339,18 +403,62 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_bgemm_tc(BGemm G, BStep st, B
                      "=r"(r[15])
                    : "r"(taddr));
       asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-      if (row < S.n) {
+      float* ep = ex + col * TC_ROWS + rl;
 #pragma unroll
-        for (int j = 0; j < 16; j++) {
-          const int n = col + j;
-          if (n < nt) {
-            const size_t o = (size_t)(t0 + n) * S.ldo + row;
-            const float y = xh.xs[t0 + n] * __uint_as_float(r[j]);
-            S.out[o] = S.add ? S.add[o] + y : y;
+      for (int j = 0; j < 16; j++) ep[j * TC_ROWS] = s_ok ? __uint_as_float(r[j]) : 0.f;   // past nt: never read
+    }
+    // this CTA's columns [cb, ce) of the tile, summed over the slices in
+    // rank order through distributed shared memory (16-byte loads); thread:
+    // rows 4*(tid % 32) .. +3, columns cb + tid / 32, + 8, ...; two column
+    // passes' loads in flight per round
+    const int cb = ks * nt / S, ce = (ks + 1) * nt / S;
+    const int rr = 4 * (tid & 31), orow = r0 + rr, cs = tid >> 5;
+    const bool vec = (s_ldo & 3) == 0 && orow + 3 < s_n;
+    uint32_t rbase[8];
+    const uint32_t lbase = smem_u32(ex) + (uint32_t)rr * 4u;
+#pragma unroll
+    for (int q = 0; q < 8; q++) {
+      rbase[q] = lbase;
+      if (q < S) asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rbase[q]) : "r"(lbase), "r"(q));
+    }
+    cluster_sync_all();
+    for (int c0 = cb + cs; c0 < ce; c0 += 16) {
+      const int c1 = c0 + 8;   // second column of the round (valid if < ce)
+      float4 v[2][8];
+#pragma unroll
+      for (int q = 0; q < 8; q++) {
+        if (q < S) {   // uniform over the CTA
+          v[0][q] = ld_dsmem4(rbase[q] + (uint32_t)(c0 * TC_ROWS * 4));
+          v[1][q] = ld_dsmem4(rbase[q] + (uint32_t)(min(c1, TC_NT - 1) * TC_ROWS * 4));
+        }
+      }
+#pragma unroll
+      for (int h = 0; h < 2; h++) {
+        const int c = h ? c1 : c0;
+        if (c >= ce || orow >= s_n) continue;
+        float4 acc = v[h][0];
+#pragma unroll
+        for (int q = 1; q < 8; q++)
+          if (q < S) { acc.x += v[h][q].x; acc.y += v[h][q].y; acc.z += v[h][q].z; acc.w += v[h][q].w; }
+        const float xs = s_xs[c];
+        float* op = s_out + (size_t)(t0 + c) * s_ldo + orow;
+        const float* ap = s_add ? s_add + (size_t)(t0 + c) * s_ldo + orow : nullptr;
+        if (vec) {
+          float4 y = make_float4(xs * acc.x, xs * acc.y, xs * acc.z, xs * acc.w);
+          if (ap) {
+            const float4 a4 = *(const float4*)ap;
+            y.x += a4.x; y.y += a4.y; y.z += a4.z; y.w += a4.w;
           }
+          *(float4*)op = y;
+        } else {
+          const float a[4] = {acc.x, acc.y, acc.z, acc.w};
+#pragma unroll
+          for (int i = 0; i < 4; i++)
+            if (orow + i < s_n) op[i] = (ap ? ap[i] : 0.f) + xs * a[i];
         }
       }
     }
+    cluster_sync_all();   // no CTA leaves while another still reads its shared memory
   }
   asm volatile("tcgen05.fence::before_thread_sync;");
   __syncthreads();
@@ -574,6 +682,76 @@ BStep bstep(const ck_batch* b) {
   return s;
 }
 
+// K slices per row tile (the cluster size): the largest size, at most 8 (the
+// portable cluster size) and at most one slice per K chunk, whose clusters
+// all fit on the device at once (cudaOccupancyMaxActiveClusters); 1 when the
+// row tiles alone fill it.
+int tc_max_clusters(int s) {
+  static int cache[64][9];
+  static bool init[64];
+  static std::mutex mu;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return 0;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!init[dev]) {
+    for (int c = 1; c <= 8; c++) {
+      cudaLaunchConfig_t cfg;
+      memset(&cfg, 0, sizeof cfg);
+      cfg.gridDim = dim3(c, 1, 1);
+      cfg.blockDim = dim3(TC_THREADS);
+      cfg.dynamicSmemBytes = TC_SMEM;
+      cudaLaunchAttribute at[1];
+      at[0].id = cudaLaunchAttributeClusterDimension;
+      at[0].val.clusterDim.x = c;
+      at[0].val.clusterDim.y = 1;
+      at[0].val.clusterDim.z = 1;
+      cfg.attrs = at;
+      cfg.numAttrs = 1;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, k_bgemm_tc, &cfg) != cudaSuccess) {
+        cudaGetLastError();
+        n = 0;
+      }
+      cache[dev][c] = n;
+    }
+    init[dev] = true;
+  }
+  return cache[dev][s];
+}
+
+int tc_splits(int units, int nch) {
+  // a cluster waits for its longest slice: among the sizes whose clusters all
+  // fit at once, the one with the shortest longest slice, the smallest such
+  // (fewer partial tiles to sum)
+  int best = 1, best_len = nch;
+  for (int s = 2; s <= 8 && s <= nch; s++) {
+    if (units > tc_max_clusters(s)) continue;
+    const int len = (nch + s - 1) / s;
+    if (len < best_len) { best = s; best_len = len; }
+  }
+  return best;
+}
+
+cudaError_t tc_launch(BGemm& G, BStep st, BXh xh, int* err, int ttiles, cudaStream_t s) {
+  const int tiles = G.tile0[G.nseg];
+  G.splits = tc_splits(tiles * ttiles, tc_nch(G.k));
+  cudaLaunchConfig_t cfg;
+  memset(&cfg, 0, sizeof cfg);
+  cfg.gridDim = dim3(tiles * G.splits, ttiles);
+  cfg.blockDim = dim3(TC_THREADS);
+  cfg.dynamicSmemBytes = TC_SMEM;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = G.splits;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = G.splits > 1 ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, k_bgemm_tc, G, st, xh, err);
+}
+
 int bgemm_launch(ck_batch* b, cudaStream_t s, int k, std::initializer_list<BSeg> segs) {
   BGemm G;
   memset(&G, 0, sizeof G);
@@ -585,8 +763,8 @@ int bgemm_launch(ck_batch* b, cudaStream_t s, int k, std::initializer_list<BSeg>
     tiles += (x.n + TC_ROWS - 1) / TC_ROWS;
   }
   G.tile0[G.nseg] = tiles;
-  const dim3 grid(tiles, (b->max_seqs + TC_NT - 1) / TC_NT);   // token tiles past T return at once
-  k_bgemm_tc<<<grid, TC_THREADS, TC_SMEM, s>>>(G, bstep(b), b->xh, b->d_err);
+  // token tiles past T return at once
+  CKB(b, tc_launch(G, bstep(b), b->xh, b->d_err, (b->max_seqs + TC_NT - 1) / TC_NT, s));
   return CK_OK;
 }
 
@@ -620,8 +798,9 @@ int batch_enqueue(ck_batch* b, cudaStream_t s) {
     const LayerW& W = h->L[i];
     __half* const* wt = &b->wt[(size_t)7 * i];
     bprep(b, s, BP_NORM, b->x, nullptr, W.attn_norm, c.norm_eps, H, H);
-    bgemm_launch(b, s, H, {bseg(W.q, wt[0], b->q, nullptr, qd), bseg(W.k, wt[1], b->k, nullptr, kvd),
-                           bseg(W.v, wt[2], b->v, nullptr, kvd)});
+    int rc = bgemm_launch(b, s, H, {bseg(W.q, wt[0], b->q, nullptr, qd), bseg(W.k, wt[1], b->k, nullptr, kvd),
+                                    bseg(W.v, wt[2], b->v, nullptr, kvd)});
+    if (rc) return rc;
     BAttn a;
     a.q = b->q; a.k = b->k; a.v = b->v;
     a.qw = c.qk_norm ? W.q_norm : nullptr;
@@ -639,14 +818,16 @@ int batch_enqueue(ck_batch* b, cudaStream_t s) {
     else if (hd == 128) k_battn<4><<<grid, CK_THREADS, 0, s>>>(a, bstep(b));
     else k_battn<8><<<grid, CK_THREADS, 0, s>>>(a, bstep(b));
     bprep(b, s, BP_COPY, b->ao, nullptr, nullptr, 0.f, qd, qd);
-    bgemm_launch(b, s, qd, {bseg(W.o, wt[3], b->x, b->x, H)});
+    if ((rc = bgemm_launch(b, s, qd, {bseg(W.o, wt[3], b->x, b->x, H)}))) return rc;
     bprep(b, s, BP_NORM, b->x, nullptr, W.post_norm, c.norm_eps, H, H);
-    bgemm_launch(b, s, H, {bseg(W.gate, wt[4], b->g, nullptr, I), bseg(W.up, wt[5], b->u, nullptr, I)});
+    rc = bgemm_launch(b, s, H, {bseg(W.gate, wt[4], b->g, nullptr, I), bseg(W.up, wt[5], b->u, nullptr, I)});
+    if (rc) return rc;
     bprep(b, s, BP_SILU, b->g, b->u, nullptr, 0.f, I, I);
-    bgemm_launch(b, s, I, {bseg(W.down, wt[6], b->x, b->x, H)});
+    if ((rc = bgemm_launch(b, s, I, {bseg(W.down, wt[6], b->x, b->x, H)}))) return rc;
   }
   bprep(b, s, BP_NORM, b->x, nullptr, h->final_norm, c.norm_eps, H, H);
-  bgemm_launch(b, s, H, {bseg(h->head, b->wt[(size_t)7 * c.layers], b->logits, nullptr, c.vocab)});
+  int rc = bgemm_launch(b, s, H, {bseg(h->head, b->wt[(size_t)7 * c.layers], b->logits, nullptr, c.vocab)});
+  if (rc) return rc;
   k_bargmax<<<b->max_seqs, CK_THREADS, 0, s>>>(b->logits, c.vocab, bstep(b), b->d_ids);
   CKB(b, cudaGetLastError());
   return CK_OK;
@@ -721,6 +902,7 @@ int ck_batch_create(ck_engine* h, int max_seqs, int kv_blocks, ck_batch** out) {
   if (cudaMallocHost(&b->pin, S * 16 + 64) != cudaSuccess) return bail(b->fail(CK_ENOMEM, "pinned staging"));
   if (cudaFuncSetAttribute(k_bgemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM) != cudaSuccess)
     return bail(b->fail(CK_ECUDA, "matmul shared memory"));
+  tc_max_clusters(1);   // the occupancy table, before the step graph is captured
   b->seqs.resize(max_seqs);
   b->btab.assign(S * max_blocks, 0);
   for (int i = b->n_blocks - 1; i >= 0; i--) b->free_blocks.push_back(i);
@@ -914,8 +1096,7 @@ int ck_matmul(int ggml_type, const void* bytes, size_t nbytes, int k, int n, con
   G.seg[0] = bseg(w, wt, dy, nullptr, n);
   G.tile0[1] = (n + TC_ROWS - 1) / TC_ROWS;
   cudaFuncSetAttribute(k_bgemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM);
-  k_bgemm_tc<<<dim3(G.tile0[1], (T + TC_NT - 1) / TC_NT), TC_THREADS, TC_SMEM, h->own>>>(G, st, xh, err);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = tc_launch(G, st, xh, err, (T + TC_NT - 1) / TC_NT, h->own);
   int herr = 0;
   if (e == cudaSuccess) e = cudaMemcpyAsync(y, dy, (size_t)T * n * 4, cudaMemcpyDeviceToHost, h->own);
   if (e == cudaSuccess) e = cudaMemcpyAsync(&herr, err, 4, cudaMemcpyDeviceToHost, h->own);

@@ -51,7 +51,7 @@ MATMUL_TOL = 2e-5   # relative: x and w each split into two fp16 parts (~22 bits
 
 
 @pytest.mark.parametrize("t,k,n,T", [(12, 1024, 300, 1), (14, 512, 129, 37), (8, 576, 260, 130), (6, 576, 200, 16),
-                                     (7, 64, 130, 5)])
+                                     (7, 64, 130, 5), (12, 256, 6272, 3), (14, 256, 20000, 200)])
 def test_tensor_core_matmul(t, k, n, T):
     """The batched path's tcgen05 GEMM (prologue split of x + dequant split of
     W, three MMAs per step) against fp64 over the oracle's dequantized
