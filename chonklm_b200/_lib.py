@@ -96,6 +96,7 @@ def lib():
             L.ck_global_error.restype = ctypes.c_char_p
             L.ck_set_stream.argtypes = [P, P]
             L.ck_set_mode.argtypes = [P, I]
+            L.ck_set_prefill_gemm.argtypes = [P, I, I]
             L.ck_enqueue_decode_steps.argtypes = [P, I]
             L.ck_sync.argtypes = [P]
             L.ck_step_bytes.argtypes = [P, pp(D), pp(D)]
@@ -225,6 +226,11 @@ class Engine:
 
     def set_mode(self, mode: int) -> None:
         _check(self._L.ck_set_mode(self.h, int(mode)), self.h)
+
+    def set_prefill_gemm(self, min_tokens: int, chunk: int = 0) -> None:
+        """Prompts of more than min_tokens ids (0: never) prefill on the
+        tensor cores, chunk ids per pass (0: the largest)."""
+        _check(self._L.ck_set_prefill_gemm(self.h, int(min_tokens), int(chunk)), self.h)
 
     def enqueue_decode_steps(self, n: int) -> None:
         _check(self._L.ck_enqueue_decode_steps(self.h, int(n)), self.h)

@@ -48,6 +48,8 @@ size_t elem_kv(const ck_model_cfg& c) { return c.kv_dtype == CK_KV_F32 ? 4 : 2; 
 
 }  // namespace
 
+struct ck_prefill_state;   // tensor-core prefill buffers (ck_prefill.cuh)
+
 struct ck_engine {
   ck_model_cfg cfg;
   int device = 0;
@@ -90,6 +92,10 @@ struct ck_engine {
   unsigned long long io_h2d = 0, io_d2h = 0;  // bytes copied by step calls
   CkState shadow;
   uint8_t* pinned = nullptr;  // staging for small copies
+  // tensor-core prefill: prompts of at least pf_min tokens (0: never), pf_chunk
+  // tokens per pass (0: the largest)
+  ck_prefill_state* pf = nullptr;
+  int pf_min = 64, pf_chunk = 0;
 
   int fail(int code, const char* fmt, ...) {
     char buf[512];
@@ -765,6 +771,13 @@ int ck_run_token(ck_engine* h, uint32_t token, int need_logits, const ck_samplin
   return CK_OK;
 }
 
+}  // extern "C"
+namespace {   // tensor-core prefill (ck_prefill.cuh)
+bool pf_supported(const ck_engine* h);
+int prefill_gemm(ck_engine* h, int n);
+}  // namespace
+extern "C" {
+
 int ck_prefill(ck_engine* h, const uint32_t* tokens, int n, int need_logits_last, const ck_sampling* s,
                uint32_t* out_id) {
   int rc = pre_step(h);
@@ -776,7 +789,14 @@ int ck_prefill(ck_engine* h, const uint32_t* tokens, int n, int need_logits_last
     if (tokens[i] >= (uint32_t)h->cfg.vocab) return h->fail(CK_EINVAL, "token id %u outside embedding table", tokens[i]);
   if ((rc = set_params(h, s, 0, 0, false))) return rc;
   CKC(h, h2d(h, h->D.tokens + h->pos, tokens, (size_t)n * 4));
-  for (int i = 0; i < n; i++)
+  int first = 0;   // tokens before this one went through the tensor-core prefill
+  if (h->pf_min > 0 && n - 1 >= h->pf_min && pf_supported(h)) {
+    if ((rc = prefill_gemm(h, n - 1))) return rc;
+    if ((rc = set_pos_dev(h, h->pos + n - 1))) return rc;
+    h->pos -= n - 1;   // advanced with the last token below
+    first = n - 1;
+  }
+  for (int i = first; i < n; i++)
     if ((rc = launch_step(h, need_logits_last && i == n - 1))) return rc;
   uint32_t* res = (uint32_t*)(h->pinned + 448);
   if (need_logits_last) CKC(h, d2h(h, res, &h->st->next_token, 4));
@@ -958,10 +978,13 @@ int ck_io_bytes(ck_engine* h, uint64_t* h2d_bytes, uint64_t* d2h_bytes) {
   return CK_OK;
 }
 
+void pf_free(ck_engine* h);
+
 int ck_destroy(ck_engine* h) {
   if (!h) return CK_OK;
   cudaSetDevice(h->device);
   cudaStreamSynchronize(h->own);
+  pf_free(h);
   for (int m = 0; m < 2; m++) {
     if (h->gx_logits[m]) cudaGraphExecDestroy(h->gx_logits[m]);
     if (h->gx_prefill[m]) cudaGraphExecDestroy(h->gx_prefill[m]);
@@ -1217,3 +1240,4 @@ extern "C" int ck_matvec_noalloc(int ggml_type, const void* w_dev, size_t nbytes
 
 // Batched decode: kernels and scheduler over this engine's weights.
 #include "ck_batch.cuh"
+#include "ck_prefill.cuh"

@@ -102,7 +102,8 @@ int ck_destroy(ck_engine* h);
 int ck_run_token(ck_engine* h, uint32_t token, int need_logits, const ck_sampling* s, uint32_t* out_id);
 /* Prefill `n` prompt tokens without host round trips between tokens; the
  * last one computes logits when need_logits_last (runToken loop at
- * llama-wgsl-runtime.ts:281-288). */
+ * llama-wgsl-runtime.ts:281-288).  Long prompts go through the tensor-core
+ * prefill (ck_set_prefill_gemm). */
 int ck_prefill(ck_engine* h, const uint32_t* tokens, int n, int need_logits_last, const ck_sampling* s,
                uint32_t* out_id);
 /* Decode loop of generateLlamaWgsl (:291-307) kept on the device: feeds
@@ -129,6 +130,15 @@ int ck_set_stream(ck_engine* h, void* stream);
 /* Step implementation: 0 = one persistent cooperative kernel per token
  * (default), 1 = per-op kernels replayed from a CUDA graph. */
 int ck_set_mode(ck_engine* h, int mode);
+/* Tensor-core prefill.  No counterpart in the reference, which feeds a prompt
+ * token by token (llama-wgsl-runtime.ts:281-288); ck_prefill keeps that
+ * interface.  A ck_prefill of at least min_tokens + 1 ids (llama / qwen3
+ * graphs) runs all but the last id through the layers together as tcgen05
+ * GEMMs, `chunk` ids per pass (0: 1024, the largest), writing their K/V rows
+ * into the cache; the last id takes the single-token step.  Logits then match
+ * the token-by-token ones within the decode tolerance, not bit for bit.
+ * min_tokens 0 disables it; the default is 64. */
+int ck_set_prefill_gemm(ck_engine* h, int min_tokens, int chunk);
 /* Enqueue n greedy decode steps on the engine stream without synchronising
  * (benchmark/profiling use).  The first step reads the token already stored
  * at the current position; each step's argmax feeds the next. */
