@@ -162,6 +162,242 @@ __global__ void __launch_bounds__(CK_THREADS, 1) k_pattn(PfAttn P, const int* na
   }
 }
 
+// Causal attention of a block of query rows on the tensor cores (fp16 cache).
+//
+// A CTA takes one kv head and FA_ROWS query rows (token-major: row r is head
+// r % G of token qt0 + r / G).  Per chunk of FA_NP cache positions: S =
+// Q K^T in tensor memory (Q as two fp16 parts, the cache's fp16 K exact), an
+// online softmax over each row by the thread owning that accumulator lane
+// (positions outside [start, pos] of the row's token weigh nothing), the
+// output rows rescaled in tensor memory when the row maximum grows, P
+// written to shared memory as fp16 and O += P V on the tensor cores.  The
+// last chunk's O / l goes to out.  Operand tiles use the GEMM's K-major
+// layout (kmaj_off); V is stored transposed (rows = dims, K = positions).
+#define FA_ROWS 128
+#define FA_NP 128
+#define FA_THREADS 256
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,"
+      "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+      "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+      "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+      "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31]));
+}
+__device__ __forceinline__ void umma_f16(uint32_t tmem, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc) {
+  asm volatile("{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+               " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem),
+               "l"(da), "l"(db), "r"(idesc), "r"(acc));
+}
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void proxy_fence_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+template <int HD>
+constexpr int fa_smem() { return (HD / 64) * 3 * TC_TILE + 4 * TC_TILE + 64; }
+
+template <int HD>
+__global__ void __launch_bounds__(FA_THREADS, 1) k_fattn(PfAttn P, const int* nact, int* err) {
+  constexpr int DC = HD / 64;
+  extern __shared__ __align__(1024) uint8_t fsm[];
+  uint8_t* sQ = fsm;                        // [DC][hi|lo]: rows = query rows, K = dims
+  uint8_t* sK = sQ + DC * 2 * TC_TILE;      // [DC]: rows = positions, K = dims
+  uint8_t* sV = sK + DC * TC_TILE;          // [2]: rows = dims, K = positions
+  uint8_t* sP = sV + 2 * TC_TILE;           // [2]: rows = query rows, K = positions
+  uint64_t* bar = (uint64_t*)(sP + 2 * TC_TILE);   // [0] S ready, [1] O updated, [2] all MMAs done
+  __shared__ uint32_t s_tmem;
+  __shared__ int s_ok;
+  const int T = *nact;
+  const int G = P.heads / P.kvh, Bt = FA_ROWS / G;
+  const int kvh = blockIdx.y, qt0 = blockIdx.x * Bt;
+  if (qt0 >= T) return;
+  const int nq = min(Bt, T - qt0);
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int qd = P.heads * HD;
+  const int pos_hi = P.pos0 + qt0 + nq - 1;
+  const int pos_lo = P.pos0 + qt0;
+  const int start_lo = (P.window != 0 && pos_lo + 1 > P.window) ? pos_lo + 1 - P.window : 0;
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
+                 "r"(256));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    mbar_init(bar + 1, 1);
+    mbar_init(bar + 2, 1);
+    mbar_fence_init();
+    s_ok = 1;
+  }
+  // Q rows as two fp16 parts
+  for (int i = tid; i < FA_ROWS * (HD / 8); i += FA_THREADS) {
+    const int r = i / (HD / 8), d0 = (i % (HD / 8)) * 8;
+    float v[8];
+    if (r < nq * G) {
+      const float* src = P.qr + (size_t)(qt0 + r / G) * qd + (size_t)(kvh * G + r % G) * HD + d0;
+      const float4 a = *(const float4*)src, b = *(const float4*)(src + 4);
+      v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; e++) v[e] = 0.f;
+    }
+    __align__(16) __half hv[8], lv[8];
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+      hv[e] = __float2half_rn(v[e]);
+      lv[e] = __float2half_rn(v[e] - __half2float(hv[e]));
+    }
+    const uint32_t off = kmaj_off(r, d0 & 63);
+    *(uint4*)(sQ + ((d0 >> 6) * 2) * TC_TILE + off) = *(const uint4*)hv;
+    *(uint4*)(sQ + ((d0 >> 6) * 2 + 1) * TC_TILE + off) = *(const uint4*)lv;
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;");
+  const uint32_t tmem = s_tmem, tS = tmem, tO = tmem + 128;
+  // the row this thread owns (warps 0-3: accumulator lane = tid)
+  const int row = tid;
+  const bool rvalid = tid < FA_ROWS && row < nq * G;
+  const int rpos = P.pos0 + qt0 + row / G;
+  const int rstart = (P.window != 0 && rpos + 1 > P.window) ? rpos + 1 - P.window : 0;
+  const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
+  float m = -INFINITY, l = 0.f;
+  const int c_first = start_lo / FA_NP, c_last = pos_hi / FA_NP;
+  const uint32_t idS = (1u << 4) | ((uint32_t)(FA_NP >> 3) << 17) | ((uint32_t)(FA_ROWS >> 4) << 24);
+  const uint32_t idO = (1u << 4) | ((uint32_t)(HD >> 3) << 17) | ((uint32_t)(FA_ROWS >> 4) << 24);
+  bool ok = true;
+  for (int ci = c_first; ci <= c_last; ci++) {
+    const int j = ci - c_first, p0 = ci * FA_NP;
+    if (j > 0 && !mbar_wait_bounded(bar + 1, (j - 1) & 1, err)) ok = false;   // K, V and P free again
+    if (!__syncthreads_and(ok)) break;
+    for (int i = tid; i < FA_NP * (HD / 8); i += FA_THREADS) {
+      const int pp = i / (HD / 8), d0 = (i % (HD / 8)) * 8, p = p0 + pp;
+      uint4 kq = make_uint4(0, 0, 0, 0), vq = make_uint4(0, 0, 0, 0);
+      if (p >= start_lo && p <= pos_hi) {   // rows outside every query's range stay zero
+        const size_t o = ((size_t)kvh * P.ctx + p) * HD + d0;
+        kq = *(const uint4*)((const __half*)P.kc + o);
+        vq = *(const uint4*)((const __half*)P.vc + o);
+      }
+      *(uint4*)(sK + (d0 >> 6) * TC_TILE + kmaj_off(pp, d0 & 63)) = kq;
+      const __half* vh = (const __half*)&vq;
+#pragma unroll
+      for (int e = 0; e < 8; e++) *(__half*)(sV + (pp >> 6) * TC_TILE + kmaj_off(d0 + e, pp & 63)) = vh[e];
+    }
+    proxy_fence_smem();
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;");
+    if (tid == 0) {
+#pragma unroll
+      for (int c = 0; c < DC; c++)
+#pragma unroll
+        for (int kk = 0; kk < 4; kk++) {
+          const uint64_t db = umma_desc(smem_u32(sK + c * TC_TILE + kk * 4096), 128, 256);
+          umma_f16(tS, umma_desc(smem_u32(sQ + (2 * c) * TC_TILE + kk * 4096), 128, 256), db, idS,
+                   (c > 0 || kk > 0) ? 1u : 0u);
+          umma_f16(tS, umma_desc(smem_u32(sQ + (2 * c + 1) * TC_TILE + kk * 4096), 128, 256), db, idS, 1u);
+        }
+      umma_commit(bar);
+    }
+    if (tid < FA_ROWS) {
+      if (!mbar_wait_bounded(bar, j & 1, err)) ok = false;
+      asm volatile("tcgen05.fence::after_thread_sync;");
+      uint32_t r[32];
+      float mx = -INFINITY;
+      for (int cb = 0; cb < FA_NP; cb += 32) {
+        tmem_ld32(tS + lane_base + cb, r);
+#pragma unroll
+        for (int e = 0; e < 32; e++) {
+          const int p = p0 + cb + e;
+          if (rvalid && p >= rstart && p <= rpos) mx = fmaxf(mx, __uint_as_float(r[e]) * P.scale);
+        }
+      }
+      const float mn = fmaxf(m, mx);
+      float sum = 0.f;
+      for (int cb = 0; cb < FA_NP; cb += 32) {
+        tmem_ld32(tS + lane_base + cb, r);
+#pragma unroll
+        for (int e8 = 0; e8 < 32; e8 += 8) {
+          __align__(16) __half pv[8];
+#pragma unroll
+          for (int e = 0; e < 8; e++) {
+            const int p = p0 + cb + e8 + e;
+            const float pr = (rvalid && p >= rstart && p <= rpos) ? expf(__uint_as_float(r[e8 + e]) * P.scale - mn) : 0.f;
+            sum += pr;
+            pv[e] = __float2half_rn(pr);
+          }
+          *(uint4*)(sP + ((cb + e8) >> 6) * TC_TILE + kmaj_off(row, (cb + e8) & 63)) = *(const uint4*)pv;
+        }
+      }
+      const float c = m == -INFINITY ? 0.f : expf(m - mn);
+      l = l * c + sum;
+      m = mn;
+      if (j > 0 && __any_sync(0xffffffffu, c != 1.f)) {   // O rows hold earlier chunks: rescale in place
+        for (int db = 0; db < HD; db += 32) {
+          tmem_ld32(tO + lane_base + db, r);
+#pragma unroll
+          for (int e = 0; e < 32; e++) r[e] = __float_as_uint(__uint_as_float(r[e]) * c);
+          tmem_st32(tO + lane_base + db, r);
+        }
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+      }
+    }
+    proxy_fence_smem();
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    if (!__syncthreads_and(ok)) break;
+    asm volatile("tcgen05.fence::after_thread_sync;");
+    if (tid == 0) {
+#pragma unroll
+      for (int pc = 0; pc < 2; pc++)
+#pragma unroll
+        for (int kk = 0; kk < 4; kk++)
+          umma_f16(tO, umma_desc(smem_u32(sP + pc * TC_TILE + kk * 4096), 128, 256),
+                   umma_desc(smem_u32(sV + pc * TC_TILE + kk * 4096), 128, 256), idO,
+                   (j > 0 || pc > 0 || kk > 0) ? 1u : 0u);
+      umma_commit(bar + 1);
+    }
+  }
+  // one more commit: arrives once every MMA issued above has completed (also
+  // after an early exit, before shared and tensor memory are released)
+  if (tid == 0) umma_commit(bar + 2);
+  if (!mbar_wait_bounded(bar + 2, 0, err)) ok = false;
+  asm volatile("tcgen05.fence::after_thread_sync;");
+  if (!ok) s_ok = 0;
+  __syncthreads();
+  if (tid < FA_ROWS && s_ok) {
+    uint32_t r[32];
+    float* dst = P.out + (size_t)(qt0 + row / G) * qd + (size_t)(kvh * G + row % G) * HD;
+    const float inv = 1.f / l;
+    for (int db = 0; db < HD; db += 32) {
+      tmem_ld32(tO + lane_base + db, r);
+      if (rvalid) {
+#pragma unroll
+        for (int e = 0; e < 32; e += 4)
+          *(float4*)(dst + db + e) = make_float4(__uint_as_float(r[e]) * inv, __uint_as_float(r[e + 1]) * inv,
+                                                 __uint_as_float(r[e + 2]) * inv, __uint_as_float(r[e + 3]) * inv);
+      }
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;");
+  __syncthreads();
+  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(256));
+}
+
 // ---------------------------------------------------------------------------
 // Host side.
 
@@ -230,6 +466,9 @@ int pf_ensure(ck_engine* h) {
   cudaError_t e = cudaGetLastError();
   if (e == cudaSuccess) e = cudaMemsetAsync(p->d_err, 0, 16, h->stream);
   if (e == cudaSuccess) e = cudaFuncSetAttribute(k_bgemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(k_fattn<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, fa_smem<64>());
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(k_fattn<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, fa_smem<128>());
   if (e == cudaSuccess) e = cudaStreamSynchronize(h->stream);
   if (e != cudaSuccess) return bail(h->fail(CK_ECUDA, "prefill setup: %s", cudaGetErrorString(e)));
   tc_max_clusters(1);
@@ -238,13 +477,23 @@ int pf_ensure(ck_engine* h) {
   return CK_OK;
 }
 
+// K/V rows into the cache, then the attention: on the tensor cores for an
+// fp16 cache with head_dim 64 or 128, else one CTA per (token, kv head).
 template <int E>
-void pf_attn_launch(const PfAttn& a, bool f32, int grid, const int* nact, cudaStream_t s) {
+void pf_attn_launch(const PfAttn& a, bool f32, int T, const int* nact, int* err, cudaStream_t s) {
+  constexpr int hd = 32 * E;
+  const int grid = T * a.kvh;
   if (f32) {
     k_pkv<E, true><<<grid, CK_THREADS, 0, s>>>(a, nact);
     k_pattn<E, true><<<grid, CK_THREADS, 0, s>>>(a, nact);
+    return;
+  }
+  k_pkv<E, false><<<grid, CK_THREADS, 0, s>>>(a, nact);
+  if (hd == 64 || hd == 128) {
+    const int bt = FA_ROWS / (a.heads / a.kvh);
+    k_fattn<hd == 64 ? 64 : 128><<<dim3((T + bt - 1) / bt, a.kvh), FA_THREADS, fa_smem<hd == 64 ? 64 : 128>(), s>>>(
+        a, nact, err);
   } else {
-    k_pkv<E, false><<<grid, CK_THREADS, 0, s>>>(a, nact);
     k_pattn<E, false><<<grid, CK_THREADS, 0, s>>>(a, nact);
   }
 }
@@ -308,10 +557,9 @@ int prefill_gemm(ck_engine* h, int n) {
       a.pos0 = p0;
       a.eps = c.qk_norm_eps;
       a.scale = (float)(1.0 / sqrt((double)hd));   // ATTN_SCALE (:1711)
-      const int grid = T * c.kv_heads;
-      if (hd == 64) pf_attn_launch<2>(a, f32, grid, p->d_nact, s);
-      else if (hd == 128) pf_attn_launch<4>(a, f32, grid, p->d_nact, s);
-      else pf_attn_launch<8>(a, f32, grid, p->d_nact, s);
+      if (hd == 64) pf_attn_launch<2>(a, f32, T, p->d_nact, p->d_err, s);
+      else if (hd == 128) pf_attn_launch<4>(a, f32, T, p->d_nact, p->d_err, s);
+      else pf_attn_launch<8>(a, f32, T, p->d_nact, p->d_err, s);
       prep(BP_COPY, p->ao, nullptr, nullptr, qd);
       CKC(h, gemm(qd, {bseg(W.o, wt[3], p->x, p->x, H)}));
       prep(BP_NORM, p->x, nullptr, W.post_norm, H);

@@ -50,14 +50,21 @@ def _continue(eng, orc, nid, oid, steps, tol):
         oid = oid2
 
 
+SHAPES = {"hd64": {}, "hd128": {"head_dim": 128}, "g3": {"heads": 6, "kv_heads": 2}}
+
+
+@pytest.mark.parametrize("shape", list(SHAPES))
 @pytest.mark.parametrize("kv", ["float16", "float32"])
 @pytest.mark.parametrize("arch", ["llama", "qwen3"])
-def test_gemm_prefill_matches_oracle(tiny_dir, arch, kv):
-    path = tiny_model(tiny_dir, arch, "q4_k_m")
+def test_gemm_prefill_matches_oracle(tiny_dir, arch, kv, shape):
+    """200-token prompts: the attention spans two 128-position chunks (the
+    online softmax rescales across them); head_dim 64 and 128, and 3 query
+    heads per kv head (42-token query blocks)."""
+    path = tiny_model(tiny_dir, arch, "q4_k_m", **SHAPES[shape])
     loaded, V = _load(path, kv)
     eng = loaded.engine.dev
     eng.set_prefill_gemm(2)
-    toks = np.random.default_rng(3).integers(0, V, size=45).tolist()
+    toks = np.random.default_rng(3).integers(0, V, size=200).tolist()
     nid = eng.prefill(toks, True)
     assert eng.position == len(toks)
     orc = oracle.OracleModel(path, max_context=256)
@@ -74,16 +81,16 @@ def test_gemm_prefill_matches_oracle(tiny_dir, arch, kv):
 
 @pytest.mark.parametrize("arch", ["llama", "qwen3"])
 def test_gemm_prefill_chunks_and_offset(tiny_dir, arch):
-    """Two prefill calls (the second starts at position 20) in 16-token
+    """Two prefill calls (the second starts at position 20) in 48-token
     chunks, so attention reads rows written by earlier calls and chunks."""
     path = tiny_model(tiny_dir, arch, "q4_k_m")
     loaded, V = _load(path)
     eng = loaded.engine.dev
-    eng.set_prefill_gemm(2, 16)
-    toks = np.random.default_rng(9).integers(0, V, size=70).tolist()
+    eng.set_prefill_gemm(2, 48)
+    toks = np.random.default_rng(9).integers(0, V, size=170).tolist()
     eng.prefill(toks[:20], False)
     nid = eng.prefill(toks[20:], True)
-    assert eng.position == 70
+    assert eng.position == 170
     orc = oracle.OracleModel(path, max_context=256)
     for t in toks[:-1]:
         orc.run_token(t, False)
