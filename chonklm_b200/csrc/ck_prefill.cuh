@@ -270,12 +270,15 @@ __global__ void __launch_bounds__(FA_THREADS, 1) k_fattn(PfAttn P, const int* na
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;");
   const uint32_t tmem = s_tmem, tS = tmem, tO = tmem + 128;
-  // the row this thread owns (warps 0-3: accumulator lane = tid)
-  const int row = tid;
-  const bool rvalid = tid < FA_ROWS && row < nq * G;
-  const int rpos = P.pos0 + qt0 + row / G;
+  // the row this thread works on: accumulator lane rl = 32 * (warp % 4) + lane,
+  // column half warp / 4; both threads of a row keep its (m, l)
+  const int rl = 32 * (warp & 3) + (tid & 31), half = warp >> 2;
+  const bool rvalid = rl < nq * G;
+  const int rpos = P.pos0 + qt0 + rl / G;
   const int rstart = (P.window != 0 && rpos + 1 > P.window) ? rpos + 1 - P.window : 0;
   const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
+  const float sl2 = P.scale * 1.4426950408889634f;   // scores in log2 units: exp(x) = exp2(x log2 e)
+  __shared__ float red[2][FA_ROWS];
   float m = -INFINITY, l = 0.f;
   const int c_first = start_lo / FA_NP, c_last = pos_hi / FA_NP;
   const uint32_t idS = (1u << 4) | ((uint32_t)(FA_NP >> 3) << 17) | ((uint32_t)(FA_ROWS >> 4) << 24);
@@ -285,18 +288,57 @@ __global__ void __launch_bounds__(FA_THREADS, 1) k_fattn(PfAttn P, const int* na
     const int j = ci - c_first, p0 = ci * FA_NP;
     if (j > 0 && !mbar_wait_bounded(bar + 1, (j - 1) & 1, err)) ok = false;   // K, V and P free again
     if (!__syncthreads_and(ok)) break;
-    for (int i = tid; i < FA_NP * (HD / 8); i += FA_THREADS) {
-      const int pp = i / (HD / 8), d0 = (i % (HD / 8)) * 8, p = p0 + pp;
-      uint4 kq = make_uint4(0, 0, 0, 0), vq = make_uint4(0, 0, 0, 0);
-      if (p >= start_lo && p <= pos_hi) {   // rows outside every query's range stay zero
-        const size_t o = ((size_t)kvh * P.ctx + p) * HD + d0;
-        kq = *(const uint4*)((const __half*)P.kc + o);
-        vq = *(const uint4*)((const __half*)P.vc + o);
-      }
-      *(uint4*)(sK + (d0 >> 6) * TC_TILE + kmaj_off(pp, d0 & 63)) = kq;
-      const __half* vh = (const __half*)&vq;
+    {
+      // K: a 16-byte piece (8 dims of one position) per item, all of a
+      // thread's loads issued before its stores
+      constexpr int KI = FA_NP * (HD / 8) / FA_THREADS;
+      uint4 kq[KI];
 #pragma unroll
-      for (int e = 0; e < 8; e++) *(__half*)(sV + (pp >> 6) * TC_TILE + kmaj_off(d0 + e, pp & 63)) = vh[e];
+      for (int u = 0; u < KI; u++) {
+        const int i = tid + u * FA_THREADS, pp = i / (HD / 8), d0 = (i % (HD / 8)) * 8, p = p0 + pp;
+        kq[u] = make_uint4(0, 0, 0, 0);
+        if (p >= start_lo && p <= pos_hi)   // rows outside every query's range stay zero
+          kq[u] = *(const uint4*)((const __half*)P.kc + ((size_t)kvh * P.ctx + p) * HD + d0);
+      }
+#pragma unroll
+      for (int u = 0; u < KI; u++) {
+        const int i = tid + u * FA_THREADS, pp = i / (HD / 8), d0 = (i % (HD / 8)) * 8;
+        *(uint4*)(sK + (d0 >> 6) * TC_TILE + kmaj_off(pp, d0 & 63)) = kq[u];
+      }
+      // V transposed: an 8 x 8 block (8 positions x 8 dims) per item, turned
+      // in registers into 8 rows of 8 positions, written in a lane-rotated
+      // order (the 8 rows of a block share their bank offset)
+      constexpr int VI = (FA_NP / 8) * (HD / 8);
+      if (tid < VI) {
+        const int pg = tid / (HD / 8), c = tid % (HD / 8);
+        __align__(16) __half in[8][8];
+#pragma unroll
+        for (int r = 0; r < 8; r++) {
+          const int p = p0 + 8 * pg + r;
+          uint4 v = make_uint4(0, 0, 0, 0);
+          if (p >= start_lo && p <= pos_hi)
+            v = *(const uint4*)((const __half*)P.vc + ((size_t)kvh * P.ctx + p) * HD + 8 * c);
+          *(uint4*)in[r] = v;
+        }
+        uint4 o[8];
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+          __align__(16) __half out[8];
+#pragma unroll
+          for (int r = 0; r < 8; r++) out[r] = in[r][e];
+          o[e] = *(const uint4*)out;
+        }
+        uint8_t* vt = sV + ((8 * pg) >> 6) * TC_TILE;
+#pragma unroll
+        for (int e0 = 0; e0 < 8; e0++) {
+          const int e = (e0 + tid) & 7;
+          uint4 v = o[0];
+#pragma unroll
+          for (int q = 1; q < 8; q++)
+            if (e == q) v = o[q];   // selects, not an indexed (local memory) array
+          *(uint4*)(vt + kmaj_off(8 * c + e, (8 * pg) & 63)) = v;
+        }
+      }
     }
     proxy_fence_smem();
     asm volatile("tcgen05.fence::before_thread_sync;");
@@ -314,41 +356,45 @@ __global__ void __launch_bounds__(FA_THREADS, 1) k_fattn(PfAttn P, const int* na
         }
       umma_commit(bar);
     }
-    if (tid < FA_ROWS) {
+    {
+      // two threads per row: warp w reads accumulator lanes 32*(w%4).. and
+      // columns 64*(w/4)..+63 of S (held in registers), the row's maximum
+      // and sum combined through shared memory; scores in log2 units
       if (!mbar_wait_bounded(bar, j & 1, err)) ok = false;
       asm volatile("tcgen05.fence::after_thread_sync;");
-      uint32_t r[32];
+      uint32_t r0[32], r1[32];
+      tmem_ld32(tS + lane_base + 64 * half, r0);
+      tmem_ld32(tS + lane_base + 64 * half + 32, r1);
+      // this row's positions inside the chunk: [vlo, vhi] relative to p0
+      const int vlo = max(rstart - p0, 64 * half), vhi = min(rpos - p0, 64 * half + 63);
       float mx = -INFINITY;
-      for (int cb = 0; cb < FA_NP; cb += 32) {
-        tmem_ld32(tS + lane_base + cb, r);
 #pragma unroll
-        for (int e = 0; e < 32; e++) {
-          const int p = p0 + cb + e;
-          if (rvalid && p >= rstart && p <= rpos) mx = fmaxf(mx, __uint_as_float(r[e]) * P.scale);
-        }
+      for (int e = 0; e < 32; e++) {
+        const int c0 = 64 * half + e, c1 = c0 + 32;
+        if (rvalid && c0 >= vlo && c0 <= vhi) mx = fmaxf(mx, __uint_as_float(r0[e]) * sl2);
+        if (rvalid && c1 >= vlo && c1 <= vhi) mx = fmaxf(mx, __uint_as_float(r1[e]) * sl2);
       }
-      const float mn = fmaxf(m, mx);
+      red[half][rl] = mx;
+      __syncthreads();
+      const float mn = fmaxf(m, fmaxf(red[0][rl], red[1][rl]));
       float sum = 0.f;
-      for (int cb = 0; cb < FA_NP; cb += 32) {
-        tmem_ld32(tS + lane_base + cb, r);
 #pragma unroll
-        for (int e8 = 0; e8 < 32; e8 += 8) {
-          __align__(16) __half pv[8];
+      for (int e8 = 0; e8 < 64; e8 += 8) {
+        __align__(16) __half pv[8];
 #pragma unroll
-          for (int e = 0; e < 8; e++) {
-            const int p = p0 + cb + e8 + e;
-            const float pr = (rvalid && p >= rstart && p <= rpos) ? expf(__uint_as_float(r[e8 + e]) * P.scale - mn) : 0.f;
-            sum += pr;
-            pv[e] = __float2half_rn(pr);
-          }
-          *(uint4*)(sP + ((cb + e8) >> 6) * TC_TILE + kmaj_off(row, (cb + e8) & 63)) = *(const uint4*)pv;
+        for (int e = 0; e < 8; e++) {
+          const int ce = e8 + e, cc = 64 * half + ce;
+          const float sv = __uint_as_float(ce < 32 ? r0[ce] : r1[ce - 32]);
+          const float pr = (rvalid && cc >= vlo && cc <= vhi) ? exp2f(sv * sl2 - mn) : 0.f;
+          sum += pr;
+          pv[e] = __float2half_rn(pr);
         }
+        *(uint4*)(sP + half * TC_TILE + kmaj_off(rl, e8)) = *(const uint4*)pv;
       }
-      const float c = m == -INFINITY ? 0.f : expf(m - mn);
-      l = l * c + sum;
-      m = mn;
+      const float c = m == -INFINITY ? 0.f : exp2f(m - mn);
       if (j > 0 && __any_sync(0xffffffffu, c != 1.f)) {   // O rows hold earlier chunks: rescale in place
-        for (int db = 0; db < HD; db += 32) {
+        uint32_t r[32];
+        for (int db = half * (HD / 2); db < (half + 1) * (HD / 2); db += 32) {
           tmem_ld32(tO + lane_base + db, r);
 #pragma unroll
           for (int e = 0; e < 32; e++) r[e] = __float_as_uint(__uint_as_float(r[e]) * c);
@@ -356,6 +402,11 @@ __global__ void __launch_bounds__(FA_THREADS, 1) k_fattn(PfAttn P, const int* na
         }
         asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       }
+      __syncthreads();   // red[] read by both threads of the row before it is reused
+      red[half][rl] = sum;
+      __syncthreads();
+      l = l * c + red[0][rl] + red[1][rl];
+      m = mn;
     }
     proxy_fence_smem();
     asm volatile("tcgen05.fence::before_thread_sync;");
@@ -379,11 +430,11 @@ __global__ void __launch_bounds__(FA_THREADS, 1) k_fattn(PfAttn P, const int* na
   asm volatile("tcgen05.fence::after_thread_sync;");
   if (!ok) s_ok = 0;
   __syncthreads();
-  if (tid < FA_ROWS && s_ok) {
+  if (s_ok) {
     uint32_t r[32];
-    float* dst = P.out + (size_t)(qt0 + row / G) * qd + (size_t)(kvh * G + row % G) * HD;
+    float* dst = P.out + (size_t)(qt0 + rl / G) * qd + (size_t)(kvh * G + rl % G) * HD;
     const float inv = 1.f / l;
-    for (int db = 0; db < HD; db += 32) {
+    for (int db = half * (HD / 2); db < (half + 1) * (HD / 2); db += 32) {
       tmem_ld32(tO + lane_base + db, r);
       if (rvalid) {
 #pragma unroll
