@@ -272,6 +272,10 @@ def main():
     ap.add_argument("--mode", type=int, default=0, help="0 megakernel, 1 per-phase CUDA graph")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-matvec", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the prefill comparison")
+    ap.add_argument("--prefill-profile", type=int, default=0, metavar="N",
+                    help="profiling run for ncu: N tensor-core prefills of the config's prompt (the first one "
+                         "formats the operand tiles), then exit")
     ap.add_argument("--profile", type=int, default=0, metavar="N",
                     help="profiling run for ncu: prefill the prompt (megakernel), decode N tokens in --mode, "
                          "print nothing else")
@@ -342,7 +346,7 @@ def main():
     spec, prompt_len, gen, sampling = CONFIGS[args.config]
     from chonklm_b200 import _lib
     from chonklm_b200.registry import ModelDef
-    from chonklm_b200.runtime import generateLlamaWgsl, loadLlamaWgslModel
+    from chonklm_b200.runtime import generateLlamaWgsl, loadLlamaWgslModel, resetLlamaWgslConversation
     from chonklm_b200.synth import SPECS
     import numpy as np
 
@@ -363,6 +367,15 @@ def main():
     if sampling:
         samp, _ = _lib.make_sampling(sampling["temperature"], sampling["topP"], sampling["topK"], 1.0,
                                      sampling["seed"], 0)
+    if args.prefill_profile:
+        eng.set_prefill_gemm(64)
+        for _ in range(args.prefill_profile):
+            eng.truncate(0)
+            nid = eng.prefill(prompt, True, samp)
+        print(json.dumps({"prefill_profile": args.config, "prefills": args.prefill_profile, "tokens": prompt_len,
+                          "next_id": int(nid)}), flush=True)
+        loaded.engine.dispose()
+        return
     if args.profile:
         eng.set_mode(0)
         nid = eng.prefill(prompt, True, samp)
@@ -427,6 +440,35 @@ def main():
             e2e_times.append(dt)
             e2e_io.append((io1[0] - io0[0], io1[1] - io0[1]))
         assert len(res["ids"]) == gen, len(res["ids"])
+
+    # ---- prefill: tensor-core path against token by token -------------------------
+    prefill = None
+    if rank == 0 and not args.no_prefill:
+        def time_prefill(min_tokens):
+            eng.set_prefill_gemm(min_tokens)
+            eng.truncate(0)
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            eng.prefill(prompt, True, samp)        # returns after the device finished
+            return 1000.0 * (time.perf_counter() - t0)
+        pf_ms = [time_prefill(64) for _ in range(4)][1:]   # the first call formats the operand tiles
+        tbt_ms = time_prefill(0)
+        eng.set_prefill_gemm(64)
+        # the reference's tok/s: generated ids over the time from before the
+        # prefill (llama-wgsl-runtime.ts:266, :312), fresh conversation each run
+        ref_def = []
+        for _ in range(2):
+            resetLlamaWgslConversation(loaded)
+            t0 = time.perf_counter()
+            res = generateLlamaWgsl(loaded, prompt, opts)
+            ref_def.append(len(res["ids"]) / (time.perf_counter() - t0))
+        prefill = {"tokens": prompt_len, "tensor_core_ms": round(statistics.median(pf_ms), 2),
+                   "tensor_core_tok_per_s": round(prompt_len / (statistics.median(pf_ms) / 1000.0), 1),
+                   "token_by_token_ms": round(tbt_ms, 2),
+                   "generate_tok_per_s_from_before_prefill": round(max(ref_def), 2),
+                   "note": "ck_prefill host-synchronised wall time; all but the last prompt id through "
+                           "tcgen05 GEMMs + flash attention (prompts >= 64 ids)"}
+        eng.truncate(prompt_len)
 
     # ---- reduce over ranks ------------------------------------------------------
     vals = torch.tensor([tot_ms, sum(e2e_times)], dtype=torch.float64, device="cuda")
@@ -495,6 +537,7 @@ def main():
             "cpu_baseline": cpu,
             "matvec": mv,
             "batched": batched,
+            "prefill": prefill,
             "clocks": clk.summary(),
             "gpu_launches": int(launches_per_token * gen * args.steps),
             "decode_ids_head": ids0[:2],
