@@ -290,19 +290,30 @@ __global__ void __launch_bounds__(FA_THREADS, 1) k_fattn(PfAttn P, const int* na
     if (!__syncthreads_and(ok)) break;
     {
       // K: a 16-byte piece (8 dims of one position) per item, all of a
-      // thread's loads issued before its stores
+      // thread's loads issued before its stores.  A warp takes 8 positions x
+      // 4 consecutive pieces: 64 contiguous bytes per position row read, and
+      // its 16-byte stores spread over every bank (the 8 positions of a core
+      // matrix are 16 bytes apart)
       constexpr int KI = FA_NP * (HD / 8) / FA_THREADS;
       uint4 kq[KI];
+      auto kitem = [&](int u, int& pp, int& d0) {
+        const int i = tid + u * FA_THREADS, ln = i & 31, w = i >> 5;
+        pp = (w % (FA_NP / 8)) * 8 + (ln & 7);
+        d0 = ((w / (FA_NP / 8)) * 4 + (ln >> 3)) * 8;
+      };
 #pragma unroll
       for (int u = 0; u < KI; u++) {
-        const int i = tid + u * FA_THREADS, pp = i / (HD / 8), d0 = (i % (HD / 8)) * 8, p = p0 + pp;
+        int pp, d0;
+        kitem(u, pp, d0);
+        const int p = p0 + pp;
         kq[u] = make_uint4(0, 0, 0, 0);
         if (p >= start_lo && p <= pos_hi)   // rows outside every query's range stay zero
           kq[u] = *(const uint4*)((const __half*)P.kc + ((size_t)kvh * P.ctx + p) * HD + d0);
       }
 #pragma unroll
       for (int u = 0; u < KI; u++) {
-        const int i = tid + u * FA_THREADS, pp = i / (HD / 8), d0 = (i % (HD / 8)) * 8;
+        int pp, d0;
+        kitem(u, pp, d0);
         *(uint4*)(sK + (d0 >> 6) * TC_TILE + kmaj_off(pp, d0 & 63)) = kq[u];
       }
       // V transposed: an 8 x 8 block (8 positions x 8 dims) per item, turned
