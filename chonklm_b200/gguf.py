@@ -279,7 +279,7 @@ def _pack_string(s: str) -> bytes:
     return struct.pack("<Q", len(b)) + b
 
 
-def _pack_value(v: Any, vt: Optional[int] = None) -> Tuple[int, bytes]:
+def _pack_value(v: Any, vt: Optional[int] = None, item_t: Optional[int] = None) -> Tuple[int, bytes]:
     if vt is None:
         if isinstance(v, bool):
             vt = VT_BOOL
@@ -301,7 +301,8 @@ def _pack_value(v: Any, vt: Optional[int] = None) -> Tuple[int, bytes]:
         return vt, _pack_string(v)
     if vt == VT_ARR:
         items = list(v)
-        item_t = _pack_value(items[0])[0] if items else VT_U32
+        if item_t is None:
+            item_t = _pack_value(items[0])[0] if items else VT_U32
         body = b"".join(_pack_value(it, item_t)[1] for it in items)
         return vt, struct.pack("<IQ", item_t, len(items)) + body
     raise ValueError(vt)
@@ -311,14 +312,17 @@ def write_gguf(path: str, kv: Dict[str, Any], tensors: List[Tuple[str, List[int]
                alignment: int = 32) -> None:
     """Write a GGUF v3 file.
 
-    kv: metadata; a value may be `(value, value_type)` to force the type.
+    kv: metadata; a value may be `(value, value_type)` to force the type, or
+    `(items, VT_ARR, item_type)` for an array of a given item type.
     tensors: `(name, ggml_shape, ggml_type, payload_bytes)`; ggml_shape[0] is
     the contiguous dimension (row length), as in the GGUF spec.
     """
     head = bytearray()
     head += struct.pack("<IIQQ", GGUF_MAGIC, 3, len(tensors), len(kv))
     for key, val in kv.items():
-        if isinstance(val, tuple):
+        if isinstance(val, tuple) and len(val) == 3:
+            vt, body = _pack_value(val[0], val[1], val[2])
+        elif isinstance(val, tuple):
             vt, body = _pack_value(val[0], val[1])
         else:
             vt, body = _pack_value(val)

@@ -25,7 +25,7 @@ from typing import Dict, List, Optional, Tuple
 import numpy as np
 import torch
 
-from .gguf import GGML_TYPE, VT_F32, VT_U32, write_gguf
+from .gguf import GGML_TYPE, VT_ARR, VT_BOOL, VT_F32, VT_I32, VT_STR, VT_U32, write_gguf
 from .quant import quantize
 
 
@@ -49,6 +49,7 @@ class SynthSpec:
     norm_init: str = "ones"    # "ones" | "random" (1 + 0.1 N) -- random catches index bugs
     tied: bool = True
     overrides: Dict[str, int] = field(default_factory=dict)  # tensor-name -> ggml type
+    tokenizer: bool = False    # write a SentencePiece vocabulary (tokenizer.synthetic_vocab)
 
 
 SPECS: Dict[str, SynthSpec] = {
@@ -142,6 +143,19 @@ def _metadata(spec: SynthSpec, name: str, seed: int) -> Dict[str, object]:
     }
     if a == "gemma3":
         kv["gemma3.attention.sliding_window"] = (spec.sliding_window, VT_U32)
+    if spec.tokenizer:
+        from .tokenizer import synthetic_vocab
+        toks, scores, types = synthetic_vocab(spec.vocab)
+        kv["tokenizer.ggml.model"] = ("llama", VT_STR)
+        kv["tokenizer.ggml.tokens"] = toks
+        kv["tokenizer.ggml.scores"] = ([float(x) for x in scores], VT_ARR, VT_F32)
+        kv["tokenizer.ggml.token_type"] = ([int(x) for x in types], VT_ARR, VT_I32)
+        kv["tokenizer.ggml.bos_token_id"] = (toks.index("<bos>"), VT_U32)
+        kv["tokenizer.ggml.eos_token_id"] = (toks.index("<eos>"), VT_U32)
+        kv["tokenizer.ggml.unknown_token_id"] = (toks.index("<unk>"), VT_U32)
+        kv["tokenizer.ggml.padding_token_id"] = (toks.index("<pad>"), VT_U32)
+        kv["tokenizer.ggml.add_bos_token"] = (True, VT_BOOL)
+        kv["tokenizer.ggml.add_space_prefix"] = (False, VT_BOOL)
     return kv
 
 

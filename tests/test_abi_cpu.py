@@ -33,6 +33,26 @@ def test_struct_layouts_match():
     assert samp == ctypes.sizeof(_lib.ck_sampling)
 
 
+def test_ts_binding_layouts_match_the_abi():
+    """The Bun FFI binding (chonklm_b200/ts/llama-cuda-runtime.ts) packs
+    ck_model_cfg and ck_sampling by hand: its offset tables and sizes must be
+    the C layout (no JavaScript runtime here to run the file itself)."""
+    src = open(os.path.join(os.path.dirname(_lib.__file__), "ts", "llama-cuda-runtime.ts")).read()
+
+    def table(name):
+        body = re.search(name + r" = \{(.*?)\} as const", src, re.S).group(1)
+        return {k: int(v) for k, v in re.findall(r"(\w+): (\d+)", body)}
+
+    for cls, tname, sname in [(_lib.ck_model_cfg, "CK_CFG_LAYOUT", "CK_CFG_SIZE"),
+                              (_lib.ck_sampling, "CK_SAMPLING_LAYOUT", "CK_SAMPLING_SIZE")]:
+        t = table(tname)
+        assert t == {f[0]: getattr(cls, f[0]).offset for f in cls._fields_}
+        assert int(re.search(sname + r" = (\d+)", src).group(1)) == ctypes.sizeof(cls)
+    # every symbol the binding opens is declared in the header
+    opened = set(re.findall(r"^  (ck_[a-z_]+): \{", src, re.M))
+    assert opened and opened <= set(declared())
+
+
 def test_library_is_sm100a_and_in_tree():
     from chonklm_b200 import build
     assert os.path.dirname(_lib.lib()._name) == os.path.dirname(build.LIB)
