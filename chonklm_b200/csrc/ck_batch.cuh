@@ -79,12 +79,23 @@ struct BAttn {
   float eps, scale;
 };
 
+// Programmatic dependent launch: the step's kernels are launched with
+// programmatic stream serialization, so a kernel's CTAs may start while its
+// predecessor is still running.  Each kernel waits (griddepcontrol.wait:
+// the predecessor grid has completed and its writes are visible) before it
+// reads or writes anything the step's kernels share, then lets its own
+// successor launch.  Without the launch attribute both are no-ops.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---------------------------------------------------------------------------
 // Embedding of every active entry's token (GGUF_*_EMBEDDING_WGSL, :2615-2866).
 __global__ void __launch_bounds__(256) k_bembed(const uint8_t* w, Lay L, float scale, BStep st, float* x, int H,
                                                 int vocab, int* err) {
   const int t = blockIdx.x;
   if (t >= *st.nact) return;
+  pdl_wait();
+  pdl_launch();
   uint32_t token = st.tok[t];
   if (token >= (uint32_t)vocab) {
     if (threadIdx.x == 0) atomicOr(err, CK_DERR_TOKEN);
@@ -191,6 +202,8 @@ __global__ void __launch_bounds__(CK_THREADS) k_bprep(BPrep p, BStep st, BXh q) 
   constexpr int PER = CK_KMAX / CK_THREADS;
   const int t = blockIdx.x;
   if (t >= *st.nact) return;
+  pdl_wait();
+  pdl_launch();
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int k = p.k, nch = tc_nch(k);
   const float* a = p.a + (size_t)t * p.lda;
@@ -295,22 +308,34 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_bgemm_tc(BGemm G, BStep st, B
   asm volatile("tcgen05.fence::after_thread_sync;");
   const uint32_t tmem = s_tmem;
   bool ok = true;
+  // instruction descriptor: fp32 D, fp16 A and B, both K-major, M = 128, N
+  const uint32_t idesc = (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(TC_ROWS >> 4) << 24);
+  const uint8_t* a_src = (const uint8_t*)s_wt + (size_t)rt * nch * 2 * TC_TILE;
+  const uint8_t* b_src = (const uint8_t*)xh.xt + (size_t)blockIdx.y * nch * 2 * TC_TILE;
+  // chunk c's four tiles complete on its stage's barrier: the weight pair
+  // (with the stage's expect_tx) and the token pair may be issued apart
+  auto issue_a = [&](int c) {
+    const int sg = (c - c_lo) % TC_STAGES;
+    uint8_t* dst = tsm + sg * 4 * TC_TILE;
+    mbar_expect_tx(full + sg, 4 * TC_TILE);
+    bulk_g2s(dst, a_src + (size_t)c * 2 * TC_TILE, TC_TILE, full + sg);
+    bulk_g2s(dst + TC_TILE, a_src + ((size_t)c * 2 + 1) * TC_TILE, TC_TILE, full + sg);
+  };
+  auto issue_b = [&](int c) {
+    const int sg = (c - c_lo) % TC_STAGES;
+    uint8_t* dst = tsm + sg * 4 * TC_TILE;
+    bulk_g2s(dst + 2 * TC_TILE, b_src + (size_t)c * 2 * TC_TILE, TC_TILE, full + sg);
+    bulk_g2s(dst + 3 * TC_TILE, b_src + ((size_t)c * 2 + 1) * TC_TILE, TC_TILE, full + sg);
+  };
+  int issued = c_lo;
+  // the weights are read-only: their first stages load while the previous
+  // kernel may still run; the token tiles wait for it
+  if (tid == 0)
+    for (; issued < c_lo + TC_STAGES && issued < c_hi; issued++) issue_a(issued);
+  pdl_wait();
+  pdl_launch();
   if (tid == 0) {
-    // instruction descriptor: fp32 D, fp16 A and B, both K-major, M = 128, N
-    const uint32_t idesc = (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(TC_ROWS >> 4) << 24);
-    const uint8_t* a_src = (const uint8_t*)s_wt + (size_t)rt * nch * 2 * TC_TILE;
-    const uint8_t* b_src = (const uint8_t*)xh.xt + (size_t)blockIdx.y * nch * 2 * TC_TILE;
-    auto issue = [&](int c) {
-      const int sg = (c - c_lo) % TC_STAGES;
-      uint8_t* dst = tsm + sg * 4 * TC_TILE;
-      mbar_expect_tx(full + sg, 4 * TC_TILE);
-      bulk_g2s(dst, a_src + (size_t)c * 2 * TC_TILE, TC_TILE, full + sg);
-      bulk_g2s(dst + TC_TILE, a_src + ((size_t)c * 2 + 1) * TC_TILE, TC_TILE, full + sg);
-      bulk_g2s(dst + 2 * TC_TILE, b_src + (size_t)c * 2 * TC_TILE, TC_TILE, full + sg);
-      bulk_g2s(dst + 3 * TC_TILE, b_src + ((size_t)c * 2 + 1) * TC_TILE, TC_TILE, full + sg);
-    };
-    int issued = c_lo;
-    for (; issued < c_lo + TC_STAGES && issued < c_hi; issued++) issue(issued);
+    for (int c = c_lo; c < issued; c++) issue_b(c);
     int c = c_lo;
     for (; c < c_hi; c++) {
       const int j = c - c_lo, sg = j % TC_STAGES;
@@ -339,7 +364,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_bgemm_tc(BGemm G, BStep st, B
                    : "memory");
       if (issued < c_hi) {   // refill this stage once its MMAs have read it
         if (!mbar_wait_bounded(empty + sg, (j / TC_STAGES) & 1, err)) { ok = false; c++; break; }
-        issue(issued++);
+        issue_a(issued);
+        issue_b(issued++);
       }
     }
     if (!ok) {   // copies still in flight must land before the CTA's shared memory is reused
@@ -474,6 +500,8 @@ __global__ void __launch_bounds__(CK_THREADS, 1) k_battn(BAttn P, BStep st) {
   constexpr int hd = 32 * E;
   const int t = blockIdx.x / P.kvh, kvh = blockIdx.x % P.kvh;
   if (t >= *st.nact) return;
+  pdl_wait();
+  pdl_launch();
   __shared__ SmemAt s;
   __shared__ int sbt[256];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -593,6 +621,8 @@ __global__ void __launch_bounds__(CK_THREADS, 1) k_battn(BAttn P, BStep st) {
 __global__ void __launch_bounds__(CK_THREADS) k_bargmax(const float* logits, int V, BStep st, uint32_t* ids) {
   const int t = blockIdx.x;
   if (t >= *st.nact) return;
+  pdl_wait();
+  pdl_launch();
   __shared__ float sv[CK_WARPS];
   __shared__ uint32_t si[CK_WARPS];
   float v = -3.402823e38f;
@@ -733,7 +763,9 @@ int tc_splits(int units, int nch) {
   return best;
 }
 
-cudaError_t tc_launch(BGemm& G, BStep st, BXh xh, int* err, int ttiles, cudaStream_t s) {
+// pdl: launch with programmatic stream serialization (the kernel may start
+// while its predecessor runs; it waits before touching shared data)
+cudaError_t tc_launch(BGemm& G, BStep st, BXh xh, int* err, int ttiles, cudaStream_t s, bool pdl = false) {
   const int tiles = G.tile0[G.nseg];
   G.splits = tc_splits(tiles * ttiles, tc_nch(G.k));
   cudaLaunchConfig_t cfg;
@@ -742,14 +774,38 @@ cudaError_t tc_launch(BGemm& G, BStep st, BXh xh, int* err, int ttiles, cudaStre
   cfg.blockDim = dim3(TC_THREADS);
   cfg.dynamicSmemBytes = TC_SMEM;
   cfg.stream = s;
-  cudaLaunchAttribute at[1];
-  at[0].id = cudaLaunchAttributeClusterDimension;
-  at[0].val.clusterDim.x = G.splits;
-  at[0].val.clusterDim.y = 1;
-  at[0].val.clusterDim.z = 1;
+  cudaLaunchAttribute at[2];
+  int na = 0;
+  if (G.splits > 1) {
+    at[na].id = cudaLaunchAttributeClusterDimension;
+    at[na].val.clusterDim.x = G.splits;
+    at[na].val.clusterDim.y = 1;
+    at[na].val.clusterDim.z = 1;
+    na++;
+  }
+  if (pdl) {
+    at[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[na].val.programmaticStreamSerializationAllowed = 1;
+    na++;
+  }
   cfg.attrs = at;
-  cfg.numAttrs = G.splits > 1 ? 1 : 0;
+  cfg.numAttrs = na;
   return cudaLaunchKernelEx(&cfg, k_bgemm_tc, G, st, xh, err);
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*k)(KArgs...), dim3 grid, dim3 block, cudaStream_t s, Args... args) {
+  cudaLaunchConfig_t cfg;
+  memset(&cfg, 0, sizeof cfg);
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k, args...);
 }
 
 int bgemm_launch(ck_batch* b, cudaStream_t s, int k, std::initializer_list<BSeg> segs) {
@@ -764,7 +820,7 @@ int bgemm_launch(ck_batch* b, cudaStream_t s, int k, std::initializer_list<BSeg>
   }
   G.tile0[G.nseg] = tiles;
   // token tiles past T return at once
-  CKB(b, tc_launch(G, bstep(b), b->xh, b->d_err, (b->max_seqs + TC_NT - 1) / TC_NT, s));
+  CKB(b, tc_launch(G, bstep(b), b->xh, b->d_err, (b->max_seqs + TC_NT - 1) / TC_NT, s, true));
   return CK_OK;
 }
 
@@ -784,7 +840,7 @@ void bprep(ck_batch* b, cudaStream_t s, int kind, const float* a, const float* b
            int lda) {
   BPrep p;
   p.kind = kind; p.a = a; p.b = bb; p.w = w; p.eps = eps; p.k = k; p.lda = lda;
-  k_bprep<<<b->max_seqs, CK_THREADS, 0, s>>>(p, bstep(b), b->xh);
+  launch_pdl(k_bprep, dim3(b->max_seqs), dim3(CK_THREADS), s, p, bstep(b), b->xh);
 }
 
 // The whole step on stream s (captured once into a graph).
@@ -793,7 +849,8 @@ int batch_enqueue(ck_batch* b, cudaStream_t s) {
   const ck_model_cfg& c = h->cfg;
   const int H = c.hidden, hd = c.head_dim, qd = c.heads * hd, kvd = c.kv_heads * hd, I = c.intermediate;
   const size_t pool = (size_t)b->n_blocks * c.kv_heads * CK_BLK * hd;
-  k_bembed<<<b->max_seqs, 256, 0, s>>>(h->emb.dev, h->emb.L, c.embedding_scale, bstep(b), b->x, H, c.vocab, b->d_err);
+  CKB(b, launch_pdl(k_bembed, dim3(b->max_seqs), dim3(256), s, (const uint8_t*)h->emb.dev, h->emb.L,
+                    c.embedding_scale, bstep(b), b->x, H, c.vocab, b->d_err));
   for (int i = 0; i < c.layers; i++) {
     const LayerW& W = h->L[i];
     __half* const* wt = &b->wt[(size_t)7 * i];
@@ -814,9 +871,9 @@ int batch_enqueue(ck_batch* b, cudaStream_t s) {
     a.eps = c.qk_norm_eps;
     a.scale = (float)(1.0 / sqrt((double)hd));   // ATTN_SCALE (:1711)
     const int grid = b->max_seqs * c.kv_heads;
-    if (hd == 64) k_battn<2><<<grid, CK_THREADS, 0, s>>>(a, bstep(b));
-    else if (hd == 128) k_battn<4><<<grid, CK_THREADS, 0, s>>>(a, bstep(b));
-    else k_battn<8><<<grid, CK_THREADS, 0, s>>>(a, bstep(b));
+    if (hd == 64) CKB(b, launch_pdl(k_battn<2>, dim3(grid), dim3(CK_THREADS), s, a, bstep(b)));
+    else if (hd == 128) CKB(b, launch_pdl(k_battn<4>, dim3(grid), dim3(CK_THREADS), s, a, bstep(b)));
+    else CKB(b, launch_pdl(k_battn<8>, dim3(grid), dim3(CK_THREADS), s, a, bstep(b)));
     bprep(b, s, BP_COPY, b->ao, nullptr, nullptr, 0.f, qd, qd);
     if ((rc = bgemm_launch(b, s, qd, {bseg(W.o, wt[3], b->x, b->x, H)}))) return rc;
     bprep(b, s, BP_NORM, b->x, nullptr, W.post_norm, c.norm_eps, H, H);
@@ -828,7 +885,8 @@ int batch_enqueue(ck_batch* b, cudaStream_t s) {
   bprep(b, s, BP_NORM, b->x, nullptr, h->final_norm, c.norm_eps, H, H);
   int rc = bgemm_launch(b, s, H, {bseg(h->head, b->wt[(size_t)7 * c.layers], b->logits, nullptr, c.vocab)});
   if (rc) return rc;
-  k_bargmax<<<b->max_seqs, CK_THREADS, 0, s>>>(b->logits, c.vocab, bstep(b), b->d_ids);
+  CKB(b, launch_pdl(k_bargmax, dim3(b->max_seqs), dim3(CK_THREADS), s, (const float*)b->logits, c.vocab, bstep(b),
+                    b->d_ids));
   CKB(b, cudaGetLastError());
   return CK_OK;
 }
