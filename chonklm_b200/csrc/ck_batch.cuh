@@ -11,14 +11,15 @@
 // * KV cache: paged, fp16, blocks of CK_BLK positions from one pool per layer
 //   ([layer][K|V][block][kv_head][CK_BLK][head_dim]), each sequence holding a
 //   block table; its blocks are reserved when it joins.
-// * Each matvec becomes a dequantizing GEMM over the step's tokens (k_bgemm):
-//   a warp owns one weight row, unpacks its 32-weight units once and dots
-//   them with every token of a token tile staged in shared memory; the
-//   per-token partial sums of the 32 lanes are combined by a butterfly
-//   reduce-scatter (31 shuffles for 32 tokens instead of 5 per token).
-// * x is quantized per token and per 32-group exactly as in the
-//   single-sequence prologue (k_bprep); attention is one CTA per
-//   (token, kv head) over that token's sequence (k_battn).
+// * Each matvec becomes a tensor-core GEMM over the step's tokens
+//   (k_bgemm_tc, below) on the weights' fp16 operand tiles, made once per
+//   batch; the per-token prologue (k_bprep: RMS norm or SiLU gate) writes x
+//   as operand tiles too, and attention (one CTA per token and kv head over
+//   that token's sequence, k_battn) writes its output straight into the o
+//   projection's tiles.
+// * The step's kernels are launched with programmatic dependent launch: each
+//   may start while its predecessor runs and waits before touching shared
+//   data (pdl_wait).
 // * The step's kernels read the active count T from device memory, so one
 //   CUDA graph, captured at the first step, serves every T.
 // Supported: llama / qwen3 architectures with an fp16 KV cache, greedy
@@ -74,7 +75,7 @@ struct BAttn {
   const float *qw, *kw;       // QK-norm weights or null
   __half *kc, *vc;            // this layer's pools [block][kv_head][CK_BLK][hd]
   const float* inv_freq;      // [hd/2]
-  float* out;                 // [T][heads*hd]
+  BXh xo;                     // the o projection's operand tiles: out written as x_hi / x_lo, scale 1
   int heads, kvh, hd, interleaved, window;
   float eps, scale;
 };
@@ -608,12 +609,20 @@ __global__ void __launch_bounds__(CK_THREADS, 1) k_battn(BAttn P, BStep st) {
     s.hl[tid] = L;
   }
   __syncthreads();
+  // the output goes straight into the o projection's operand tiles (the
+  // COPY prologue's split: x_hi = fp16(x), x_lo = fp16(x - x_hi))
+  const int nch = tc_nch(qd);
   for (int i = tid; i < G * hd; i += CK_THREADS) {
     const int gg = i / hd, d = i % hd;
     float A = 0.f;
     for (int w = gg * wpg; w < gg * wpg + wpg; w++) A += s.wacc[w * CK_HDMAX + d] * s.wf[w];
-    P.out[(size_t)t * qd + (size_t)(kvh * G + gg) * hd + d] = A / s.hl[gg];
+    const float o = A / s.hl[gg];
+    const int col = (kvh * G + gg) * hd + d;
+    const __half h = __float2half_rn(o);
+    P.xo.xt[tc_index(t, col, nch, 0)] = h;
+    P.xo.xt[tc_index(t, col, nch, 1)] = __float2half_rn(o - __half2float(h));
   }
+  if (tid == 0 && kvh == 0) P.xo.xs[t] = 1.0f;
 }
 
 // Greedy id of every active entry: ARGMAX_STAGE1/2 rules (NaN never wins,
@@ -657,8 +666,7 @@ struct ck_batch {
   uint32_t* d_tok = nullptr;
   int *d_slot = nullptr, *d_pos = nullptr, *d_nact = nullptr, *d_btab = nullptr, *d_err = nullptr;
   uint32_t* d_ids = nullptr;
-  float *x = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *ao = nullptr, *g = nullptr, *u = nullptr,
-        *logits = nullptr;
+  float *x = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *g = nullptr, *u = nullptr, *logits = nullptr;
   BXh xh{};
   std::vector<__half*> wt;    // operand tiles per weight: layer-major q k v o gate up down, then the head
   uint8_t* pin = nullptr;     // pinned staging: tok | slot | pos | nact | ids | err
@@ -865,7 +873,7 @@ int batch_enqueue(ck_batch* b, cudaStream_t s) {
     a.kc = b->kv + (size_t)(2 * i) * pool;
     a.vc = b->kv + (size_t)(2 * i + 1) * pool;
     a.inv_freq = h->inv_freq + (size_t)i * (hd / 2);
-    a.out = b->ao;
+    a.xo = b->xh;
     a.heads = c.heads; a.kvh = c.kv_heads; a.hd = hd; a.interleaved = c.rope_interleaved;
     a.window = (int)c.layer_window[i];
     a.eps = c.qk_norm_eps;
@@ -874,7 +882,6 @@ int batch_enqueue(ck_batch* b, cudaStream_t s) {
     if (hd == 64) CKB(b, launch_pdl(k_battn<2>, dim3(grid), dim3(CK_THREADS), s, a, bstep(b)));
     else if (hd == 128) CKB(b, launch_pdl(k_battn<4>, dim3(grid), dim3(CK_THREADS), s, a, bstep(b)));
     else CKB(b, launch_pdl(k_battn<8>, dim3(grid), dim3(CK_THREADS), s, a, bstep(b)));
-    bprep(b, s, BP_COPY, b->ao, nullptr, nullptr, 0.f, qd, qd);
     if ((rc = bgemm_launch(b, s, qd, {bseg(W.o, wt[3], b->x, b->x, H)}))) return rc;
     bprep(b, s, BP_NORM, b->x, nullptr, W.post_norm, c.norm_eps, H, H);
     rc = bgemm_launch(b, s, H, {bseg(W.gate, wt[4], b->g, nullptr, I), bseg(W.up, wt[5], b->u, nullptr, I)});
@@ -932,7 +939,7 @@ int ck_batch_create(ck_engine* h, int max_seqs, int kv_blocks, ck_batch** out) {
       (rc = balloc(b, &b->d_err, 16)) || (rc = balloc(b, &b->d_ids, S * 4)) ||
       (rc = balloc(b, &b->x, S * H * 4)) || (rc = balloc(b, &b->q, S * qd * 4)) ||
       (rc = balloc(b, &b->k, S * kvd * 4)) || (rc = balloc(b, &b->v, S * kvd * 4)) ||
-      (rc = balloc(b, &b->ao, S * qd * 4)) || (rc = balloc(b, &b->g, S * I * 4)) ||
+      (rc = balloc(b, &b->g, S * I * 4)) ||
       (rc = balloc(b, &b->u, S * I * 4)) || (rc = balloc(b, &b->logits, S * c.vocab * 4)) ||
       (rc = balloc(b, &b->xh.xt, tc_bytes(max_seqs, CK_KMAX))) || (rc = balloc(b, &b->xh.xs, S * 4)))
     return bail(rc);

@@ -7,7 +7,8 @@
 // batched path's kernels:
 //
 // * every matmul is the tcgen05 GEMM over the chunk's tokens (k_bgemm_tc on
-//   the weights' operand tiles, the norm / copy / SiLU prologue in k_bprep);
+//   the weights' operand tiles, the norm / SiLU prologue in k_bprep; the
+//   attention kernels write the o projection's operand tiles themselves);
 // * k_pkv applies the QK-norm and RoPE of each (token, kv head) and writes
 //   the token's K and V rows into the engine's own cache at its position
 //   (the ropeStore / qkNormRopeStore rows, :1467-1545), so that every row of
@@ -32,7 +33,7 @@ struct PfAttn {
   void *kc, *vc;              // this layer's cache [kv_head][ctx][hd]
   const float* inv_freq;      // [hd/2]
   float* qr;                  // [T][heads*hd] q after norm + rope
-  float* out;                 // [T][heads*hd]
+  BXh xo;                     // the o projection's operand tiles: out written as x_hi / x_lo, scale 1
   int heads, kvh, hd, ctx, window, interleaved, pos0;
   float eps, scale;
 };
@@ -154,12 +155,18 @@ __global__ void __launch_bounds__(CK_THREADS, 1) k_pattn(PfAttn P, const int* na
     hl[tid] = L;
   }
   __syncthreads();
+  const int nch = tc_nch(qd);
   for (int i = tid; i < G * hd; i += CK_THREADS) {
     const int gg = i / hd, d = i % hd;
     float A = 0.f;
     for (int w = gg * wpg; w < gg * wpg + wpg; w++) A += wacc[w * CK_HDMAX + d] * wf[w];
-    P.out[(size_t)t * qd + (size_t)(kvh * G + gg) * hd + d] = A / hl[gg];
+    const float o = A / hl[gg];
+    const int col = (kvh * G + gg) * hd + d;
+    const __half h = __float2half_rn(o);
+    P.xo.xt[tc_index(t, col, nch, 0)] = h;
+    P.xo.xt[tc_index(t, col, nch, 1)] = __float2half_rn(o - __half2float(h));
   }
+  if (tid == 0 && kvh == 0) P.xo.xs[t] = 1.0f;
 }
 
 // Causal attention of a block of query rows on the tensor cores (fp16 cache).
@@ -442,18 +449,30 @@ __global__ void __launch_bounds__(FA_THREADS, 1) k_fattn(PfAttn P, const int* na
   if (!ok) s_ok = 0;
   __syncthreads();
   if (s_ok) {
+    // O / l straight into the o projection's operand tiles (8 dims = one
+    // 16-byte row of a core matrix per store)
     uint32_t r[32];
-    float* dst = P.out + (size_t)(qt0 + rl / G) * qd + (size_t)(kvh * G + rl % G) * HD;
+    const int tok = qt0 + rl / G, col0 = (kvh * G + rl % G) * HD, nch = tc_nch(qd);
     const float inv = 1.f / l;
     for (int db = half * (HD / 2); db < (half + 1) * (HD / 2); db += 32) {
       tmem_ld32(tO + lane_base + db, r);
       if (rvalid) {
 #pragma unroll
-        for (int e = 0; e < 32; e += 4)
-          *(float4*)(dst + db + e) = make_float4(__uint_as_float(r[e]) * inv, __uint_as_float(r[e + 1]) * inv,
-                                                 __uint_as_float(r[e + 2]) * inv, __uint_as_float(r[e + 3]) * inv);
+        for (int e8 = 0; e8 < 32; e8 += 8) {
+          __align__(16) __half hv[8], lv[8];
+#pragma unroll
+          for (int e = 0; e < 8; e++) {
+            const float o = __uint_as_float(r[e8 + e]) * inv;
+            hv[e] = __float2half_rn(o);
+            lv[e] = __float2half_rn(o - __half2float(hv[e]));
+          }
+          *(uint4*)(P.xo.xt + tc_index(tok, col0 + db + e8, nch, 0)) = *(const uint4*)hv;
+          *(uint4*)(P.xo.xt + tc_index(tok, col0 + db + e8, nch, 1)) = *(const uint4*)lv;
+        }
       }
     }
+    if (tid == 0 && kvh == 0)
+      for (int t = 0; t < nq; t++) P.xo.xs[qt0 + t] = 1.0f;
   }
   asm volatile("tcgen05.fence::before_thread_sync;");
   __syncthreads();
@@ -469,8 +488,7 @@ struct ck_prefill_state {
   int chunk = 0;              // tokens per pass (<= PF_CHUNK_MAX)
   int* d_nact = nullptr;
   int* d_err = nullptr;
-  float *x = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *qr = nullptr, *ao = nullptr, *g = nullptr,
-        *u = nullptr;
+  float *x = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *qr = nullptr, *g = nullptr, *u = nullptr;
   BXh xh{};
 };
 
@@ -511,7 +529,7 @@ int pf_ensure(ck_engine* h) {
   if ((rc = palloc(h, p, &p->d_nact, 16)) || (rc = palloc(h, p, &p->d_err, 16)) ||
       (rc = palloc(h, p, &p->x, T * H * 4)) || (rc = palloc(h, p, &p->q, T * qd * 4)) ||
       (rc = palloc(h, p, &p->k, T * kvd * 4)) || (rc = palloc(h, p, &p->v, T * kvd * 4)) ||
-      (rc = palloc(h, p, &p->qr, T * qd * 4)) || (rc = palloc(h, p, &p->ao, T * qd * 4)) ||
+      (rc = palloc(h, p, &p->qr, T * qd * 4)) ||
       (rc = palloc(h, p, &p->g, T * I * 4)) || (rc = palloc(h, p, &p->u, T * I * 4)) ||
       (rc = palloc(h, p, &p->xh.xt, tc_bytes((int)T, CK_KMAX))) || (rc = palloc(h, p, &p->xh.xs, T * 4)))
     return bail(rc);
@@ -612,7 +630,7 @@ int prefill_gemm(ck_engine* h, int n) {
       a.vc = h->kv + (size_t)(2 * i + 1) * per;
       a.inv_freq = h->inv_freq + (size_t)i * (hd / 2);
       a.qr = p->qr;
-      a.out = p->ao;
+      a.xo = p->xh;
       a.heads = c.heads; a.kvh = c.kv_heads; a.hd = hd; a.ctx = c.context_length;
       a.window = (int)c.layer_window[i];
       a.interleaved = c.rope_interleaved;
@@ -622,7 +640,6 @@ int prefill_gemm(ck_engine* h, int n) {
       if (hd == 64) pf_attn_launch<2>(a, f32, T, p->d_nact, p->d_err, s);
       else if (hd == 128) pf_attn_launch<4>(a, f32, T, p->d_nact, p->d_err, s);
       else pf_attn_launch<8>(a, f32, T, p->d_nact, p->d_err, s);
-      prep(BP_COPY, p->ao, nullptr, nullptr, qd);
       CKC(h, gemm(qd, {bseg(W.o, wt[3], p->x, p->x, H)}));
       prep(BP_NORM, p->x, nullptr, W.post_norm, H);
       CKC(h, gemm(H, {bseg(W.gate, wt[4], p->g, nullptr, I), bseg(W.up, wt[5], p->u, nullptr, I)}));
