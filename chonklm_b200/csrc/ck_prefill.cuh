@@ -40,58 +40,74 @@ struct PfAttn {
 
 __global__ void k_set_int(int* p, int v) { *p = v; }
 
-// QK-norm + RoPE of one (token, kv head): the G query heads into qr, the K
-// and V rows into the cache at the token's position (the decode step's
-// attention prologue, one token per CTA).
+// QK-norm + RoPE, one warp per (token, head row): the query heads into qr,
+// the K rows (rounded as the cache stores them) and V rows into the cache at
+// the token's position (the decode step's attention prologue).  Lane l holds
+// dims l, l + 32, ...: the sum of squares runs in the decode prologue's
+// order, a split-layout pair (d, d + hd/2) sits in one lane, an interleaved
+// pair (2d, 2d + 1) in neighbouring lanes.
+#define PKV_WARPS 8
 template <int E, bool F32>
-__global__ void __launch_bounds__(CK_THREADS) k_pkv(PfAttn P, const int* nact) {
+__global__ void __launch_bounds__(32 * PKV_WARPS) k_pkv(PfAttn P, const int* nact) {
   constexpr int hd = 32 * E;
-  const int t = blockIdx.x / P.kvh, kvh = blockIdx.x % P.kvh;
+  const int lane = threadIdx.x & 31;
+  const int units = P.heads + 2 * P.kvh;                  // q heads, k heads, v heads
+  const int gw = blockIdx.x * PKV_WARPS + (threadIdx.x >> 5);
+  const int t = gw / units, u = gw % units;
   if (t >= *nact) return;
-  __shared__ SmemAt s;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int G = P.heads / P.kvh, qd = P.heads * hd, kvd = P.kvh * hd;
+  const int qd = P.heads * hd, kvd = P.kvh * hd;
   const int pos = P.pos0 + t;
-  for (int d = tid; d < (hd >> 1); d += CK_THREADS) {
-    float sn, cn;
-    sincosf((float)pos * P.inv_freq[d], &sn, &cn);
-    s.cs[d] = make_float2(cn, sn);
-  }
-  const float* qsrc = P.q + (size_t)t * qd + (size_t)kvh * G * hd;
-  for (int i = tid; i < G * hd; i += CK_THREADS) s.raw[i] = qsrc[i];
-  for (int d = tid; d < hd; d += CK_THREADS) {
-    s.kvw[0][d] = P.k[(size_t)t * kvd + (size_t)kvh * hd + d];
-    s.kvw[1][d] = P.v[(size_t)t * kvd + (size_t)kvh * hd + d];
-    if (P.kw) s.kvw[3][d] = P.kw[d];
-    if (P.qw) s.kvw[2][d] = P.qw[d];
-  }
-  __syncthreads();
-  if (P.qw) {
-    for (int gg = warp; gg < G + 1; gg += CK_WARPS) {
-      const float* src = gg < G ? s.raw + gg * hd : s.kvw[0];
+  const bool isq = u < P.heads, isk = !isq && u < P.heads + P.kvh;
+  const int head = isq ? u : isk ? u - P.heads : u - P.heads - P.kvh;
+  const float* src = isq ? P.q + (size_t)t * qd + (size_t)head * hd
+                         : (isk ? P.k : P.v) + (size_t)t * kvd + (size_t)head * hd;
+  float v[E];
+#pragma unroll
+  for (int e = 0; e < E; e++) v[e] = src[lane + 32 * e];
+  if (isq || isk) {
+    const float* w = isq ? P.qw : P.kw;
+    if (w) {
       float ss = 0.f;
-      for (int d = lane; d < hd; d += 32) ss += src[d] * src[d];
-      ss = warp_sum(ss);
-      if (lane == 0) s.inv[gg] = rms_inv(ss, hd, P.eps);
+#pragma unroll
+      for (int e = 0; e < E; e++) ss += v[e] * v[e];
+      const float inv = rms_inv(warp_sum(ss), hd, P.eps);
+#pragma unroll
+      for (int e = 0; e < E; e++) v[e] = (v[e] * inv) * w[lane + 32 * e];
     }
-    __syncthreads();
-  }
-  for (int gg = 0; gg < G; gg++)
-    rope_head(s.raw + gg * hd, P.qw ? s.kvw[2] : nullptr, P.qw ? s.inv[gg] : 1.f, s.qs + gg * hd, hd, P.interleaved,
-              s.cs, tid, CK_THREADS);
-  rope_head(s.kvw[0], P.kw ? s.kvw[3] : nullptr, P.kw ? s.inv[G] : 1.f, s.kst, hd, P.interleaved, s.cs, tid,
-            CK_THREADS);
-  __syncthreads();
-  float* qdst = P.qr + (size_t)t * qd + (size_t)kvh * G * hd;
-  for (int i = tid; i < G * hd; i += CK_THREADS) qdst[i] = s.qs[i];
-  const size_t cb = ((size_t)kvh * P.ctx + pos) * hd;
-  for (int d = tid; d < hd; d += CK_THREADS) {
-    if (F32) {
-      ((float*)P.kc)[cb + d] = s.kst[d];
-      ((float*)P.vc)[cb + d] = s.kvw[1][d];
+    float o[E];
+    if (P.interleaved) {
+#pragma unroll
+      for (int e = 0; e < E; e++) {
+        const int d = lane + 32 * e;
+        const float other = __shfl_xor_sync(0xffffffffu, v[e], 1);
+        float sn, cn;
+        sincosf((float)pos * P.inv_freq[d >> 1], &sn, &cn);
+        o[e] = (d & 1) ? other * sn + v[e] * cn : v[e] * cn - other * sn;
+      }
     } else {
-      ((__half*)P.kc)[cb + d] = __float2half_rn(s.kst[d]);
-      ((__half*)P.vc)[cb + d] = __float2half_rn(s.kvw[1][d]);
+#pragma unroll
+      for (int e = 0; e < E / 2; e++) {
+        float sn, cn;
+        sincosf((float)pos * P.inv_freq[lane + 32 * e], &sn, &cn);
+        const float a = v[e], b = v[e + E / 2];
+        o[e] = a * cn - b * sn;
+        o[e + E / 2] = a * sn + b * cn;
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < E; e++) v[e] = o[e];
+  }
+  if (isq) {
+    float* dst = P.qr + (size_t)t * qd + (size_t)head * hd;
+#pragma unroll
+    for (int e = 0; e < E; e++) dst[lane + 32 * e] = v[e];
+  } else {
+    const size_t cb = ((size_t)head * P.ctx + pos) * hd;
+    void* cache = isk ? P.kc : P.vc;
+#pragma unroll
+    for (int e = 0; e < E; e++) {
+      if (F32) ((float*)cache)[cb + lane + 32 * e] = v[e];
+      else ((__half*)cache)[cb + lane + 32 * e] = __float2half_rn(v[e]);
     }
   }
 }
@@ -563,12 +579,13 @@ template <int E>
 void pf_attn_launch(const PfAttn& a, bool f32, int T, const int* nact, int* err, cudaStream_t s) {
   constexpr int hd = 32 * E;
   const int grid = T * a.kvh;
+  const int pkv_grid = (T * (a.heads + 2 * a.kvh) + PKV_WARPS - 1) / PKV_WARPS;
   if (f32) {
-    k_pkv<E, true><<<grid, CK_THREADS, 0, s>>>(a, nact);
+    k_pkv<E, true><<<pkv_grid, 32 * PKV_WARPS, 0, s>>>(a, nact);
     k_pattn<E, true><<<grid, CK_THREADS, 0, s>>>(a, nact);
     return;
   }
-  k_pkv<E, false><<<grid, CK_THREADS, 0, s>>>(a, nact);
+  k_pkv<E, false><<<pkv_grid, 32 * PKV_WARPS, 0, s>>>(a, nact);
   if (hd == 64 || hd == 128) {
     const int bt = FA_ROWS / (a.heads / a.kvh);
     k_fattn<hd == 64 ? 64 : 128><<<dim3((T + bt - 1) / bt, a.kvh), FA_THREADS, fa_smem<hd == 64 ? 64 : 128>(), s>>>(
