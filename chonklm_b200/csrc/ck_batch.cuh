@@ -363,8 +363,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_bgemm_tc(BGemm G, BStep st, B
       asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                        smem_u32(empty + sg))
                    : "memory");
-      if (issued < c_hi) {   // refill this stage once its MMAs have read it
-        if (!mbar_wait_bounded(empty + sg, (j / TC_STAGES) & 1, err)) { ok = false; c++; break; }
+      // refill the previous chunk's stage (its MMAs ran ahead of this
+      // chunk's, which stay queued on the tensor pipe meanwhile)
+      if (j >= 1 && issued < c_hi) {
+        const int pj = j - 1;
+        if (!mbar_wait_bounded(empty + pj % TC_STAGES, (pj / TC_STAGES) & 1, err)) { ok = false; c++; break; }
         issue_a(issued);
         issue_b(issued++);
       }
