@@ -64,14 +64,16 @@ def peaks():
         return 6650.0, "fallback"
 
 
-def model_file(spec_name: str, rank: int, world: int, barrier) -> str:
+def model_file(spec_name: str, rank: int, world: int, barrier, tokenizer: bool = False) -> str:
+    import dataclasses
     from chonklm_b200.synth import SPECS, write_synthetic_gguf
     d = os.environ.get("CK_BENCH_DIR", "/tmp/chonk_bench")
     os.makedirs(d, exist_ok=True)
-    path = os.path.join(d, f"{spec_name}.gguf")
+    path = os.path.join(d, f"{spec_name}{'-tok' if tokenizer else ''}.gguf")
     if rank == 0 and not os.path.exists(path):
         t = time.time()
-        write_synthetic_gguf(SPECS[spec_name], path + ".tmp", seed=0)
+        spec = dataclasses.replace(SPECS[spec_name], tokenizer=True) if tokenizer else SPECS[spec_name]
+        write_synthetic_gguf(spec, path + ".tmp", seed=0)
         os.replace(path + ".tmp", path)
         log(f"[bench] wrote {path} in {time.time() - t:.1f}s")
     barrier()
@@ -220,6 +222,46 @@ def matvec_report(path, peak):
     return out
 
 
+def run_gemma_text(args, rank: int, world: int, barrier, local: int, dist) -> None:
+    """Config 4's model through the text API (gemma-runtime.ts interface,
+    chonklm_b200.gemma_runtime): a fixed user message, 256 sampled ids
+    (temperature 1, top-k 64, top-p 0.95), tok/s as generateGemma reports it
+    (generated ids over the time of the call, prompt prefill included)."""
+    import torch
+    from chonklm_b200.gemma_runtime import generateGemma, loadGemmaModel, resetGemmaConversation
+    from chonklm_b200.registry import ModelDef
+    torch.cuda.set_device(local)
+    path = model_file("gemma3-270m", rank, world, barrier, tokenizer=True)
+    loaded = loadGemmaModel(ModelDef(id="gemma3-270m-text", label="gemma3-270m-text", runtime="gemma-webgpu",
+                                     maxContext=MAX_CONTEXT["gemma3-270m"], gguf=path), device=local)
+    history = [{"role": "user", "content": "please answer the question about the world model " * 4}]
+    opts = {"maxNewTokens": 256, "temperature": 1.0}
+    vals = []
+    for i in range(args.warmup + args.steps):
+        resetGemmaConversation(loaded)
+        r = generateGemma(loaded, history, opts)
+        if i >= args.warmup:
+            vals.append((r["tokensPerSec"], r["generatedTokens"]))
+    barrier()
+    tps = torch.tensor([statistics.median(v[0] for v in vals)], dtype=torch.float64, device="cuda")
+    if dist is not None:
+        dist.all_reduce(tps, op=dist.ReduceOp.SUM)
+    if rank == 0:
+        v = float(tps[0])
+        print(json.dumps({"metric": "gemma text API tok/s (generateGemma, 256 sampled ids)", "value": round(v, 2),
+                          "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                          "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                          "dtype": "int8-dp4a/fp32", "data": "synthetic",
+                          "config": {"workload": "gemma3-270m-text",
+                                     "prompt_ids": len(loaded.engine.history_ids) - len(loaded.engine.last_reply_ids),
+                                     "generated": 256, "sampling": "T 1.0, top-k 64, top-p 0.95, Philox seed 0",
+                                     "parallelism": f"replicas x{world}"},
+                          "e2e": {"value": round(v, 2), "unit": "tok/s", "h2d_bytes_per_step": None,
+                                  "d2h_bytes_per_step": None},
+                          "generated_last": vals[-1][1]}), flush=True)
+    loaded.engine.dispose()
+
+
 def run_batched(rank: int, world: int, barrier, local: int, warmup: int, max_steps: int = 0):
     """Config 5 on this rank's share of the sequences: every step advances
     each running sequence one position (ck_batch_step, host-synchronised);
@@ -267,7 +309,8 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", default="qwen3-0.6b-q4_k_m", choices=list(CONFIGS) + ["smollm2-135m-batched"])
+    ap.add_argument("--config", default="qwen3-0.6b-q4_k_m",
+                    choices=list(CONFIGS) + ["smollm2-135m-batched", "gemma3-270m-text"])
     ap.add_argument("--no-batched", action="store_true", help="skip the batched (config 5) summary")
     ap.add_argument("--mode", type=int, default=0, help="0 megakernel, 1 per-phase CUDA graph")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -307,6 +350,18 @@ def main():
                                   "WebGPU runtime is unavailable on this box"}), flush=True)
         else:
             run_reference(args, args.config, rank, world, barrier)
+        if dist is not None:
+            dist.destroy_process_group()
+        return
+
+    if args.config == "gemma3-270m-text":
+        if args.impl == "reference":
+            if rank == 0:
+                print(json.dumps({"impl": "reference", "unavailable":
+                                  "the reference's gemma-webgpu engine is a third-party WebGPU package, absent "
+                                  "here; no WebGPU on this box"}), flush=True)
+        else:
+            run_gemma_text(args, rank, world, barrier, local, dist)
         if dist is not None:
             dist.destroy_process_group()
         return
