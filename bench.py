@@ -262,6 +262,24 @@ def run_gemma_text(args, rank: int, world: int, barrier, local: int, dist) -> No
     loaded.engine.dispose()
 
 
+def shard(n: int, rank: int, world: int):
+    """Sequences of the batched workload on this rank: i mod world == rank
+    (independent sequences, no collective on the data path)."""
+    return [i for i in range(n) if i % world == rank]
+
+
+def aggregate(dist, seconds: float, generated: float, device: str = "cuda"):
+    """Whole-job figures over ranks: the slowest rank's time, the sum of the
+    tokens all ranks generated (every rank takes the same collective steps)."""
+    import torch
+    t = torch.tensor([seconds], dtype=torch.float64, device=device)
+    g = torch.tensor([generated], dtype=torch.float64, device=device)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.all_reduce(g, op=dist.ReduceOp.SUM)
+    return float(t[0]), float(g[0])
+
+
 def run_batched(rank: int, world: int, barrier, local: int, warmup: int, max_steps: int = 0):
     """Config 5 on this rank's share of the sequences: every step advances
     each running sequence one position (ck_batch_step, host-synchronised);
@@ -277,7 +295,7 @@ def run_batched(rank: int, world: int, barrier, local: int, warmup: int, max_ste
     loaded = loadLlamaWgslModel(ModelDef(id="batched", label="batched", vocab=S.vocab, maxContext=B["max_context"],
                                          gguf=path, eosIds=[]), device=local)
     eng = loaded.engine.dev
-    mine = [i for i in range(B["seqs"]) if i % world == rank]
+    mine = shard(B["seqs"], rank, world)
     prompts = {i: np.random.default_rng(1 + i).integers(0, S.vocab, size=B["prompt"]).tolist() for i in mine}
     # warm-up: the same shapes on a throw-away batch (kernel loading, graph capture)
     wb = _lib.Batch(eng, max_seqs=len(mine))
@@ -369,14 +387,7 @@ def main():
     if args.config == "smollm2-135m-batched":
         torch.cuda.set_device(local)
         gen, dt, steps, fed = run_batched(rank, world, barrier, local, args.warmup, args.profile)
-        vals = torch.tensor([dt, float(gen)], dtype=torch.float64, device="cuda")
-        if dist is not None:
-            t = vals[:1].clone()
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            g = vals[1:].clone()
-            dist.all_reduce(g, op=dist.ReduceOp.SUM)
-            vals = torch.cat([t, g])
-        max_s, total_gen = float(vals[0]), float(vals[1])
+        max_s, total_gen = aggregate(dist, dt, float(gen))
         if rank == 0:
             B = BATCHED
             print(json.dumps({
