@@ -564,7 +564,9 @@ __global__ void __launch_bounds__(CK_THREADS, 1) k_battn(BAttn P, BStep st) {
       return (((size_t)sbt[p >> 4] * P.kvh + kvh) * CK_BLK + (p & (CK_BLK - 1))) * hd + lane * E;
     };
     // CH positions of the warp per round, all their rows requested before
-    // the round's math (a round trip per round, not per position)
+    // the round's math (a round trip per round, not per position); deeper
+    // rounds (16 positions at head_dim 64) measured slower: more registers,
+    // one CTA per SM instead of two
     constexpr int CH = E <= 4 ? 8 : 4;
     for (int p0 = start + sub; p0 < pos; p0 += CH * wpg) {
       KvRow<E, false> kr[CH], vr[CH];
