@@ -51,12 +51,14 @@ MATMUL_TOL = 2e-5   # relative: x and w each split into two fp16 parts (~22 bits
 
 
 @pytest.mark.parametrize("t,k,n,T", [(12, 1024, 300, 1), (14, 512, 129, 37), (8, 576, 260, 130), (6, 576, 200, 16),
-                                     (7, 64, 130, 5), (12, 256, 6272, 3), (14, 256, 20000, 200)])
+                                     (7, 64, 130, 5), (12, 256, 6272, 3), (14, 256, 20000, 200),
+                                     (8, 576, 300, 600), (12, 1024, 260, 520), (14, 256, 20000, 600)])
 def test_tensor_core_matmul(t, k, n, T):
     """The batched path's tcgen05 GEMM (prologue split of x + dequant split of
     W, three MMAs per step) against fp64 over the oracle's dequantized
     weights: single token, partial and multiple 128-token tiles, partial
-    128-row tiles, every block type."""
+    128-row tiles, every block type, K split over clusters, and two token
+    tiles per CTA (>= 4 token tiles, the last CTA holding only one)."""
     import torch
     from chonklm_b200 import _lib
     from chonklm_b200.quant import quantize
