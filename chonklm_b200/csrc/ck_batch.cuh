@@ -68,6 +68,18 @@ struct BGemm {
   int k;
   int tile0[4];          // first 128-row tile of each segment; tile0[nseg] = total
   int splits;            // K slices per row tile (the cluster size, <= 8 and <= the K chunks)
+  // epilogue of a residual-stream GEMM (one segment): also write the next RMS
+  // norm's operand tiles, out * nw, and each row tile's sum of squares of out
+  // per token (nssq[token][row tile], ntiles row tiles); off when nw is null
+  const float* nw;
+  __half* nxt;
+  float* nssq;
+  int ntiles;
+  // prologue scale of each token from those partial sums:
+  // 1 / sqrt(sum / k + eps) (RMS_NORM_WGSL); xh.xs when ssq_in is null
+  const float* ssq_in;
+  int ssq_tiles;
+  float eps;
 };
 
 struct BAttn {
@@ -270,6 +282,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_bgemm_tc(BGemm G, BStep st, B
   __shared__ uint32_t s_tmem;
   __shared__ int s_ok;
   __shared__ float s_xs[TC_NT];
+  __shared__ float s_red[4][TC_NT];             // norm epilogue: per-warp-quarter sums of squares
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int T = *st.nact;
   const int t0 = blockIdx.y * TC_NT;
@@ -380,10 +393,21 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_bgemm_tc(BGemm G, BStep st, B
                      smem_u32(done))
                  : "memory");
   }
-  // while thread 0 runs the K loop: the tokens' output scales
+  // while thread 0 runs the K loop: the tokens' output scales (the row
+  // tiles' partial sums in tile order, or the prologue's scale)
   if (tid >= TC_THREADS - TC_NT) {
     const int n = tid - (TC_THREADS - TC_NT);
-    s_xs[n] = n < nt ? xh.xs[t0 + n] : 0.f;
+    float v = 0.f;
+    if (n < nt) {
+      if (G.ssq_in) {
+        float sum = 0.f;
+        for (int q = 0; q < G.ssq_tiles; q++) sum += G.ssq_in[(size_t)(t0 + n) * G.ssq_tiles + q];
+        v = rms_inv(sum, G.k, G.eps);
+      } else {
+        v = xh.xs[t0 + n];
+      }
+    }
+    s_xs[n] = v;
   }
   __syncthreads();
   if (!mbar_wait_bounded(done, 0, err)) ok = false;
@@ -414,12 +438,40 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_bgemm_tc(BGemm G, BStep st, B
         for (int j = 0; j < 16; j++) av[j] = 0.f;
       }
       asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+      float yv[16];
+#pragma unroll
+      for (int j = 0; j < 16; j++) yv[j] = (row < s_n && j < m) ? av[j] + s_xs[col + j] * __uint_as_float(r[j]) : 0.f;
       if (s_ok && row < s_n) {
         float* op = s_out + (size_t)(t0 + col) * s_ldo + row;
 #pragma unroll
         for (int j = 0; j < 16; j++)
-          if (j < m) op[(size_t)j * s_ldo] = av[j] + s_xs[col + j] * __uint_as_float(r[j]);
+          if (j < m) op[(size_t)j * s_ldo] = yv[j];
       }
+      if (G.nw) {   // the next norm's operand tiles and this warp's 32 rows' sums of squares per token
+        const int nchn = tc_nch(s_n);
+        if (row < s_n) {
+          const float wn = G.nw[row];
+#pragma unroll
+          for (int j = 0; j < 16; j++) {
+            if (j < m) {
+              const float v = yv[j] * wn;
+              const __half h = __float2half_rn(v);
+              G.nxt[tc_index(t0 + col + j, row, nchn, 0)] = h;
+              G.nxt[tc_index(t0 + col + j, row, nchn, 1)] = __float2half_rn(v - __half2float(h));
+            }
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < 16; j++) {
+          const float sq = warp_sum(yv[j] * yv[j]);
+          if (lane == 0) s_red[q4][col + j] = sq;
+        }
+      }
+    }
+    if (G.nw) {
+      __syncthreads();
+      if (tid < nt)
+        G.nssq[(size_t)(t0 + tid) * G.ntiles + rt] = ((s_red[0][tid] + s_red[1][tid]) + s_red[2][tid]) + s_red[3][tid];
     }
   } else {
     // accumulator -> ex[column][row] (fp32, over the drained stage buffers)
@@ -465,26 +517,57 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_bgemm_tc(BGemm G, BStep st, B
 #pragma unroll
       for (int h = 0; h < 2; h++) {
         const int c = h ? c1 : c0;
-        if (c >= ce || orow >= s_n) continue;
+        if (c >= ce) continue;   // uniform over the warp (one column per warp)
         float4 acc = v[h][0];
 #pragma unroll
         for (int q = 1; q < 8; q++)
           if (q < S) { acc.x += v[h][q].x; acc.y += v[h][q].y; acc.z += v[h][q].z; acc.w += v[h][q].w; }
         const float xs = s_xs[c];
         float* op = s_out + (size_t)(t0 + c) * s_ldo + orow;
-        const float* ap = s_add ? s_add + (size_t)(t0 + c) * s_ldo + orow : nullptr;
+        const float* ap = (s_add && orow < s_n) ? s_add + (size_t)(t0 + c) * s_ldo + orow : nullptr;
+        float y[4] = {xs * acc.x, xs * acc.y, xs * acc.z, xs * acc.w};
         if (vec) {
-          float4 y = make_float4(xs * acc.x, xs * acc.y, xs * acc.z, xs * acc.w);
           if (ap) {
             const float4 a4 = *(const float4*)ap;
-            y.x += a4.x; y.y += a4.y; y.z += a4.z; y.w += a4.w;
+            y[0] += a4.x; y[1] += a4.y; y[2] += a4.z; y[3] += a4.w;
           }
-          *(float4*)op = y;
+          *(float4*)op = make_float4(y[0], y[1], y[2], y[3]);
         } else {
-          const float a[4] = {acc.x, acc.y, acc.z, acc.w};
 #pragma unroll
-          for (int i = 0; i < 4; i++)
-            if (orow + i < s_n) op[i] = (ap ? ap[i] : 0.f) + xs * a[i];
+          for (int i = 0; i < 4; i++) {
+            if (orow + i < s_n) {
+              y[i] = (ap ? ap[i] : 0.f) + y[i];
+              op[i] = y[i];
+            }
+          }
+        }
+        if (G.nw) {   // the next norm's operand tiles; the column's sum of squares over all 128 rows
+          const int nchn = tc_nch(s_n);
+          float sq = 0.f;
+          __align__(8) __half hv[4], lv[4];
+#pragma unroll
+          for (int i = 0; i < 4; i++) {
+            const bool in = orow + i < s_n;
+            const float yi = in ? y[i] : 0.f;
+            sq += yi * yi;
+            const float vn = in ? yi * G.nw[orow + i] : 0.f;
+            hv[i] = __float2half_rn(vn);
+            lv[i] = __float2half_rn(vn - __half2float(hv[i]));
+          }
+          if (orow + 3 < s_n) {   // 4 consecutive K = 8 bytes of one 16-byte core-matrix row
+            *(uint2*)(G.nxt + tc_index(t0 + c, orow, nchn, 0)) = *(const uint2*)hv;
+            *(uint2*)(G.nxt + tc_index(t0 + c, orow, nchn, 1)) = *(const uint2*)lv;
+          } else {
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+              if (orow + i < s_n) {
+                G.nxt[tc_index(t0 + c, orow + i, nchn, 0)] = hv[i];
+                G.nxt[tc_index(t0 + c, orow + i, nchn, 1)] = lv[i];
+              }
+            }
+          }
+          sq = warp_sum(sq);
+          if ((tid & 31) == 0) G.nssq[(size_t)(t0 + c) * G.ntiles + rt] = sq;
         }
       }
     }
@@ -672,7 +755,9 @@ struct ck_batch {
   int *d_slot = nullptr, *d_pos = nullptr, *d_nact = nullptr, *d_btab = nullptr, *d_err = nullptr;
   uint32_t* d_ids = nullptr;
   float *x = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *g = nullptr, *u = nullptr, *logits = nullptr;
-  BXh xh{};
+  BXh xh{};                   // operand tiles of the attention output / SiLU product (scale 1)
+  BXh xn{};                   // operand tiles of the normed residual stream (scale from ssq or the prologue)
+  float* ssq = nullptr;       // [max_seqs][row tiles of hidden] sums of squares of the residual stream
   std::vector<__half*> wt;    // operand tiles per weight: layer-major q k v o gate up down, then the head
   uint8_t* pin = nullptr;     // pinned staging: tok | slot | pos | nact | ids | err
   std::vector<BSeq> seqs;     // one per slot
@@ -821,10 +906,27 @@ cudaError_t launch_pdl(void (*k)(KArgs...), dim3 grid, dim3 block, cudaStream_t 
   return cudaLaunchKernelEx(&cfg, k, args...);
 }
 
-int bgemm_launch(ck_batch* b, cudaStream_t s, int k, std::initializer_list<BSeg> segs) {
+// x: the operand tiles to read.  nw: the residual-stream GEMMs (o, down) also
+// write the next RMS norm's operand tiles (x * nw) into xn with their row
+// tiles' sums of squares; norm_in: the GEMM's prologue scale comes from
+// those sums (the GEMMs that read xn after such an epilogue).
+int bgemm_launch(ck_batch* b, cudaStream_t s, int k, std::initializer_list<BSeg> segs, BXh x,
+                 const float* nw = nullptr, bool norm_in = false) {
   BGemm G;
   memset(&G, 0, sizeof G);
   G.k = k;
+  const int htiles = (b->h->cfg.hidden + TC_ROWS - 1) / TC_ROWS;
+  if (nw) {
+    G.nw = nw;
+    G.nxt = b->xn.xt;
+    G.nssq = b->ssq;
+    G.ntiles = htiles;
+  }
+  if (norm_in) {
+    G.ssq_in = b->ssq;
+    G.ssq_tiles = htiles;
+    G.eps = b->h->cfg.norm_eps;
+  }
   int tiles = 0;
   for (const BSeg& x : segs) {
     G.tile0[G.nseg] = tiles;
@@ -833,7 +935,7 @@ int bgemm_launch(ck_batch* b, cudaStream_t s, int k, std::initializer_list<BSeg>
   }
   G.tile0[G.nseg] = tiles;
   // token tiles past T return at once
-  CKB(b, tc_launch(G, bstep(b), b->xh, b->d_err, (b->max_seqs + TC_NT - 1) / TC_NT, s, true));
+  CKB(b, tc_launch(G, bstep(b), x, b->d_err, (b->max_seqs + TC_NT - 1) / TC_NT, s, true));
   return CK_OK;
 }
 
@@ -850,10 +952,10 @@ BSeg bseg(const Weight& w, const __half* wt, float* out, const float* add, int l
 }
 
 void bprep(ck_batch* b, cudaStream_t s, int kind, const float* a, const float* bb, const float* w, float eps, int k,
-           int lda) {
+           int lda, BXh x) {
   BPrep p;
   p.kind = kind; p.a = a; p.b = bb; p.w = w; p.eps = eps; p.k = k; p.lda = lda;
-  launch_pdl(k_bprep, dim3(b->max_seqs), dim3(CK_THREADS), s, p, bstep(b), b->xh);
+  launch_pdl(k_bprep, dim3(b->max_seqs), dim3(CK_THREADS), s, p, bstep(b), x);
 }
 
 // The whole step on stream s (captured once into a graph).
@@ -864,12 +966,15 @@ int batch_enqueue(ck_batch* b, cudaStream_t s) {
   const size_t pool = (size_t)b->n_blocks * c.kv_heads * CK_BLK * hd;
   CKB(b, launch_pdl(k_bembed, dim3(b->max_seqs), dim3(256), s, (const uint8_t*)h->emb.dev, h->emb.L,
                     c.embedding_scale, bstep(b), b->x, H, c.vocab, b->d_err));
+  // The RMS norms after the first: the o and down GEMMs (which produce the
+  // residual stream) write the next norm's operand tiles and partial sums of
+  // squares in their epilogue, so only layer 0's attention norm is a prologue.
+  bprep(b, s, BP_NORM, b->x, nullptr, h->L[0].attn_norm, c.norm_eps, H, H, b->xn);
   for (int i = 0; i < c.layers; i++) {
     const LayerW& W = h->L[i];
     __half* const* wt = &b->wt[(size_t)7 * i];
-    bprep(b, s, BP_NORM, b->x, nullptr, W.attn_norm, c.norm_eps, H, H);
     int rc = bgemm_launch(b, s, H, {bseg(W.q, wt[0], b->q, nullptr, qd), bseg(W.k, wt[1], b->k, nullptr, kvd),
-                                    bseg(W.v, wt[2], b->v, nullptr, kvd)});
+                                    bseg(W.v, wt[2], b->v, nullptr, kvd)}, b->xn, nullptr, i > 0);
     if (rc) return rc;
     BAttn a;
     a.q = b->q; a.k = b->k; a.v = b->v;
@@ -887,15 +992,16 @@ int batch_enqueue(ck_batch* b, cudaStream_t s) {
     if (hd == 64) CKB(b, launch_pdl(k_battn<2>, dim3(grid), dim3(CK_THREADS), s, a, bstep(b)));
     else if (hd == 128) CKB(b, launch_pdl(k_battn<4>, dim3(grid), dim3(CK_THREADS), s, a, bstep(b)));
     else CKB(b, launch_pdl(k_battn<8>, dim3(grid), dim3(CK_THREADS), s, a, bstep(b)));
-    if ((rc = bgemm_launch(b, s, qd, {bseg(W.o, wt[3], b->x, b->x, H)}))) return rc;
-    bprep(b, s, BP_NORM, b->x, nullptr, W.post_norm, c.norm_eps, H, H);
-    rc = bgemm_launch(b, s, H, {bseg(W.gate, wt[4], b->g, nullptr, I), bseg(W.up, wt[5], b->u, nullptr, I)});
+    if ((rc = bgemm_launch(b, s, qd, {bseg(W.o, wt[3], b->x, b->x, H)}, b->xh, W.post_norm))) return rc;
+    rc = bgemm_launch(b, s, H, {bseg(W.gate, wt[4], b->g, nullptr, I), bseg(W.up, wt[5], b->u, nullptr, I)}, b->xn,
+                      nullptr, true);
     if (rc) return rc;
-    bprep(b, s, BP_SILU, b->g, b->u, nullptr, 0.f, I, I);
-    if ((rc = bgemm_launch(b, s, I, {bseg(W.down, wt[6], b->x, b->x, H)}))) return rc;
+    bprep(b, s, BP_SILU, b->g, b->u, nullptr, 0.f, I, I, b->xh);
+    const float* next_norm = i + 1 < c.layers ? h->L[i + 1].attn_norm : h->final_norm;
+    if ((rc = bgemm_launch(b, s, I, {bseg(W.down, wt[6], b->x, b->x, H)}, b->xh, next_norm))) return rc;
   }
-  bprep(b, s, BP_NORM, b->x, nullptr, h->final_norm, c.norm_eps, H, H);
-  int rc = bgemm_launch(b, s, H, {bseg(h->head, b->wt[(size_t)7 * c.layers], b->logits, nullptr, c.vocab)});
+  int rc = bgemm_launch(b, s, H, {bseg(h->head, b->wt[(size_t)7 * c.layers], b->logits, nullptr, c.vocab)}, b->xn,
+                        nullptr, true);
   if (rc) return rc;
   CKB(b, launch_pdl(k_bargmax, dim3(b->max_seqs), dim3(CK_THREADS), s, (const float*)b->logits, c.vocab, bstep(b),
                     b->d_ids));
@@ -946,7 +1052,9 @@ int ck_batch_create(ck_engine* h, int max_seqs, int kv_blocks, ck_batch** out) {
       (rc = balloc(b, &b->k, S * kvd * 4)) || (rc = balloc(b, &b->v, S * kvd * 4)) ||
       (rc = balloc(b, &b->g, S * I * 4)) ||
       (rc = balloc(b, &b->u, S * I * 4)) || (rc = balloc(b, &b->logits, S * c.vocab * 4)) ||
-      (rc = balloc(b, &b->xh.xt, tc_bytes(max_seqs, CK_KMAX))) || (rc = balloc(b, &b->xh.xs, S * 4)))
+      (rc = balloc(b, &b->xh.xt, tc_bytes(max_seqs, CK_KMAX))) || (rc = balloc(b, &b->xh.xs, S * 4)) ||
+      (rc = balloc(b, &b->xn.xt, tc_bytes(max_seqs, CK_KMAX))) || (rc = balloc(b, &b->xn.xs, S * 4)) ||
+      (rc = balloc(b, &b->ssq, S * ((c.hidden + TC_ROWS - 1) / TC_ROWS) * 4)))
     return bail(rc);
   // every weight as operand tiles (dequantized once: 4 bytes per weight)
   {
