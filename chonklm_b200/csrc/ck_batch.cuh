@@ -13,10 +13,10 @@
 //   block table; its blocks are reserved when it joins.
 // * Each matvec becomes a tensor-core GEMM over the step's tokens
 //   (k_bgemm_tc, below) on the weights' fp16 operand tiles, made once per
-//   batch; the per-token prologue (k_bprep: RMS norm or SiLU gate) writes x
-//   as operand tiles too, and attention (one CTA per token and kv head over
-//   that token's sequence, k_battn) writes its output straight into the o
-//   projection's tiles.
+//   batch; x reaches a GEMM as operand tiles too: written by the per-token
+//   prologue (k_bprep: layer 0's RMS norm, the SiLU gate), by attention (one
+//   CTA per token and kv head over that token's sequence, k_battn) for the o
+//   projection, and by the o / down GEMMs' epilogue for the next RMS norm.
 // * The step's kernels are launched with programmatic dependent launch: each
 //   may start while its predecessor runs and waits before touching shared
 //   data (pdl_wait).
@@ -698,7 +698,7 @@ __global__ void __launch_bounds__(CK_THREADS, 1) k_battn(BAttn P, BStep st) {
   }
   __syncthreads();
   // the output goes straight into the o projection's operand tiles (the
-  // COPY prologue's split: x_hi = fp16(x), x_lo = fp16(x - x_hi))
+  // prologue's split: x_hi = fp16(x), x_lo = fp16(x - x_hi))
   const int nch = tc_nch(qd);
   for (int i = tid; i < G * hd; i += CK_THREADS) {
     const int gg = i / hd, d = i % hd;
