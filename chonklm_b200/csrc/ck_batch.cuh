@@ -80,7 +80,20 @@ struct BGemm {
   const float* ssq_in;
   int ssq_tiles;
   float eps;
+  // gate/up GEMM over interleaved tiles (k_tc_format with a second weight):
+  // instead of its outputs, write silu(gate) * up for the 64 features of each
+  // row tile as the down projection's operand tiles (K = glu_k); off when null
+  __half* glu_xt;
+  int glu_k;
 };
+
+// SILU_MUL_WGSL (llama-wgsl-runtime.ts:3529-3547), split into the two fp16
+// parts of an operand tile
+__device__ __forceinline__ void glu_parts(float g, float u, __half& hi, __half& lo) {
+  const float v = (g / (1.0f + expf(-g))) * u;
+  hi = __float2half_rn(v);
+  lo = __float2half_rn(v - __half2float(hi));
+}
 
 struct BAttn {
   const float *q, *k, *v;     // [T][heads*hd], [T][kv_heads*hd]
@@ -175,13 +188,22 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
 // Dequantize n x k weights into operand tiles (grid: row tiles x K chunks;
 // a thread per 32-weight unit of the chunk).  Rows past n and columns past k
 // are zero.
-__global__ void __launch_bounds__(256) k_tc_format(const uint8_t* w, Lay L, int n, int k, __half* out) {
+// With a second weight (w2: the up projection of a gate weight w), tile row r
+// of each 128-row tile holds gate row 64 m + r for r < 64 and up row
+// 64 m + r - 64 for r >= 64 (m = the tile): a GEMM over these tiles has a
+// gate value and its up value in the same tile (n = rows of each weight).
+__global__ void __launch_bounds__(256) k_tc_format(const uint8_t* w, Lay L, int n, int k, __half* out,
+                                                   const uint8_t* w2 = nullptr, Lay L2 = Lay()) {
   const int row = blockIdx.x * TC_ROWS + (threadIdx.x >> 1), uu = threadIdx.x & 1;
   const int c = blockIdx.y, unit = c * 2 + uu, nch = gridDim.y;
+  const bool second = w2 && (row & (TC_ROWS - 1)) >= TC_ROWS / 2;
+  const int src = w2 ? (row / TC_ROWS) * (TC_ROWS / 2) + (row & (TC_ROWS / 2 - 1)) : row;
+  const uint8_t* ws = second ? w2 : w;
+  const Lay& Ls = second ? L2 : L;
   float wv[32];
-  if (row < n && unit < (k >> 5)) {
+  if (src < n && unit < (k >> 5)) {
     U8 u;
-    unpack_unit<true>(L.type, w + (size_t)row * L.row_bytes, L, unit, u);
+    unpack_unit<true>(Ls.type, ws + (size_t)src * Ls.row_bytes, Ls, unit, u);
 #pragma unroll
     for (int i = 0; i < 32; i++) {
       // byte codes are signed (Q8_0 stores int8; the other types' codes are < 64)
@@ -441,7 +463,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_bgemm_tc(BGemm G, BStep st, B
       float yv[16];
 #pragma unroll
       for (int j = 0; j < 16; j++) yv[j] = (row < s_n && j < m) ? av[j] + s_xs[col + j] * __uint_as_float(r[j]) : 0.f;
-      if (s_ok && row < s_n) {
+      if (G.glu_xt) {   // gate / up values to shared memory (the drained stage buffers), [column][row]
+        float* ex = (float*)tsm;
+#pragma unroll
+        for (int j = 0; j < 16; j++) ex[(col + j) * TC_ROWS + rl] = yv[j];
+      } else if (s_ok && row < s_n) {
         float* op = s_out + (size_t)(t0 + col) * s_ldo + row;
 #pragma unroll
         for (int j = 0; j < 16; j++)
@@ -472,6 +498,24 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_bgemm_tc(BGemm G, BStep st, B
       __syncthreads();
       if (tid < nt)
         G.nssq[(size_t)(t0 + tid) * G.ntiles + rt] = ((s_red[0][tid] + s_red[1][tid]) + s_red[2][tid]) + s_red[3][tid];
+    }
+    if (G.glu_xt) {
+      // silu(gate) * up of this tile's 64 features (feature 64 rt + f), 8
+      // consecutive features of one token per item: 16-byte tile stores
+      __syncthreads();
+      const float* ex = (const float*)tsm;
+      const int nchg = tc_nch(G.glu_k);
+      for (int it = tid; it < 8 * nt; it += TC_THREADS) {
+        const int cc = it >> 3, f0 = (it & 7) * 8;
+        __align__(16) __half hv[8], lv[8];
+#pragma unroll
+        for (int e = 0; e < 8; e++)
+          glu_parts(ex[cc * TC_ROWS + f0 + e], ex[cc * TC_ROWS + TC_ROWS / 2 + f0 + e], hv[e], lv[e]);
+        if (s_ok) {
+          *(uint4*)(G.glu_xt + tc_index(t0 + cc, (TC_ROWS / 2) * rt + f0, nchg, 0)) = *(const uint4*)hv;
+          *(uint4*)(G.glu_xt + tc_index(t0 + cc, (TC_ROWS / 2) * rt + f0, nchg, 1)) = *(const uint4*)lv;
+        }
+      }
     }
   } else {
     // accumulator -> ex[column][row] (fp32, over the drained stage buffers)
@@ -526,6 +570,20 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_bgemm_tc(BGemm G, BStep st, B
         float* op = s_out + (size_t)(t0 + c) * s_ldo + orow;
         const float* ap = (s_add && orow < s_n) ? s_add + (size_t)(t0 + c) * s_ldo + orow : nullptr;
         float y[4] = {xs * acc.x, xs * acc.y, xs * acc.z, xs * acc.w};
+        if (G.glu_xt) {   // lanes 0-15 hold gate rows 0-63, lanes 16-31 the matching up rows
+          __align__(8) __half hv[4], lv[4];
+#pragma unroll
+          for (int i = 0; i < 4; i++) {
+            const float up = __shfl_xor_sync(0xffffffffu, y[i], 16);
+            glu_parts(y[i], up, hv[i], lv[i]);
+          }
+          if ((tid & 31) < 16) {
+            const int f = (TC_ROWS / 2) * rt + rr, nchg = tc_nch(G.glu_k);
+            *(uint2*)(G.glu_xt + tc_index(t0 + c, f, nchg, 0)) = *(const uint2*)hv;
+            *(uint2*)(G.glu_xt + tc_index(t0 + c, f, nchg, 1)) = *(const uint2*)lv;
+          }
+          continue;
+        }
         if (vec) {
           if (ap) {
             const float4 a4 = *(const float4*)ap;
@@ -758,6 +816,7 @@ struct ck_batch {
   BXh xh{};                   // operand tiles of the attention output / SiLU product (scale 1)
   BXh xn{};                   // operand tiles of the normed residual stream (scale from ssq or the prologue)
   float* ssq = nullptr;       // [max_seqs][row tiles of hidden] sums of squares of the residual stream
+  bool glu = false;           // gate / up interleaved into one tile set (SiLU in the GEMM epilogue)
   std::vector<__half*> wt;    // operand tiles per weight: layer-major q k v o gate up down, then the head
   uint8_t* pin = nullptr;     // pinned staging: tok | slot | pos | nact | ids | err
   std::vector<BSeq> seqs;     // one per slot
@@ -911,10 +970,12 @@ cudaError_t launch_pdl(void (*k)(KArgs...), dim3 grid, dim3 block, cudaStream_t 
 // tiles' sums of squares; norm_in: the GEMM's prologue scale comes from
 // those sums (the GEMMs that read xn after such an epilogue).
 int bgemm_launch(ck_batch* b, cudaStream_t s, int k, std::initializer_list<BSeg> segs, BXh x,
-                 const float* nw = nullptr, bool norm_in = false) {
+                 const float* nw = nullptr, bool norm_in = false, __half* glu_xt = nullptr) {
   BGemm G;
   memset(&G, 0, sizeof G);
   G.k = k;
+  G.glu_xt = glu_xt;
+  G.glu_k = b->h->cfg.intermediate;
   const int htiles = (b->h->cfg.hidden + TC_ROWS - 1) / TC_ROWS;
   if (nw) {
     G.nw = nw;
@@ -993,10 +1054,17 @@ int batch_enqueue(ck_batch* b, cudaStream_t s) {
     else if (hd == 128) CKB(b, launch_pdl(k_battn<4>, dim3(grid), dim3(CK_THREADS), s, a, bstep(b)));
     else CKB(b, launch_pdl(k_battn<8>, dim3(grid), dim3(CK_THREADS), s, a, bstep(b)));
     if ((rc = bgemm_launch(b, s, qd, {bseg(W.o, wt[3], b->x, b->x, H)}, b->xh, W.post_norm))) return rc;
-    rc = bgemm_launch(b, s, H, {bseg(W.gate, wt[4], b->g, nullptr, I), bseg(W.up, wt[5], b->u, nullptr, I)}, b->xn,
-                      nullptr, true);
-    if (rc) return rc;
-    bprep(b, s, BP_SILU, b->g, b->u, nullptr, 0.f, I, I, b->xh);
+    if (b->glu) {   // silu(gate) * up straight into the down projection's tiles (xh.xs stays 1)
+      BSeg gu = bseg(W.gate, wt[4], nullptr, nullptr, 0);
+      gu.n = 2 * I;
+      rc = bgemm_launch(b, s, H, {gu}, b->xn, nullptr, true, b->xh.xt);
+      if (rc) return rc;
+    } else {
+      rc = bgemm_launch(b, s, H, {bseg(W.gate, wt[4], b->g, nullptr, I), bseg(W.up, wt[5], b->u, nullptr, I)}, b->xn,
+                        nullptr, true);
+      if (rc) return rc;
+      bprep(b, s, BP_SILU, b->g, b->u, nullptr, 0.f, I, I, b->xh);
+    }
     const float* next_norm = i + 1 < c.layers ? h->L[i + 1].attn_norm : h->final_norm;
     if ((rc = bgemm_launch(b, s, I, {bseg(W.down, wt[6], b->x, b->x, H)}, b->xh, next_norm))) return rc;
   }
@@ -1064,11 +1132,28 @@ int ck_batch_create(ck_engine* h, int max_seqs, int kv_blocks, ck_batch** out) {
       for (const Weight* w : {&W.q, &W.k, &W.v, &W.o, &W.gate, &W.up, &W.down}) ws.push_back(w);
     }
     ws.push_back(&h->head);
-    for (const Weight* w : ws) {
+    // gate and up as one interleaved tile set when the intermediate size is a
+    // multiple of 64: the gate/up GEMM then applies SiLU in its epilogue
+    b->glu = c.intermediate % (TC_ROWS / 2) == 0;
+    for (size_t j = 0; j < ws.size(); j++) {
+      const Weight* w = ws[j];
+      const int role = j < (size_t)7 * c.layers ? (int)(j % 7) : -1;   // 4 gate, 5 up
       __half* t = nullptr;
       const int kk = w->L.k;
-      if ((rc = balloc(b, &t, tc_bytes(w->n, kk)))) return bail(rc);
-      k_tc_format<<<dim3((w->n + TC_ROWS - 1) / TC_ROWS, tc_nch(kk)), 256, 0, b->stream>>>(w->dev, w->L, w->n, kk, t);
+      if (b->glu && role == 5) {   // held by the gate's tiles
+        b->wt.push_back(nullptr);
+        continue;
+      }
+      if (b->glu && role == 4) {
+        const Weight* up = ws[j + 1];
+        if ((rc = balloc(b, &t, tc_bytes(2 * w->n, kk)))) return bail(rc);
+        k_tc_format<<<dim3(2 * w->n / TC_ROWS, tc_nch(kk)), 256, 0, b->stream>>>(w->dev, w->L, w->n, kk, t, up->dev,
+                                                                               up->L);
+      } else {
+        if ((rc = balloc(b, &t, tc_bytes(w->n, kk)))) return bail(rc);
+        k_tc_format<<<dim3((w->n + TC_ROWS - 1) / TC_ROWS, tc_nch(kk)), 256, 0, b->stream>>>(w->dev, w->L, w->n, kk,
+                                                                                           t);
+      }
       b->wt.push_back(t);
     }
     if (cudaGetLastError() != cudaSuccess || cudaStreamSynchronize(b->stream) != cudaSuccess)

@@ -72,10 +72,12 @@ def test_tensor_core_matmul(t, k, n, T):
     assert err < MATMUL_TOL, err
 
 
-@pytest.mark.parametrize("arch", ["llama", "qwen3"])
-def test_batch_matches_oracle_greedy(tiny_dir, arch):
+@pytest.mark.parametrize("arch,kw", [("llama", {}), ("qwen3", {}), ("llama", {"intermediate": 544})])
+def test_batch_matches_oracle_greedy(tiny_dir, arch, kw):
+    """intermediate 544 (not a multiple of 64) keeps gate and up as separate
+    tiles with the SiLU prologue; the others fuse SiLU into the GEMM."""
     from chonklm_b200 import _lib
-    path = tiny_model(tiny_dir, arch, "q4_k_m")
+    path = tiny_model(tiny_dir, arch, "q4_k_m", **kw)
     loaded, V = _engine(path)
     rng = np.random.default_rng(5)
     pending = []
