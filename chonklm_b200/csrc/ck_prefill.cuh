@@ -505,7 +505,10 @@ struct ck_prefill_state {
   int* d_nact = nullptr;
   int* d_err = nullptr;
   float *x = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *qr = nullptr, *g = nullptr, *u = nullptr;
-  BXh xh{};
+  BXh xh{};                   // attention output / SiLU product tiles
+  BXh xn{};                   // normed residual-stream tiles (written by the o / down epilogues)
+  float* ssq = nullptr;       // [token][row tile of hidden] sums of squares of the residual stream
+  bool glu = false;           // gate / up interleaved (SiLU in the gate/up GEMM's epilogue)
 };
 
 namespace {
@@ -547,16 +550,33 @@ int pf_ensure(ck_engine* h) {
       (rc = palloc(h, p, &p->k, T * kvd * 4)) || (rc = palloc(h, p, &p->v, T * kvd * 4)) ||
       (rc = palloc(h, p, &p->qr, T * qd * 4)) ||
       (rc = palloc(h, p, &p->g, T * I * 4)) || (rc = palloc(h, p, &p->u, T * I * 4)) ||
-      (rc = palloc(h, p, &p->xh.xt, tc_bytes((int)T, CK_KMAX))) || (rc = palloc(h, p, &p->xh.xs, T * 4)))
+      (rc = palloc(h, p, &p->xh.xt, tc_bytes((int)T, CK_KMAX))) || (rc = palloc(h, p, &p->xh.xs, T * 4)) ||
+      (rc = palloc(h, p, &p->xn.xt, tc_bytes((int)T, CK_KMAX))) || (rc = palloc(h, p, &p->xn.xs, T * 4)) ||
+      (rc = palloc(h, p, &p->ssq, T * ((H + TC_ROWS - 1) / TC_ROWS) * 4)))
     return bail(rc);
+  p->glu = I % (TC_ROWS / 2) == 0;
   for (int i = 0; i < c.layers; i++) {
     const LayerW& W = h->L[i];
+    int role = 0;
     for (const Weight* w : {&W.q, &W.k, &W.v, &W.o, &W.gate, &W.up, &W.down}) {
       __half* t = nullptr;
       const int kk = w->L.k;
-      if ((rc = palloc(h, p, &t, tc_bytes(w->n, kk)))) return bail(rc);
-      k_tc_format<<<dim3((w->n + TC_ROWS - 1) / TC_ROWS, tc_nch(kk)), 256, 0, h->stream>>>(w->dev, w->L, w->n, kk, t);
+      if (p->glu && role == 5) {   // held by the gate's interleaved tiles
+        p->wt.push_back(nullptr);
+        role++;
+        continue;
+      }
+      if (p->glu && role == 4) {
+        if ((rc = palloc(h, p, &t, tc_bytes(2 * w->n, kk)))) return bail(rc);
+        k_tc_format<<<dim3(2 * w->n / TC_ROWS, tc_nch(kk)), 256, 0, h->stream>>>(w->dev, w->L, w->n, kk, t,
+                                                                               W.up.dev, W.up.L);
+      } else {
+        if ((rc = palloc(h, p, &t, tc_bytes(w->n, kk)))) return bail(rc);
+        k_tc_format<<<dim3((w->n + TC_ROWS - 1) / TC_ROWS, tc_nch(kk)), 256, 0, h->stream>>>(w->dev, w->L, w->n,
+                                                                                            kk, t);
+      }
       p->wt.push_back(t);
+      role++;
     }
   }
   cudaError_t e = cudaGetLastError();
@@ -614,15 +634,24 @@ int prefill_gemm(ck_engine* h, int n) {
     memset(&st, 0, sizeof st);
     st.tok = h->D.tokens + p0;
     st.nact = p->d_nact;
-    auto prep = [&](int kind, const float* a, const float* bb, const float* w, int k) {
+    const int htiles = (H + TC_ROWS - 1) / TC_ROWS;
+    auto prep = [&](int kind, const float* a, const float* bb, const float* w, int k, BXh x) {
       BPrep pp;
       pp.kind = kind; pp.a = a; pp.b = bb; pp.w = w; pp.eps = c.norm_eps; pp.k = k; pp.lda = k;
-      k_bprep<<<T, CK_THREADS, 0, s>>>(pp, st, p->xh);
+      k_bprep<<<T, CK_THREADS, 0, s>>>(pp, st, x);
     };
-    auto gemm = [&](int k, std::initializer_list<BSeg> segs) {
+    // x: operand tiles read; nw: also write the next norm's tiles into xn
+    // (residual-stream GEMMs); norm_in: prologue scale from those sums;
+    // glu_xt: gate/up over interleaved tiles, silu(gate) * up into glu_xt
+    auto gemm = [&](int k, std::initializer_list<BSeg> segs, BXh x, const float* nw, bool norm_in,
+                    __half* glu_xt) {
       BGemm G;
       memset(&G, 0, sizeof G);
       G.k = k;
+      if (nw) { G.nw = nw; G.nxt = p->xn.xt; G.nssq = p->ssq; G.ntiles = htiles; }
+      if (norm_in) { G.ssq_in = p->ssq; G.ssq_tiles = htiles; G.eps = c.norm_eps; }
+      G.glu_xt = glu_xt;
+      G.glu_k = I;
       int tiles = 0;
       for (const BSeg& x : segs) {
         G.tile0[G.nseg] = tiles;
@@ -630,15 +659,17 @@ int prefill_gemm(ck_engine* h, int n) {
         tiles += (x.n + TC_ROWS - 1) / TC_ROWS;
       }
       G.tile0[G.nseg] = tiles;
-      return tc_launch(G, st, p->xh, p->d_err, ttiles, s);
+      return tc_launch(G, st, x, p->d_err, ttiles, s);
     };
     k_bembed<<<T, 256, 0, s>>>(h->emb.dev, h->emb.L, c.embedding_scale, st, p->x, H, c.vocab, p->d_err);
+    // only layer 0's attention norm is a prologue; the o and down GEMMs write
+    // the next norm's operand tiles in their epilogue
+    prep(BP_NORM, p->x, nullptr, h->L[0].attn_norm, H, p->xn);
     for (int i = 0; i < c.layers; i++) {
       const LayerW& W = h->L[i];
       __half* const* wt = &p->wt[(size_t)7 * i];
-      prep(BP_NORM, p->x, nullptr, W.attn_norm, H);
       CKC(h, gemm(H, {bseg(W.q, wt[0], p->q, nullptr, qd), bseg(W.k, wt[1], p->k, nullptr, kvd),
-                      bseg(W.v, wt[2], p->v, nullptr, kvd)}));
+                      bseg(W.v, wt[2], p->v, nullptr, kvd)}, p->xn, nullptr, i > 0, nullptr));
       PfAttn a;
       a.q = p->q; a.k = p->k; a.v = p->v;
       a.qw = c.qk_norm ? W.q_norm : nullptr;
@@ -657,11 +688,19 @@ int prefill_gemm(ck_engine* h, int n) {
       if (hd == 64) pf_attn_launch<2>(a, f32, T, p->d_nact, p->d_err, s);
       else if (hd == 128) pf_attn_launch<4>(a, f32, T, p->d_nact, p->d_err, s);
       else pf_attn_launch<8>(a, f32, T, p->d_nact, p->d_err, s);
-      CKC(h, gemm(qd, {bseg(W.o, wt[3], p->x, p->x, H)}));
-      prep(BP_NORM, p->x, nullptr, W.post_norm, H);
-      CKC(h, gemm(H, {bseg(W.gate, wt[4], p->g, nullptr, I), bseg(W.up, wt[5], p->u, nullptr, I)}));
-      prep(BP_SILU, p->g, p->u, nullptr, I);
-      CKC(h, gemm(I, {bseg(W.down, wt[6], p->x, p->x, H)}));
+      CKC(h, gemm(qd, {bseg(W.o, wt[3], p->x, p->x, H)}, p->xh, W.post_norm, false, nullptr));
+      if (p->glu) {
+        BSeg gu = bseg(W.gate, wt[4], nullptr, nullptr, 0);
+        gu.n = 2 * I;
+        CKC(h, gemm(H, {gu}, p->xn, nullptr, true, p->xh.xt));
+      } else {
+        CKC(h, gemm(H, {bseg(W.gate, wt[4], p->g, nullptr, I), bseg(W.up, wt[5], p->u, nullptr, I)}, p->xn, nullptr,
+                    true, nullptr));
+        prep(BP_SILU, p->g, p->u, nullptr, I, p->xh);
+      }
+      // the last layer's output only feeds the single-token step (its own norm)
+      const float* next_norm = i + 1 < c.layers ? h->L[i + 1].attn_norm : nullptr;
+      CKC(h, gemm(I, {bseg(W.down, wt[6], p->x, p->x, H)}, p->xh, next_norm, false, nullptr));
     }
     CKC(h, cudaGetLastError());
   }

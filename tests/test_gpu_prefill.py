@@ -50,7 +50,8 @@ def _continue(eng, orc, nid, oid, steps, tol):
         oid = oid2
 
 
-SHAPES = {"hd64": {}, "hd128": {"head_dim": 128}, "g3": {"heads": 6, "kv_heads": 2}}
+SHAPES = {"hd64": {}, "hd128": {"head_dim": 128}, "g3": {"heads": 6, "kv_heads": 2},
+          "i544": {"intermediate": 544}}   # not a multiple of 64: gate / up tiles kept apart
 
 
 @pytest.mark.parametrize("shape", list(SHAPES))
