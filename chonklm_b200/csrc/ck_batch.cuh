@@ -636,24 +636,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_bgemm_tc(BGemm G, BStep st, B
   if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TC_NT));
 }
 
-// Attention for one (active entry, kv head): QK-norm + RoPE + K/V store at
-// the entry's position in its sequence's blocks, then an online softmax over
-// [start, pos] (the single-sequence attention unit with one split), one
-// warp group per query head.
+// Prologue of the batched attention for one (active entry t, kv head):
+// block table to shared memory, QK-norm + RoPE of the G query heads (into
+// s.qs) and of the new K row (s.kst), and the K/V rows stored into the
+// entry's block at its position.
 template <int E>
-__global__ void __launch_bounds__(CK_THREADS, 1) k_battn(BAttn P, BStep st) {
+__device__ __forceinline__ void battn_prologue(const BAttn& P, const BStep& st, SmemAt& s, int* sbt, int t, int kvh,
+                                               int pos) {
   constexpr int hd = 32 * E;
-  const int t = blockIdx.x / P.kvh, kvh = blockIdx.x % P.kvh;
-  if (t >= *st.nact) return;
-  pdl_wait();
-  pdl_launch();
-  __shared__ SmemAt s;
-  __shared__ int sbt[256];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int G = P.heads / P.kvh, qd = P.heads * hd, kvd = P.kvh * hd;
-  const int pos = st.pos[t];
   const int* bt = st.btab + (size_t)st.slot[t] * st.max_blocks;
-  const int start = (P.window != 0 && pos + 1 > P.window) ? pos + 1 - P.window : 0;
   for (int i = tid; i <= (pos >> 4) && i < 256; i += CK_THREADS) sbt[i] = bt[i];
   for (int d = tid; d < (hd >> 1); d += CK_THREADS) {
     float sn, cn;
@@ -685,13 +678,30 @@ __global__ void __launch_bounds__(CK_THREADS, 1) k_battn(BAttn P, BStep st) {
   rope_head(s.kvw[0], P.kw ? s.kvw[3] : nullptr, P.kw ? s.inv[G] : 1.f, s.kst, hd, P.interleaved, s.cs, tid,
             CK_THREADS);
   __syncthreads();
-  {
-    const size_t cb = (((size_t)sbt[pos >> 4] * P.kvh + kvh) * CK_BLK + (pos & (CK_BLK - 1))) * hd;
-    for (int d = tid; d < hd; d += CK_THREADS) {
-      P.kc[cb + d] = __float2half_rn(s.kst[d]);
-      P.vc[cb + d] = __float2half_rn(s.kvw[1][d]);
-    }
+  const size_t cb = (((size_t)sbt[pos >> 4] * P.kvh + kvh) * CK_BLK + (pos & (CK_BLK - 1))) * hd;
+  for (int d = tid; d < hd; d += CK_THREADS) {
+    P.kc[cb + d] = __float2half_rn(s.kst[d]);
+    P.vc[cb + d] = __float2half_rn(s.kvw[1][d]);
   }
+}
+
+// Attention for one (active entry, kv head): the prologue above, then an
+// online softmax over [start, pos] (the single-sequence attention unit with
+// one split), one warp group per query head.
+template <int E>
+__global__ void __launch_bounds__(CK_THREADS, 1) k_battn(BAttn P, BStep st) {
+  constexpr int hd = 32 * E;
+  const int t = blockIdx.x / P.kvh, kvh = blockIdx.x % P.kvh;
+  if (t >= *st.nact) return;
+  pdl_wait();
+  pdl_launch();
+  __shared__ SmemAt s;
+  __shared__ int sbt[256];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int G = P.heads / P.kvh, qd = P.heads * hd;
+  const int pos = st.pos[t];
+  const int start = (P.window != 0 && pos + 1 > P.window) ? pos + 1 - P.window : 0;
+  battn_prologue<E>(P, st, s, sbt, t, kvh, pos);
   const int wpg = CK_WARPS / G;
   const int g = warp / wpg, sub = warp % wpg;
   float q[E], acc[E], m = -INFINITY, l = 0.f;
@@ -763,6 +773,112 @@ __global__ void __launch_bounds__(CK_THREADS, 1) k_battn(BAttn P, BStep st) {
     float A = 0.f;
     for (int w = gg * wpg; w < gg * wpg + wpg; w++) A += s.wacc[w * CK_HDMAX + d] * s.wf[w];
     const float o = A / s.hl[gg];
+    const int col = (kvh * G + gg) * hd + d;
+    const __half h = __float2half_rn(o);
+    P.xo.xt[tc_index(t, col, nch, 0)] = h;
+    P.xo.xt[tc_index(t, col, nch, 1)] = __float2half_rn(o - __half2float(h));
+  }
+  if (tid == 0 && kvh == 0) P.xo.xs[t] = 1.0f;
+}
+
+// Attention for one (active entry, kv head) with the G query heads of the
+// group handled together: every warp takes positions start + warp, + 16, ...
+// for all G heads (each K/V row is loaded once for the group, 16 positions in
+// flight per round across the CTA), keeping one online softmax per head; the
+// warps' partials are then merged per head.  Same prologue and output as
+// k_battn.  Used for head_dim 64 (E = 2), where it fits two CTAs per SM.
+template <int E, int G>
+__global__ void __launch_bounds__(CK_THREADS, 2) k_battn_g(BAttn P, BStep st) {
+  constexpr int hd = 32 * E;
+  static_assert(G * hd <= CK_HDMAX, "the warps' partials live in SmemAt::wacc");
+  const int t = blockIdx.x / P.kvh, kvh = blockIdx.x % P.kvh;
+  if (t >= *st.nact) return;
+  pdl_wait();
+  pdl_launch();
+  __shared__ SmemAt s;
+  __shared__ int sbt[256];
+  __shared__ float wm[CK_WARPS * G], wl[CK_WARPS * G], wf[CK_WARPS * G], hl[G];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int qd = P.heads * hd;
+  const int pos = st.pos[t];
+  const int start = (P.window != 0 && pos + 1 > P.window) ? pos + 1 - P.window : 0;
+  battn_prologue<E>(P, st, s, sbt, t, kvh, pos);
+  float q[G][E], acc[G][E], m[G], l[G];
+#pragma unroll
+  for (int g = 0; g < G; g++) {
+    m[g] = -INFINITY;
+    l[g] = 0.f;
+#pragma unroll
+    for (int e = 0; e < E; e++) {
+      q[g][e] = s.qs[g * hd + lane * E + e];
+      acc[g][e] = 0.f;
+    }
+  }
+  auto off = [&](int p) {
+    return (((size_t)sbt[p >> 4] * P.kvh + kvh) * CK_BLK + (p & (CK_BLK - 1))) * hd + lane * E;
+  };
+  constexpr int CH = E <= 4 ? 8 : 4;   // positions of a warp per round
+  for (int p0 = start + warp; p0 < pos; p0 += CH * CK_WARPS) {
+    KvRow<E, false> kr[CH], vr[CH];
+#pragma unroll
+    for (int j = 0; j < CH; j++) {
+      const int p = p0 + j * CK_WARPS;
+      kv_zero(kr[j]); kv_zero(vr[j]);
+      if (p < pos) { kv_load(P.kc, off(p), kr[j]); kv_load(P.vc, off(p), vr[j]); }
+    }
+#pragma unroll
+    for (int j = 0; j < CH; j += 2) {   // positions grow with j: a pair past pos ends the round
+      if (p0 + j * CK_WARPS < pos) {
+        const bool has1 = p0 + (j + 1) * CK_WARPS < pos;
+#pragma unroll
+        for (int g = 0; g < G; g++)
+          softmax_pair<E, false>(q[g], kr[j], vr[j], kr[j + 1], vr[j + 1], has1, P.scale, m[g], l[g], acc[g]);
+      }
+    }
+  }
+  if (warp == 0) {   // position pos, as the cache now holds it
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+      float d0 = 0.f;
+#pragma unroll
+      for (int e = 0; e < E; e++) d0 += q[g][e] * kv_round<false>(s.kst[lane * E + e]);
+      const float s0 = warp_sum(d0) * P.scale;
+      const float mn = fmaxf(m[g], s0);
+      const float c = expf(m[g] - mn), p0 = expf(s0 - mn);
+      l[g] = l[g] * c + p0;
+#pragma unroll
+      for (int e = 0; e < E; e++) acc[g][e] = acc[g][e] * c + p0 * kv_round<false>(s.kvw[1][lane * E + e]);
+      m[g] = mn;
+    }
+  }
+#pragma unroll
+  for (int g = 0; g < G; g++) {
+    if (lane == 0) {
+      wm[warp * G + g] = m[g];
+      wl[warp * G + g] = l[g];
+    }
+#pragma unroll
+    for (int e = 0; e < E; e++) s.wacc[warp * (G * hd) + g * hd + lane * E + e] = acc[g][e];
+  }
+  __syncthreads();
+  if (tid < G) {   // per head: the warps' weights exp(m_w - M) and the merged sum
+    float M = -INFINITY;
+    for (int w = 0; w < CK_WARPS; w++) M = fmaxf(M, wm[w * G + tid]);
+    float L = 0.f;
+    for (int w = 0; w < CK_WARPS; w++) {
+      const float f = wm[w * G + tid] == -INFINITY ? 0.f : expf(wm[w * G + tid] - M);
+      wf[w * G + tid] = f;
+      L += wl[w * G + tid] * f;
+    }
+    hl[tid] = L;
+  }
+  __syncthreads();
+  const int nch = tc_nch(qd);
+  for (int i = tid; i < G * hd; i += CK_THREADS) {
+    const int gg = i / hd, d = i % hd;
+    float A = 0.f;
+    for (int w = 0; w < CK_WARPS; w++) A += s.wacc[w * (G * hd) + gg * hd + d] * wf[w * G + gg];
+    const float o = A / hl[gg];
     const int col = (kvh * G + gg) * hd + d;
     const __half h = __float2half_rn(o);
     P.xo.xt[tc_index(t, col, nch, 0)] = h;
@@ -1049,8 +1165,10 @@ int batch_enqueue(ck_batch* b, cudaStream_t s) {
     a.window = (int)c.layer_window[i];
     a.eps = c.qk_norm_eps;
     a.scale = (float)(1.0 / sqrt((double)hd));   // ATTN_SCALE (:1711)
-    const int grid = b->max_seqs * c.kv_heads;
-    if (hd == 64) CKB(b, launch_pdl(k_battn<2>, dim3(grid), dim3(CK_THREADS), s, a, bstep(b)));
+    const int grid = b->max_seqs * c.kv_heads, G = c.heads / c.kv_heads;
+    if (hd == 64 && G == 3) CKB(b, launch_pdl(k_battn_g<2, 3>, dim3(grid), dim3(CK_THREADS), s, a, bstep(b)));
+    else if (hd == 64 && G == 2) CKB(b, launch_pdl(k_battn_g<2, 2>, dim3(grid), dim3(CK_THREADS), s, a, bstep(b)));
+    else if (hd == 64) CKB(b, launch_pdl(k_battn<2>, dim3(grid), dim3(CK_THREADS), s, a, bstep(b)));
     else if (hd == 128) CKB(b, launch_pdl(k_battn<4>, dim3(grid), dim3(CK_THREADS), s, a, bstep(b)));
     else CKB(b, launch_pdl(k_battn<8>, dim3(grid), dim3(CK_THREADS), s, a, bstep(b)));
     if ((rc = bgemm_launch(b, s, qd, {bseg(W.o, wt[3], b->x, b->x, H)}, b->xh, W.post_norm))) return rc;

@@ -72,10 +72,15 @@ def test_tensor_core_matmul(t, k, n, T):
     assert err < MATMUL_TOL, err
 
 
-@pytest.mark.parametrize("arch,kw", [("llama", {}), ("qwen3", {}), ("llama", {"intermediate": 544})])
+@pytest.mark.parametrize("arch,kw", [("llama", {}), ("qwen3", {}), ("llama", {"intermediate": 544}),
+                                     ("llama", {"heads": 6, "kv_heads": 2}), ("qwen3", {"head_dim": 128}),
+                                     ("llama", {"heads": 8, "kv_heads": 2})])
 def test_batch_matches_oracle_greedy(tiny_dir, arch, kw):
     """intermediate 544 (not a multiple of 64) keeps gate and up as separate
-    tiles with the SiLU prologue; the others fuse SiLU into the GEMM."""
+    tiles with the SiLU prologue; the others fuse SiLU into the GEMM.  The
+    attention shapes cover the grouped-heads kernel (2 or 3 query heads per
+    kv head at head_dim 64) and the per-head-group kernel (head_dim 128, or 4
+    query heads per kv head)."""
     from chonklm_b200 import _lib
     path = tiny_model(tiny_dir, arch, "q4_k_m", **kw)
     loaded, V = _engine(path)
