@@ -170,32 +170,116 @@ void or_embedding(int t, const uint8_t* table, int k, uint32_t token, float scal
   for (int c = 0; c < k; c++) out[c] = weight_at(t, row, (uint32_t)c) * scale;
 }
 
+/* One row of weights into out[0..k), each value computed by the same
+ * expression, in the same operation order, as weight_at (the per-block
+ * factors d*sc and dmin*m are the leading products of that expression, so
+ * hoisting them per sub-block leaves every rounding unchanged). */
+static void dequant_row(int t, const uint8_t* row, int k, float* out) {
+  switch (t) {
+    case GT_Q4_K: case GT_Q5_K: {
+      const size_t bb = t == GT_Q4_K ? 144 : 176;
+      for (int sb = 0; sb < k / 256; sb++) {
+        const size_t base = (size_t)sb * bb;
+        const float d = f16_at(row, base), dmin = f16_at(row, base + 2);
+        for (uint32_t j = 0; j < 8; j++) {
+          uint32_t sc, mn;
+          scale_min_k4(row + base + 4, j, &sc, &mn);
+          const float a = d * (float)sc, b = dmin * (float)mn;
+          const uint32_t group64 = j >> 1, high = j & 1u;
+          float* o = out + 256 * sb + 64 * group64 + 32 * high;
+          for (uint32_t lane = 0; lane < 32; lane++) {
+            uint32_t qv;
+            if (t == GT_Q4_K) {
+              const uint32_t q_byte = row[base + 16 + group64 * 32 + lane];
+              qv = high ? (q_byte >> 4) : (q_byte & 15u);
+            } else {
+              const uint32_t q_byte = row[base + 48 + group64 * 32 + lane];
+              const uint32_t low4 = high ? (q_byte >> 4) : (q_byte & 15u);
+              const uint32_t qh_mask = (high ? 2u : 1u) << (group64 * 2);
+              qv = low4 + ((row[base + 16 + lane] & qh_mask) != 0 ? 16u : 0u);
+            }
+            o[lane] = a * (float)qv - b;
+          }
+        }
+      }
+      return;
+    }
+    case GT_Q6_K: {
+      for (int sb = 0; sb < k / 256; sb++) {
+        const size_t base = (size_t)sb * 210;
+        const float d = f16_at(row, base + 208);
+        for (uint32_t half = 0; half < 2; half++)
+          for (uint32_t quarter = 0; quarter < 4; quarter++)
+            for (uint32_t lane = 0; lane < 32; lane++) {
+              const uint32_t ql = row[base + half * 64 + lane + ((quarter & 1u) ? 32 : 0)];
+              const uint32_t lo = quarter < 2 ? (ql & 15u) : (ql >> 4);
+              const uint32_t qh = (row[base + 128 + half * 32 + lane] >> (quarter * 2)) & 3u;
+              const int32_t q = (int32_t)(lo | (qh << 4)) - 32;
+              const int32_t scale = (int8_t)row[base + 192 + half * 8 + (lane >> 4) + quarter * 2];
+              out[256 * sb + 128 * half + 32 * quarter + lane] = d * (float)scale * (float)q;
+            }
+      }
+      return;
+    }
+    case GT_Q8_0: {
+      for (int b = 0; b < k / 32; b++) {
+        const size_t base = (size_t)b * 34;
+        const float d = f16_at(row, base);
+        for (int i = 0; i < 32; i++) out[32 * b + i] = (float)(int8_t)row[base + 2 + i] * d;
+      }
+      return;
+    }
+    case GT_Q5_0: case GT_Q5_1: {
+      const size_t bb = t == GT_Q5_0 ? 22 : 24;
+      for (int b = 0; b < k / 32; b++) {
+        const size_t base = (size_t)b * bb;
+        const uint32_t qh = u32_at(row, base + (t == GT_Q5_0 ? 2 : 4));
+        const float d = f16_at(row, base);
+        const float m = t == GT_Q5_1 ? f16_at(row, base + 2) : 0.0f;
+        for (uint32_t w = 0; w < 32; w++) {
+          const uint32_t q_byte = row[base + (t == GT_Q5_0 ? 6 : 8) + (w & 15u)];
+          const uint32_t qv = (w >= 16u ? (q_byte >> 4) : (q_byte & 15u)) | (((qh >> w) & 1u) << 4);
+          out[32 * b + w] = t == GT_Q5_0 ? d * (float)((int32_t)qv - 16) : d * (float)qv + m;
+        }
+      }
+      return;
+    }
+    default:
+      for (int c = 0; c < k; c++) out[c] = weight_at(t, row, (uint32_t)c);
+  }
+}
+
 /* GGUF_*_MATVEC_WGSL main (:2247-2277 and siblings): 128 threads stride k,
  * `sum = sum + input[k] * w`, then a stride-64..1 tree. */
 void or_matvec(int t, const uint8_t* w, int k, int n, const float* x, float* y, int mode) {
   size_t rb = or_row_bytes(t, k);
   /* rows are independent: spreading them over host threads changes no result */
-#pragma omp parallel for schedule(static)
-  for (int r = 0; r < n; r++) {
-    const uint8_t* row = w + rb * r;
-    if (mode == OR_MODE_F64) {
-      double s = 0.0;
-      for (int c = 0; c < k; c++) s += (double)x[c] * (double)weight_at(t, row, (uint32_t)c);
-      y[r] = (float)s;
-      continue;
-    }
-    float partial[128];
-    for (int tid = 0; tid < 128; tid++) {
-      float sum = 0.0f;
-      for (int c = tid; c < k; c += 128) {
-        float p = x[c] * weight_at(t, row, (uint32_t)c);
-        sum = sum + p;
+#pragma omp parallel
+  {
+    float* wr = (float*)malloc((size_t)k * sizeof(float));
+#pragma omp for schedule(static)
+    for (int r = 0; r < n; r++) {
+      dequant_row(t, w + rb * r, k, wr);
+      if (mode == OR_MODE_F64) {
+        double s = 0.0;
+        for (int c = 0; c < k; c++) s += (double)x[c] * (double)wr[c];
+        y[r] = (float)s;
+        continue;
       }
-      partial[tid] = sum;
+      float partial[128];
+      for (int tid = 0; tid < 128; tid++) {
+        float sum = 0.0f;
+        for (int c = tid; c < k; c += 128) {
+          float p = x[c] * wr[c];
+          sum = sum + p;
+        }
+        partial[tid] = sum;
+      }
+      for (int stride = 64; stride >= 1; stride >>= 1)
+        for (int tid = 0; tid < stride; tid++) partial[tid] = partial[tid] + partial[tid + stride];
+      y[r] = partial[0];
     }
-    for (int stride = 64; stride >= 1; stride >>= 1)
-      for (int tid = 0; tid < stride; tid++) partial[tid] = partial[tid] + partial[tid + stride];
-    y[r] = partial[0];
+    free(wr);
   }
 }
 
@@ -331,26 +415,35 @@ void or_attention(const float* q, const float* kc, const float* vc, float* out, 
       }
       scores[(size_t)h * max_ctx + t] = s * attn_scale;
     }
-    const float* sc = scores + (size_t)h * max_ctx;
+    float* sc = scores + (size_t)h * max_ctx;
     float m = -3.402823e38f;
     for (uint32_t t = start; t <= (uint32_t)pos; t++) m = fmaxf(m, sc[t]);
     float den = 0.0f;
-    for (uint32_t t = start; t <= (uint32_t)pos; t++) den = den + expf(sc[t] - m);
-    for (int d = 0; d < hd; d++) {
-      if (mode == OR_MODE_F64) {
-        double acc = 0.0;
-        for (uint32_t t = start; t <= (uint32_t)pos; t++)
-          acc += ((double)expf(sc[t] - m) / (double)den) * (double)vc[((size_t)kvh * max_ctx + t) * hd + d];
-        out[h * hd + d] = (float)acc;
-      } else {
-        float acc = 0.0f;
-        for (uint32_t t = start; t <= (uint32_t)pos; t++) {
-          float p = expf(sc[t] - m) / den;
-          float pv = p * vc[((size_t)kvh * max_ctx + t) * hd + d];
-          acc = acc + pv;
-        }
-        out[h * hd + d] = acc;
+    /* sc[t] becomes exp(score - max): the same value for every d below */
+    for (uint32_t t = start; t <= (uint32_t)pos; t++) { sc[t] = expf(sc[t] - m); den = den + sc[t]; }
+    /* per d the terms are added in position order, as the WGSL loop does;
+     * the loops are only nested position-outer for cache locality */
+    if (mode == OR_MODE_F64) {
+      double acc[256];
+      for (int d = 0; d < hd; d++) acc[d] = 0.0;
+      for (uint32_t t = start; t <= (uint32_t)pos; t++) {
+        const double p = (double)sc[t] / (double)den;
+        const float* vr = vc + ((size_t)kvh * max_ctx + t) * hd;
+        for (int d = 0; d < hd; d++) acc[d] += p * (double)vr[d];
       }
+      for (int d = 0; d < hd; d++) out[h * hd + d] = (float)acc[d];
+    } else {
+      float acc[256];
+      for (int d = 0; d < hd; d++) acc[d] = 0.0f;
+      for (uint32_t t = start; t <= (uint32_t)pos; t++) {
+        const float p = sc[t] / den;
+        const float* vr = vc + ((size_t)kvh * max_ctx + t) * hd;
+        for (int d = 0; d < hd; d++) {
+          float pv = p * vr[d];
+          acc[d] = acc[d] + pv;
+        }
+      }
+      for (int d = 0; d < hd; d++) out[h * hd + d] = acc[d];
     }
   }
 }

@@ -203,6 +203,38 @@ def sample_from_candidates(cand_val: np.ndarray, cand_idx: np.ndarray, temperatu
     return limited[max(0, cutoff - 1)][1] if limited else 0
 
 
+def sampler_probabilities(cand_val: np.ndarray, cand_idx: np.ndarray, temperature: float, top_p: float = 1.0,
+                          top_k: int = 0) -> Dict[int, float]:
+    """The probability sampleFromCandidateBuffer (sampling.ts:23-76) gives
+    each id: the candidates it keeps after top-k and the top-p cutoff, with
+    weight exp((v - max) / T) over their sum (no repetition penalty)."""
+    cands = [(float(np.float32(v)), int(i)) for v, i in zip(cand_val.tolist(), cand_idx.tolist())
+             if math.isfinite(float(v)) and i != 0xFFFFFFFF]
+    cands.sort(key=lambda c: -c[0])
+    k = max(0, int(math.floor(top_k))) if top_k else 0
+    limited = cands[:min(k, len(cands))] if k > 0 else cands
+    if not limited:
+        return {}
+    if temperature <= 0:
+        return {limited[0][1]: 1.0}
+    probs = [math.exp((v - limited[0][0]) / temperature) for v, _ in limited]
+    total = sum(probs)
+    cutoff = len(limited)
+    tp = min(max(top_p, 0.0), 1.0)
+    if tp < 1 and total > 0:
+        cdf = 0.0
+        for i, p in enumerate(probs):
+            cdf += p / total
+            if cdf >= tp:
+                cutoff = i + 1
+                break
+    st = sum(probs[:cutoff])
+    out: Dict[int, float] = {}
+    for i in range(cutoff):
+        out[limited[i][1]] = out.get(limited[i][1], 0.0) + probs[i] / st
+    return out
+
+
 def needs_sampling_readback(temperature: float = 0.0, top_p: float = 1.0, top_k: int = 0) -> bool:
     """needsSamplingReadback (sampling.ts:9-16)."""
     k = max(0, int(math.floor(top_k))) if top_k is not None and math.isfinite(top_k) else 0

@@ -73,6 +73,40 @@ def test_matvec_wgsl_order_vs_f64():
     assert np.abs(y32 - y64).max() <= 1e-5 * np.abs(y64).max()
 
 
+@pytest.mark.parametrize("name", list(TYPES))
+def test_matvec_wgsl_mode_bit_exact_restatement(name):
+    """The oracle's fp32 matvec (rows dequantized once, then summed) equals,
+    bit for bit, the GGUF_*_MATVEC_WGSL reduction written out here in numpy
+    over the per-weight dequantizer: 128 strided per-thread sums in column
+    order, then the stride-64..1 tree (llama-wgsl-runtime.ts:2247-2277)."""
+    t = TYPES[name]
+    k = 1024 if name in ("Q4_K", "Q6_K") else 576
+    n = 48
+    rng = np.random.default_rng(5)
+    data = _quantized_blocks(t, k, n, rng)
+    x = rng.standard_normal(k).astype(np.float32)
+    w = oracle.dequant(t, data, k, n)
+    prod = (x[None, :] * w).astype(np.float32)
+    acc = np.zeros((n, 128), dtype=np.float32)
+    pad = np.zeros((n, -k % 128), dtype=np.float32)
+    cols = np.concatenate([prod, pad], axis=1).reshape(n, -1, 128)
+    for j in range(cols.shape[1]):
+        acc = (acc + cols[:, j, :]).astype(np.float32)
+    stride = 64
+    while stride >= 1:
+        acc[:, :stride] = (acc[:, :stride] + acc[:, stride:2 * stride]).astype(np.float32)
+        stride //= 2
+    got = oracle.matvec(t, data, k, n, x, oracle.MODE_WGSL)
+    assert np.array_equal(got.view(np.uint32), acc[:, 0].view(np.uint32))
+
+
+def _quantized_blocks(t, k, n, rng):
+    import torch
+    from chonklm_b200.quant import quantize
+    w = torch.from_numpy(rng.standard_normal((n, k)).astype(np.float32) * 0.02)
+    return np.frombuffer(quantize(w, t), dtype=np.uint8)
+
+
 def test_philox_known_answers():
     """Random123 known-answer vectors for philox4x32-10."""
     assert oracle.philox4x32([0, 0, 0, 0], [0, 0]) == [0x6627E8D5, 0xE169C58D, 0xBC57AC4C, 0x9B00DBD8]
