@@ -31,6 +31,7 @@ CK_MAX_LAYERS = 128
 
 MODE_MEGAKERNEL = 0
 MODE_GRAPH = 1
+MODE_STREAM = 2
 
 
 class CkError(RuntimeError):

@@ -16,6 +16,7 @@
 
 #include "../../include/chonk_b200.h"
 #include "ck_ops.cuh"
+#include "ck_step.cuh"
 
 namespace {
 
@@ -57,7 +58,7 @@ struct ck_engine {
   cudaStream_t own = nullptr, stream = nullptr;
   std::string err;
   bool finalized = false;
-  int mode = 0;  // 0 megakernel, 1 graph of per-phase kernels
+  int mode = 0;  // 0 megakernel, 1 graph of per-phase kernels, 2 streaming step (k_step)
 
   std::vector<LayerW> L;
   Weight emb, head;
@@ -83,7 +84,13 @@ struct ck_engine {
   Phase *d_logits = nullptr, *d_prefill = nullptr;     // per-phase launches (mode 1)
   Phase *dm_logits = nullptr, *dm_prefill = nullptr;   // same phases partitioned for the megakernel grid
   int mega_grid = 0;
-  cudaGraphExec_t gx_logits[2] = {nullptr, nullptr}, gx_prefill[2] = {nullptr, nullptr};
+  cudaGraphExec_t gx_logits[3] = {nullptr, nullptr, nullptr}, gx_prefill[3] = {nullptr, nullptr, nullptr};
+  // streaming step (mode 2): schedules and its tagged vectors (ck_step.cuh)
+  bool sk_ok = false;
+  std::vector<SkPhase> sk_logits, sk_prefill;
+  SkPhase *dsk_logits = nullptr, *dsk_prefill = nullptr;
+  unsigned long long *pk_sub = nullptr, *pk_q = nullptr, *pk_k = nullptr, *pk_v = nullptr, *pk_att = nullptr,
+                     *pk_act = nullptr, *pk_part = nullptr;
 
   CkDev Dlaunch;            // CkDev passed to kernels (trace pointer only when tracing)
   bool trace_on = false;
@@ -390,8 +397,206 @@ void build_schedule(ck_engine* h, bool logits, std::vector<Phase>& out) {
   assign_tags(h, out);
 }
 
+// ---- streaming step (mode 2) -------------------------------------------------
+// Words of a row-partitioned tagged vector of n elements over `grid` CTAs:
+// CTA c's rows start its own segment of 2^sh words (at least 16 words, one
+// 128-byte line).  grid 1: a flat vector.
+int pk_sh(int per) {
+  int sh = 4;
+  while ((1 << sh) < per) sh++;
+  return sh;
+}
+unsigned long long magic40(int d) { return ((1ull << 40) + (unsigned long long)d - 1) / (unsigned long long)d; }
+PkVec make_pk(unsigned long long* p, int n, int grid) {
+  PkVec v;
+  memset(&v, 0, sizeof v);
+  v.p = p; v.n = n; v.grid = grid; v.sh = pk_sh((n + grid - 1) / grid);
+  v.mn = magic40(n);
+  v.mg = magic40(grid);
+  return v;
+}
+size_t pk_words(int n, int grid) { return (size_t)grid << pk_sh((n + grid - 1) / grid); }
+
+bool sk_supported(const ck_engine* h) {
+  const ck_model_cfg& c = h->cfg;
+  const int G = c.heads / c.kv_heads, I = c.intermediate, grid = h->sms;
+  // every CTA must own rows of every matvec phase (see sk_row0)
+  const bool fanin = c.hidden >= grid && I >= grid && c.heads * c.head_dim >= grid;
+  return fanin && c.hidden <= SK_HMAX && c.hidden <= CK_KMAX && I <= CK_KMAX && c.heads * c.head_dim <= CK_KMAX &&
+         G <= CK_GMAX && (c.head_dim == 64 || c.head_dim == 128 || c.head_dim == 256) &&
+         (I + grid - 1) / grid <= SK_GLU_MAX && c.vocab < (1 << 20);
+}
+
+SkPhase sk_mv(const ck_engine* h, int k, std::initializer_list<std::pair<const Weight*, PkVec>> segs) {
+  SkPhase p;
+  memset(&p, 0, sizeof p);
+  p.kind = SK_MV;
+  p.mv.k = k;
+  p.mv.eps = h->cfg.norm_eps;
+  for (const auto& sg : segs) {
+    SkSeg& S = p.mv.seg[p.mv.nseg++];
+    S.w = sg.first->dev; S.L = sg.first->L; S.n = sg.first->n; S.out = sg.second;
+  }
+  sk_partition(p.mv, h->sms);
+  return p;
+}
+
+// The step as streaming phases (see ck_step.cuh): per layer QKV, attention,
+// o, gate/up (+ activation), down; the LM head last.  Residual updates and
+// norms sit in the prologue of the phase that reads a sub-layer's output.
+void build_sk_schedule(ck_engine* h, bool logits, std::vector<SkPhase>& out) {
+  const ck_model_cfg& c = h->cfg;
+  const int H = c.hidden, hd = c.head_dim, qd = c.heads * hd, kvd = c.kv_heads * hd, I = c.intermediate;
+  const int grid = h->sms;
+  const bool gemma = c.arch == CK_ARCH_GEMMA3;
+  const PkVec sub = make_pk(h->pk_sub, H, grid);
+  const PkVec q = make_pk(h->pk_q, qd, grid), k = make_pk(h->pk_k, kvd, grid), v = make_pk(h->pk_v, kvd, grid);
+  const PkVec att = make_pk(h->pk_att, qd, 1);    // flat: written by the attention owners
+  const PkVec act = make_pk(h->pk_act, I, grid);
+  PkVec none;
+  memset(&none, 0, sizeof none);
+  out.clear();
+  auto push = [&](SkPhase p) {
+    p.index = (int)out.size();
+    p.out_tag = p.index + 1;
+    out.push_back(p);
+    return p.out_tag;
+  };
+  int sub_tag = 0;
+  for (int i = 0; i < c.layers; i++) {
+    const LayerW& W = h->L[i];
+    SkPhase a = sk_mv(h, H, {{&W.q, q}, {&W.k, k}, {&W.v, v}});
+    a.mv.in = sub;
+    a.mv.in_tag = sub_tag;
+    a.mv.norm = 1;
+    a.mv.wnorm = W.attn_norm;
+    if (i == 0) {
+      a.mv.res = RES_EMBED;
+      a.mv.emb = h->emb.dev;
+      a.mv.embL = h->emb.L;
+      a.mv.emb_scale = c.embedding_scale;
+    } else if (gemma) {
+      a.mv.res = RES_GEMMA;
+      a.mv.wpost = h->L[i - 1].post_ffn;
+    } else {
+      a.mv.res = RES_ADD;
+    }
+    const int qkv_tag = push(a);
+
+    SkPhase t;
+    memset(&t, 0, sizeof t);
+    t.kind = SK_ATTN;
+    t.at.q = q; t.at.k = k; t.at.v = v;
+    t.at.in_tag = qkv_tag;
+    t.at.qw = c.qk_norm ? W.q_norm : nullptr;
+    t.at.kw = c.qk_norm ? W.k_norm : nullptr;
+    const size_t per_layer = (size_t)c.kv_heads * c.context_length * hd * elem_kv(c);
+    t.at.kc = h->kv + (size_t)(2 * i) * per_layer;
+    t.at.vc = h->kv + (size_t)(2 * i + 1) * per_layer;
+    t.at.inv_freq = h->inv_freq + (size_t)i * (hd / 2);
+    t.at.out = h->pk_att;
+    t.at.part = h->pk_part;
+    t.at.heads = c.heads; t.at.kvh = c.kv_heads; t.at.hd = hd; t.at.ctx = c.context_length;
+    t.at.group = c.heads / c.kv_heads;
+    t.at.window = (int)c.layer_window[i];
+    t.at.interleaved = c.rope_interleaved;
+    t.at.kv_f32 = c.kv_dtype == CK_KV_F32;
+    t.at.smax = h->smax;
+    t.at.eps = c.qk_norm_eps;
+    t.at.scale = (float)(1.0 / sqrt((double)hd));  // ATTN_SCALE constant (:1711)
+    const int att_tag = push(t);
+    // without logits nothing reads the last layer past its K/V store
+    if (!logits && i == c.layers - 1) break;
+
+    SkPhase o = sk_mv(h, qd, {{&W.o, sub}});
+    o.mv.in = att;
+    o.mv.in_tag = att_tag;
+    const int o_tag = push(o);
+
+    SkPhase gu = sk_mv(h, H, {{&W.gate, none}, {&W.up, none}});
+    gu.mv.in = sub;
+    gu.mv.in_tag = o_tag;
+    gu.mv.norm = 1;
+    if (gemma) {
+      gu.mv.res = RES_GEMMA;
+      gu.mv.wpost = W.post_norm;
+      gu.mv.wnorm = W.pre_ffn;
+      gu.mv.epi = EPI_GELU;
+    } else {
+      gu.mv.res = RES_ADD;
+      gu.mv.wnorm = W.post_norm;
+      gu.mv.epi = EPI_SILU;
+    }
+    gu.mv.act = act;
+    const int gu_tag = push(gu);
+
+    SkPhase d = sk_mv(h, I, {{&W.down, sub}});
+    d.mv.in = act;
+    d.mv.in_tag = gu_tag;
+    sub_tag = push(d);
+  }
+  if (logits) {
+    SkPhase hp = sk_mv(h, H, {{&h->head, none}});
+    hp.kind = SK_HEAD;
+    hp.mv.in = sub;
+    hp.mv.in_tag = sub_tag;
+    hp.mv.norm = 1;
+    hp.mv.wnorm = h->final_norm;
+    hp.mv.logits = h->D.logits;
+    if (gemma) {
+      hp.mv.res = RES_GEMMA;
+      hp.mv.wpost = h->L[c.layers - 1].post_ffn;
+    } else {
+      hp.mv.res = RES_ADD;
+    }
+    push(hp);
+  }
+}
+
+int sk_setup(ck_engine* h) {
+  const ck_model_cfg& c = h->cfg;
+  if (!sk_supported(h)) return CK_OK;   // the other modes serve this model
+  const int grid = h->sms, G = c.heads / c.kv_heads, hd = c.head_dim;
+  const size_t words[6] = {pk_words(c.hidden, grid), pk_words(c.heads * hd, grid), pk_words(c.kv_heads * hd, grid),
+                           pk_words(c.kv_heads * hd, grid), (size_t)c.heads * hd, pk_words(c.intermediate, grid)};
+  unsigned long long** bufs[6] = {&h->pk_sub, &h->pk_q, &h->pk_k, &h->pk_v, &h->pk_att, &h->pk_act};
+  int rc;
+  for (int i = 0; i < 6; i++) {
+    if ((rc = dalloc(h, bufs[i], words[i] * 8))) return rc;
+    CKC(h, cudaMemset(*bufs[i], 0, words[i] * 8));
+    h->tagged_bufs.push_back({*bufs[i], words[i] * 8});
+  }
+  const size_t part = (size_t)c.kv_heads * h->smax * G * (hd + 2) * 8;
+  if ((rc = dalloc(h, &h->pk_part, part))) return rc;
+  CKC(h, cudaMemset(h->pk_part, 0, part));
+  h->tagged_bufs.push_back({h->pk_part, part});
+  build_sk_schedule(h, true, h->sk_logits);
+  build_sk_schedule(h, false, h->sk_prefill);
+  for (int l = 0; l < 2; l++) {
+    std::vector<SkPhase>& v = l ? h->sk_logits : h->sk_prefill;
+    SkPhase** dst = l ? &h->dsk_logits : &h->dsk_prefill;
+    if ((rc = dalloc(h, dst, v.size() * sizeof(SkPhase)))) return rc;
+    CKC(h, cudaMemcpy(*dst, v.data(), v.size() * sizeof(SkPhase), cudaMemcpyHostToDevice));
+  }
+  CKC(h, cudaFuncSetAttribute(k_step, cudaFuncAttributeMaxDynamicSharedMemorySize, SK_DYN_BYTES));
+  int per_sm = 0;
+  CKC(h, cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_step, SK_THREADS, SK_DYN_BYTES));
+  if (per_sm < 1) return CK_OK;
+  h->sk_ok = true;
+  return CK_OK;
+}
+
 int enqueue_phases(ck_engine* h, bool logits, int mode, cudaStream_t s) {
   const std::vector<Phase>& ph = logits ? h->ph_logits : h->ph_prefill;
+  if (mode == 2) {
+    CKC(h, cudaMemsetAsync(&h->st->bar, 0, sizeof(uint32_t), s));
+    const SkPhase* dph = logits ? h->dsk_logits : h->dsk_prefill;
+    int nph = (int)(logits ? h->sk_logits.size() : h->sk_prefill.size());
+    int lg = logits ? 1 : 0;
+    void* args[] = {(void*)&dph, (void*)&nph, (void*)&lg, (void*)&h->Dlaunch};
+    CKC(h, cudaLaunchCooperativeKernel((const void*)k_step, dim3(h->sms), dim3(SK_THREADS), args, SK_DYN_BYTES, s));
+    return CK_OK;
+  }
   if (mode == 1) {
     const Phase* dph = logits ? h->d_logits : h->d_prefill;
     for (size_t i = 0; i < ph.size(); i++) {
@@ -715,7 +920,11 @@ int ck_finalize(ck_engine* h) {
     if ((rc = dalloc(h, dst, mp.size() * sizeof(Phase)))) return rc;
     CKC(h, cudaMemcpy(*dst, mp.data(), mp.size() * sizeof(Phase), cudaMemcpyHostToDevice));
   }
-  for (int m = 0; m < 2; m++) {
+  if ((rc = sk_setup(h))) return rc;
+  const char* menv = getenv("CK_MODE");
+  if (h->sk_ok && menv && atoi(menv) == 2) h->mode = 2;
+  for (int m = 0; m < 3; m++) {
+    if (m == 2 && !h->sk_ok) continue;
     if ((rc = capture(h, true, m, &h->gx_logits[m]))) {
       cudaGetLastError();
       h->gx_logits[m] = nullptr;  // fall back to direct launches
@@ -740,7 +949,8 @@ int ck_set_stream(ck_engine* h, void* stream) {
 
 int ck_set_mode(ck_engine* h, int mode) {
   if (!h) return set_global(CK_EINVAL, "null engine");
-  if (mode != 0 && mode != 1) return h->fail(CK_EINVAL, "mode %d", mode);
+  if (mode != 0 && mode != 1 && mode != 2) return h->fail(CK_EINVAL, "mode %d", mode);
+  if (mode == 2 && !h->sk_ok) return h->fail(CK_EINVAL, "the streaming step does not support this model's shapes");
   h->mode = mode;
   return CK_OK;
 }
@@ -952,9 +1162,10 @@ int ck_trace(ck_engine* h, int enable) {
   if (!enable) D.trace = nullptr;
   h->Dlaunch = D;
   // graphs hold the kernel arguments: rebuild them with the new CkDev
-  for (int m = 0; m < 2; m++) {
+  for (int m = 0; m < 3; m++) {
     if (h->gx_logits[m]) { cudaGraphExecDestroy(h->gx_logits[m]); h->gx_logits[m] = nullptr; }
     if (h->gx_prefill[m]) { cudaGraphExecDestroy(h->gx_prefill[m]); h->gx_prefill[m] = nullptr; }
+    if (m == 2 && !h->sk_ok) continue;
     if (capture(h, true, m, &h->gx_logits[m])) { cudaGetLastError(); h->gx_logits[m] = nullptr; }
     if (capture(h, false, m, &h->gx_prefill[m])) { cudaGetLastError(); h->gx_prefill[m] = nullptr; }
   }
@@ -985,7 +1196,7 @@ int ck_destroy(ck_engine* h) {
   cudaSetDevice(h->device);
   cudaStreamSynchronize(h->own);
   pf_free(h);
-  for (int m = 0; m < 2; m++) {
+  for (int m = 0; m < 3; m++) {
     if (h->gx_logits[m]) cudaGraphExecDestroy(h->gx_logits[m]);
     if (h->gx_prefill[m]) cudaGraphExecDestroy(h->gx_prefill[m]);
   }
@@ -1169,8 +1380,26 @@ static_assert(sizeof(CkState) <= CK_NOALLOC_STATE_BYTES, "state slot");
 static_assert(sizeof(Phase) <= CK_NOALLOC_PHASE_BYTES, "phase slot");
 
 #define CK_NOALLOC_MAX_DEVICES 64
-static uint8_t* g_noalloc_dev[CK_NOALLOC_MAX_DEVICES];   // device address of the array, per device
-static int g_noalloc_sms[CK_NOALLOC_MAX_DEVICES];
+// Per-device set-up, done once under std::call_once: the array's device
+// address (cudaGetSymbolAddress with that device current), the kernel's
+// shared-memory attribute and the SM count.  A device reset invalidates the
+// address; the entry point is not meant to be used across cudaDeviceReset.
+struct NoallocDev {
+  uint8_t* base;
+  int sms;
+  cudaError_t rc;
+};
+static NoallocDev g_noalloc_dev[CK_NOALLOC_MAX_DEVICES];
+static std::once_flag g_noalloc_once[CK_NOALLOC_MAX_DEVICES];
+
+static void noalloc_setup(int dev) {
+  NoallocDev& d = g_noalloc_dev[dev];
+  void* p = nullptr;
+  d.rc = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+  if (d.rc == cudaSuccess) d.rc = cudaFuncSetAttribute(k_mv, cudaFuncAttributeMaxDynamicSharedMemorySize, CK_DYN_SMEM_MAX);
+  if (d.rc == cudaSuccess) d.rc = cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
+  d.base = d.rc == cudaSuccess ? (uint8_t*)p : nullptr;
+}
 
 extern "C" int ck_matvec_noalloc(int ggml_type, const void* w_dev, size_t nbytes, int k, int n, const float* x_dev,
                                  float* y_dev, void* stream) {
@@ -1188,19 +1417,14 @@ extern "C" int ck_matvec_noalloc(int ggml_type, const void* w_dev, size_t nbytes
   int dev = 0;
   CKG(cudaGetDevice(&dev));
   if (dev < 0 || dev >= CK_NOALLOC_MAX_DEVICES) return set_global(CK_EINVAL, "ck_matvec_noalloc: device %d", dev);
-  if (!g_noalloc_dev[dev]) {
-    // one-time set-up on this device (the device is current): resolve the
-    // array's device address; the first call on a device should therefore
-    // come before any stream capture
-    void* p = nullptr;
-    CKG(cudaGetSymbolAddress(&p, g_noalloc_scratch));
-    CKG(cudaFuncSetAttribute(k_mv, cudaFuncAttributeMaxDynamicSharedMemorySize, CK_DYN_SMEM_MAX));
-    int sms = 0;
-    CKG(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-    g_noalloc_sms[dev] = sms;
-    g_noalloc_dev[dev] = (uint8_t*)p;
-  }
-  uint8_t* base = g_noalloc_dev[dev];
+  // one-time set-up on this device (current here), so the first call on a
+  // device should come before any stream capture; threads that make their
+  // first calls at the same time wait for the one that runs it
+  std::call_once(g_noalloc_once[dev], noalloc_setup, dev);
+  const NoallocDev& nd = g_noalloc_dev[dev];
+  if (nd.rc != cudaSuccess)
+    return set_global(CK_ECUDA, "ck_matvec_noalloc: device %d set-up: %s", dev, cudaGetErrorString(nd.rc));
+  uint8_t* base = nd.base;
   CkState* st = (CkState*)base;
   Phase* dph = (Phase*)(base + CK_NOALLOC_STATE_BYTES);
   uint8_t* wl = base + CK_NOALLOC_STATE_BYTES + CK_NOALLOC_PHASE_BYTES;
@@ -1218,7 +1442,7 @@ extern "C" int ck_matvec_noalloc(int ggml_type, const void* w_dev, size_t nbytes
   ph.mv.seg[0].add = nullptr;
   ph.mv.seg[0].L = L;
   ph.mv.seg[0].n = n;
-  int grid = n < g_noalloc_sms[dev] ? n : g_noalloc_sms[dev];
+  int grid = n < nd.sms ? n : nd.sms;
   set_partition(ph, grid);
   CkDev D;
   memset(&D, 0, sizeof D);

@@ -182,9 +182,11 @@ int ck_bench_matvec(int ggml_type, const void* bytes, size_t nbytes, int k, int 
  * allocated: the device-layout copy of the weights goes to a static device
  * array of 16 MiB (plus 4.25 KiB of state), held by every GPU that loads the
  * library until exit; larger weights are rejected with CK_EINVAL.  The first
- * call on a device resolves that array's address (one-time set-up) and should
- * come before any stream capture.  All calls share the array: calls that
- * overlap on the GPU race. */
+ * call on a device resolves that array's address (one-time set-up, done once
+ * even when several host threads call at once) and should come before any
+ * stream capture.  Every call waits for its work on `stream` to finish
+ * before it returns.  All calls share the array: calls that overlap on the
+ * GPU race. */
 int ck_matvec_noalloc(int ggml_type, const void* w_dev, size_t nbytes, int k, int n, const float* x_dev,
                       float* y_dev, void* stream);
 

@@ -98,7 +98,7 @@ def _rel(a, b):
 ARCHS = ["llama", "qwen3", "gemma3"]
 
 
-@pytest.mark.parametrize("mode", [_lib.MODE_MEGAKERNEL, _lib.MODE_GRAPH])
+@pytest.mark.parametrize("mode", [_lib.MODE_STREAM, _lib.MODE_MEGAKERNEL, _lib.MODE_GRAPH])
 @pytest.mark.parametrize("kv", ["float16", "float32"])
 @pytest.mark.parametrize("quant", ["q4_k_m", "q8_0"])
 @pytest.mark.parametrize("arch", ARCHS)
@@ -146,27 +146,32 @@ def test_greedy_64_identical(tiny_dir, arch):
 
 @pytest.mark.parametrize("arch", ARCHS)
 def test_modes_and_prefill_bitwise(tiny_dir, arch):
-    """Size-independent properties: megakernel == per-phase graph and
-    ck_prefill == token-by-token runs, bit for bit."""
+    """Size-independent properties: megakernel == per-phase graph (the same
+    phase functions), and ck_prefill == token-by-token runs in the megakernel
+    and in the streaming step, bit for bit."""
     path = tiny_model(tiny_dir, arch, "q4_k_m")
     V = _vocab(path)
     toks = np.random.default_rng(5).integers(0, V, size=30).tolist()
-    outs = []
-    for mode, batched in [(_lib.MODE_MEGAKERNEL, False), (_lib.MODE_GRAPH, False), (_lib.MODE_MEGAKERNEL, True)]:
-        loaded = loadLlamaWgslModel(_def(path, V))
-        eng = loaded.engine.dev
-        eng.set_mode(mode)
-        if batched:
-            nid = eng.prefill(toks, True)
-        else:
-            for t in toks[:-1]:
-                eng.run_token(t, False)
-            nid = eng.run_token(toks[-1], True)
-        outs.append((nid, eng.logits()))
-        loaded.engine.dispose()
-    for nid, lg in outs[1:]:
-        assert nid == outs[0][0]
-        assert np.array_equal(lg.view(np.uint32), outs[0][1].view(np.uint32))
+    groups = [[(_lib.MODE_MEGAKERNEL, False), (_lib.MODE_GRAPH, False), (_lib.MODE_MEGAKERNEL, True)],
+              [(_lib.MODE_STREAM, False), (_lib.MODE_STREAM, True)]]
+    for group in groups:
+        outs = []
+        for mode, batched in group:
+            loaded = loadLlamaWgslModel(_def(path, V))
+            eng = loaded.engine.dev
+            eng.set_mode(mode)
+            eng.set_prefill_gemm(0)        # every prompt id through the step under test
+            if batched:
+                nid = eng.prefill(toks, True)
+            else:
+                for t in toks[:-1]:
+                    eng.run_token(t, False)
+                nid = eng.run_token(toks[-1], True)
+            outs.append((nid, eng.logits()))
+            loaded.engine.dispose()
+        for nid, lg in outs[1:]:
+            assert nid == outs[0][0]
+            assert np.array_equal(lg.view(np.uint32), outs[0][1].view(np.uint32))
 
 
 @pytest.mark.parametrize("arch", ["gemma3", "qwen3"])
