@@ -200,25 +200,38 @@ def run_reference(args, cfg_name, rank, world, barrier):
 
 
 def matvec_report(path, peak):
-    """Per-shape matvec GB/s (algorithmic bytes: weights + x + y) for the
-    Q4_K / Q6_K tensors of the model, each launch streaming from HBM."""
+    """Matvec GB/s (algorithmic bytes: device-layout weights + 4k + 4n) of the
+    streaming matvec kernel on the two large single-type matrices of the
+    model, each launch streaming from HBM (copies rotated past L2): the tied
+    LM head (Q6_K, 151936 x 1024 for Qwen3) and every layer's gate and up
+    projections stacked into one Q4_K matrix."""
     from chonklm_b200 import _lib
     from chonklm_b200.gguf import ByteSource, fetch_gguf_header
     src = ByteSource(path)
     g = fetch_gguf_header(src)
     out = {}
-    for name in ["blk.1.attn_q.weight", "blk.1.ffn_up.weight", "blk.1.ffn_down.weight", "blk.0.ffn_down.weight",
-                 "token_embd.weight"]:
-        t = g.tensor_map.get(name)
-        if t is None:
-            continue
-        data = src.read(g.data_offset + t.offset, t.n_bytes)
-        k, n = t.shape[0], t.shape[1]
-        us = _lib.bench_matvec(t.type, data, k, n, reps=100 if n > 100000 else 400)
-        byts = t.n_bytes + 4 * k + 4 * n
+
+    def one(label, t_type, k, n, data):
+        us = _lib.bench_matvec(t_type, data, k, n, reps=50)
+        dev_bytes = _lib.layout_row_bytes(t_type, k) * n
+        byts = dev_bytes + 4 * k + 4 * n
         gbs = byts / (us * 1e-6) / 1e9
-        out[name] = {"type": t.type, "k": k, "n": n, "us": round(us, 2), "GBps": round(gbs, 1),
-                     "frac": round(gbs / peak, 3)}
+        out[label] = {"type": t_type, "k": k, "n": n, "MB": round(dev_bytes / 1e6, 1), "us": round(us, 2),
+                      "GBps": round(gbs, 1), "frac": round(gbs / peak, 3)}
+
+    t = g.tensor_map.get("output.weight") or g.tensor_map.get("token_embd.weight")
+    if t is not None:
+        one("lm_head", t.type, t.shape[0], t.shape[1], src.read(g.data_offset + t.offset, t.n_bytes))
+    parts, rows, k, typ = [], 0, None, None
+    for name, t in g.tensor_map.items():
+        if name.endswith("ffn_gate.weight") or name.endswith("ffn_up.weight"):
+            if typ is None:
+                typ, k = t.type, t.shape[0]
+            if t.type == typ and t.shape[0] == k:
+                parts.append(src.read(g.data_offset + t.offset, t.n_bytes))
+                rows += t.shape[1]
+    if parts:
+        one("gate_up_all_layers", typ, k, rows, b"".join(parts))
     return out
 
 

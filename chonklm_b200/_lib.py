@@ -359,6 +359,24 @@ def matvec_noalloc(ggml_type: int, w_dev: int, nbytes: int, k: int, n: int, x_de
                                    ctypes.c_void_p(y_dev), ctypes.c_void_p(stream)))
 
 
+def layout_row_bytes(ggml_type: int, k: int) -> int:
+    """Bytes of one row of the engine's device layout (GGUF blocks re-laid
+    into 16-byte units; equal to the GGUF row up to 16-byte padding)."""
+    nb = k // (256 if ggml_type in (12, 14) else 32)
+    r16 = lambda v: (v + 15) & ~15
+    if ggml_type == 12:                       # Q4_K
+        return 16 * nb + 128 * nb
+    if ggml_type == 14:                       # Q6_K
+        return 16 * nb + r16(2 * nb) + 128 * nb + 64 * nb
+    if ggml_type == 8:                        # Q8_0
+        return r16(2 * nb) + 32 * nb
+    if ggml_type == 6:                        # Q5_0
+        return r16(2 * nb) + r16(4 * nb) + 16 * nb
+    if ggml_type == 7:                        # Q5_1
+        return r16(2 * nb) + r16(2 * nb) + r16(4 * nb) + 16 * nb
+    raise ValueError(f"type {ggml_type}")
+
+
 def bench_matvec(ggml_type: int, data: bytes, k: int, n: int, reps: int = 200, device: int = 0) -> float:
     buf = np.ascontiguousarray(np.frombuffer(data, dtype=np.uint8))
     us = ctypes.c_double(0)

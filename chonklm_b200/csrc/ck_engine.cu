@@ -17,6 +17,7 @@
 #include "../../include/chonk_b200.h"
 #include "ck_ops.cuh"
 #include "ck_step.cuh"
+#include "ck_gemv.cuh"
 
 namespace {
 
@@ -1262,6 +1263,16 @@ int ck_dequant(int ggml_type, const void* bytes, size_t nbytes, int k, int n, fl
   return CK_OK;
 }
 
+// The streaming matvec (ck_gemv.cuh) over a whole device-layout weight.
+static cudaError_t gv_launch(ck_engine* h, const Weight& w, const float* dx, float* dy, cudaStream_t s) {
+  GvKernel fn = gv_kernel(w.L.type);
+  if (!fn) return cudaErrorInvalidValue;
+  cudaError_t e = cudaFuncSetAttribute((const void*)fn, cudaFuncAttributeMaxDynamicSharedMemorySize, GV_DYN_BYTES);
+  if (e != cudaSuccess) return e;
+  fn<<<h->sms, GV_THREADS, GV_DYN_BYTES, s>>>(w.dev, w.L, w.n, dx, dy, &h->st->err);
+  return cudaGetLastError();
+}
+
 static int matvec_setup(ck_engine* h, int type, const void* bytes, size_t nbytes, int k, int n, Weight& w, float** x,
                         float** y, Phase** dph, Phase& ph) {
   int rc;
@@ -1292,10 +1303,8 @@ int ck_matvec(int ggml_type, const void* bytes, size_t nbytes, int k, int n, con
     free_tmp(h);
     return set_global(rc, "%s", m.c_str());
   }
-  CkDev D = h->D;
   cudaMemcpyAsync(dx, x, (size_t)k * 4, cudaMemcpyHostToDevice, h->own);
-  k_mv<<<ph.grid, CK_THREADS, CK_DYN_PHASES + sizeof(Phase), h->own>>>(dph, D);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = gv_launch(h, w, dx, dy, h->own);
   if (e == cudaSuccess) e = cudaMemcpyAsync(y, dy, (size_t)n * 4, cudaMemcpyDeviceToHost, h->own);
   if (e == cudaSuccess) e = cudaStreamSynchronize(h->own);
   free_tmp(h);
@@ -1318,35 +1327,30 @@ int ck_bench_matvec(int ggml_type, const void* bytes, size_t nbytes, int k, int 
     free_tmp(h);
     return set_global(rc, "%s", m.c_str());
   }
-  CkDev D = h->D;
   cudaMemsetAsync(dx, 0, (size_t)k * 4, h->own);
   // Rotate over enough weight copies to exceed L2 so every launch streams
   // from HBM.
   size_t wbytes = (size_t)w.L.row_bytes * n;
   int copies = (int)((256ull << 20) / (wbytes ? wbytes : 1)) + 1;
   if (copies > 64) copies = 64;
-  std::vector<Phase*> phs;
-  std::vector<uint8_t*> ws;
-  phs.push_back(dph);
+  std::vector<Weight> ws;
+  ws.push_back(w);
   for (int c = 1; c < copies; c++) {
-    uint8_t* wc = nullptr;
-    if (dalloc(h, &wc, wbytes)) break;
-    cudaMemcpyAsync(wc, w.dev, wbytes, cudaMemcpyDeviceToDevice, h->own);
-    Phase pc = ph;
-    pc.mv.seg[0].w = wc;
-    Phase* dpc = nullptr;
-    if (dalloc(h, &dpc, sizeof(Phase))) break;
-    cudaMemcpyAsync(dpc, &pc, sizeof(Phase), cudaMemcpyHostToDevice, h->own);
-    phs.push_back(dpc);
+    Weight wc = w;
+    if (dalloc(h, &wc.dev, wbytes)) break;
+    cudaMemcpyAsync(wc.dev, w.dev, wbytes, cudaMemcpyDeviceToDevice, h->own);
+    ws.push_back(wc);
   }
-  for (int i = 0; i < 3; i++) k_mv<<<ph.grid, CK_THREADS, CK_DYN_PHASES + sizeof(Phase), h->own>>>(phs[i % phs.size()], D);
+  (void)dph; (void)ph;
+  cudaError_t e = cudaSuccess;
+  for (int i = 0; i < 3 && e == cudaSuccess; i++) e = gv_launch(h, ws[i % ws.size()], dx, dy, h->own);
   cudaEvent_t a, b;
   cudaEventCreate(&a);
   cudaEventCreate(&b);
   cudaEventRecord(a, h->own);
-  for (int i = 0; i < reps; i++) k_mv<<<ph.grid, CK_THREADS, CK_DYN_PHASES + sizeof(Phase), h->own>>>(phs[i % phs.size()], D);
+  for (int i = 0; i < reps && e == cudaSuccess; i++) e = gv_launch(h, ws[i % ws.size()], dx, dy, h->own);
   cudaEventRecord(b, h->own);
-  cudaError_t e = cudaEventSynchronize(b);
+  if (e == cudaSuccess) e = cudaEventSynchronize(b);
   float ms = 0.f;
   if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, a, b);
   cudaEventDestroy(a);
