@@ -67,13 +67,15 @@ def peaks():
 def model_file(spec_name: str, rank: int, world: int, barrier, tokenizer: bool = False) -> str:
     import dataclasses
     from chonklm_b200.synth import SPECS, write_synthetic_gguf
-    d = os.environ.get("CK_BENCH_DIR", "/tmp/chonk_bench")
+    d = os.environ.get("CK_BENCH_DIR", "/tmp/chonk_bench_cpuq")
     os.makedirs(d, exist_ok=True)
     path = os.path.join(d, f"{spec_name}{'-tok' if tokenizer else ''}.gguf")
     if rank == 0 and not os.path.exists(path):
         t = time.time()
         spec = dataclasses.replace(SPECS[spec_name], tokenizer=True) if tokenizer else SPECS[spec_name]
-        write_synthetic_gguf(spec, path + ".tmp", seed=0)
+        # quantized on the CPU: the same bytes on every machine, the bytes the
+        # oracle fixture (tests/golden/bench_decode_ids.json) was made from
+        write_synthetic_gguf(spec, path + ".tmp", seed=0, device="cpu")
         os.replace(path + ".tmp", path)
         log(f"[bench] wrote {path} in {time.time() - t:.1f}s")
     barrier()
@@ -129,19 +131,29 @@ class Clocks:
                 "reasons": sorted(reasons), "samples": len(self.rows)}
 
 
-def cpu_baseline_sample(path: str, vocab: int, max_context: int, seconds: float = 12.0):
+def oracle_at_position(path: str, vocab: int, max_context: int, pos: int):
+    """The oracle on the bench's model, its engine moved to position `pos`
+    (the GPU arm's first decode position).  The prompt's KV rows are not
+    computed: decoding at `pos` costs the same arithmetic whatever the cache
+    holds (every position up to `pos` is attended), which is what the timing
+    needs."""
+    from oracle import oracle
+    m = oracle.OracleModel(path, vocab=vocab, max_context=max_context)
+    m.set_position(pos)
+    return m
+
+
+def cpu_baseline_sample(path: str, vocab: int, max_context: int, pos: int, seconds: float = 12.0):
     """Oracle (fp32, WGSL operation order, OpenMP over output rows) decode
-    tok/s on the host cores: a bounded sample of the same model."""
+    tok/s on the host cores: a bounded sample of the same model at the GPU
+    arm's positions."""
     cores = os.cpu_count() or 1
     os.environ.setdefault("OMP_NUM_THREADS", str(cores))
     cores = int(os.environ["OMP_NUM_THREADS"])
-    from oracle import oracle
     import numpy as np
-    m = oracle.OracleModel(path, vocab=vocab, max_context=max_context)
-    rng = np.random.default_rng(1)
-    for t in rng.integers(0, vocab, size=4).tolist():
-        m.run_token(t, False)
-    nid = int(rng.integers(0, vocab))
+    m = oracle_at_position(path, vocab, max_context, pos)
+    nid = int(np.random.default_rng(1).integers(0, vocab))
+    nid = m.run_token(nid, True)       # warm-up step (page-in of the weights)
     n = 0
     t0 = time.perf_counter()
     while n < 64:
@@ -152,8 +164,8 @@ def cpu_baseline_sample(path: str, vocab: int, max_context: int, seconds: float 
     dt = time.perf_counter() - t0
     m.close()
     return {"value": n / dt, "unit": "tok/s", "cores": cores, "kind": "port",
-            "sample": f"{n} greedy decode steps of the same synthetic model at positions 4..{4 + n} "
-                      f"(C oracle, fp32, OpenMP over rows, {cores} threads)"}
+            "sample": f"{n} greedy decode steps of the same synthetic model at positions {pos + 1}..{pos + n} "
+                      f"(the GPU arm decodes from {pos}; C oracle, fp32, OpenMP over rows, {cores} threads)"}
 
 
 def run_reference(args, cfg_name, rank, world, barrier):
@@ -166,13 +178,9 @@ def run_reference(args, cfg_name, rank, world, barrier):
     cores = os.cpu_count() or 1
     os.environ.setdefault("OMP_NUM_THREADS", str(cores))
     cores = int(os.environ["OMP_NUM_THREADS"])
-    from oracle import oracle
     import numpy as np
-    m = oracle.OracleModel(path, vocab=vocab, max_context=MAX_CONTEXT[spec])
-    rng = np.random.default_rng(1)
-    for t in rng.integers(0, vocab, size=4).tolist():
-        m.run_token(t, False)
-    nid = int(rng.integers(0, vocab))
+    m = oracle_at_position(path, vocab, MAX_CONTEXT[spec], prompt_len)
+    nid = int(np.random.default_rng(1).integers(0, vocab))
     per_step = 2   # tokens decoded per step: a bounded sample of the 256-token step
     for _ in range(args.warmup):
         for _ in range(per_step):
@@ -192,11 +200,37 @@ def run_reference(args, cfg_name, rank, world, barrier):
                        "note": "reference WebGPU runtime unavailable on this box (no Node/Chromium/WebGPU "
                                "adapter); CPU restatement of its WGSL kernels timed instead"},
             "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": "port",
-                             "sample": f"{per_step} greedy decode steps per step at positions >= 4, "
-                                       f"C oracle fp32, {cores} OpenMP threads"},
+                             "sample": f"{per_step} greedy decode steps per step from position {prompt_len} "
+                                       f"(the GPU arm's positions), C oracle fp32, {cores} OpenMP threads"},
             "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     m.close()
+
+
+def decode_ids_check(cfg_name, path, ids, rank, sampling):
+    """The first greedy ids after the prompt against the CPU oracle's, from
+    the committed fixture (tests/golden/make_bench_fixture.py).  Only greedy
+    configs on rank 0's prompt have a fixture; the model file's sha256 is
+    compared first, so different model bytes are not reported as a parity
+    failure."""
+    fx_path = os.path.join(ROOT, "tests", "golden", "bench_decode_ids.json")
+    try:
+        with open(fx_path) as f:
+            fx = json.load(f).get(cfg_name)
+    except Exception:
+        fx = None
+    if fx is None or sampling or rank != 0:
+        return {"match": None, "note": "no oracle fixture for this config"}
+    import hashlib
+    h = hashlib.sha256()
+    with open(path, "rb") as f:
+        for chunk in iter(lambda: f.read(1 << 24), b""):
+            h.update(chunk)
+    if h.hexdigest() != fx["gguf_sha256"]:
+        return {"match": None, "note": "model bytes differ from the fixture's model"}
+    n = min(len(fx["ids"]), len(ids))
+    return {"match": list(ids[:n]) == fx["ids"][:n], "got": list(ids[:n]), "expected": fx["ids"][:n],
+            "source": "CPU oracle, token-by-token prompt (tests/golden/bench_decode_ids.json)"}
 
 
 def matvec_report(path, peak):
@@ -466,7 +500,7 @@ def main():
         loaded.engine.dispose()
         return
     nid = eng.prefill(prompt, True, samp)
-    ids0 = eng.decode(nid, 2, samp)           # stores the first id at the prompt end
+    ids0 = eng.decode(nid, 8, samp)           # stores the first id at the prompt end
     eng.truncate(prompt_len)
     w0, kv0 = eng.step_bytes()
     eng.truncate(prompt_len)
@@ -554,11 +588,29 @@ def main():
     if dist is not None:
         dist.all_reduce(vals, op=dist.ReduceOp.MAX)
     max_ms, max_e2e = float(vals[0]), float(vals[1])
+
+    # ---- batched workload at this N: sequence i on rank
+    # i mod N, no collective on the data path; every rank takes part ----------
+    batched = None
+    if not args.no_batched:
+        gen_b, dt_b, steps_b, fed_b = run_batched(rank, world, barrier, local, 3)
+        max_b, total_b = aggregate(dist, dt_b, float(gen_b))
+        steps_t = torch.tensor([float(steps_b)], dtype=torch.float64, device="cuda")
+        if dist is not None:
+            dist.all_reduce(steps_t, op=dist.ReduceOp.MAX)
+        B = BATCHED
+        batched = {"metric": BATCHED_METRIC, "value": round(total_b / max_b, 1), "unit": "tok/s", "n_gpus": world,
+                   "scaling": "strong", "sequences": B["seqs"], "sequences_per_gpu": -(-B["seqs"] // world),
+                   "ms_per_step": round(1000 * max_b / max(float(steps_t[0]), 1), 3),
+                   "steps": int(steps_t[0]), "tokens_generated": int(total_b),
+                   "config": "smollm2-135m-batched (BASELINE configs[4]): 256 x (128 prompt + 256 greedy), "
+                             f"sequences sharded over {world} GPU(s) (i mod N), slowest rank's wall time"}
     tokens = gen * args.steps * world
     value = tokens / (max_ms / 1000.0)
     e2e_value = tokens / max_e2e
 
     out = None
+    check = decode_ids_check(args.config, path, ids0, rank, sampling) if rank == 0 else None
     if rank == 0:
         peak, peak_kind = peaks()
         per_tok_s = (tot_ms / 1000.0) / (gen * args.steps)
@@ -577,18 +629,9 @@ def main():
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
             try:
-                cpu = cpu_baseline_sample(path, S.vocab, MAX_CONTEXT[spec])
+                cpu = cpu_baseline_sample(path, S.vocab, MAX_CONTEXT[spec], prompt_len)
             except Exception as e:  # reported, not fatal
                 cpu = {"value": None, "error": str(e)}
-        batched = None
-        if world == 1 and not args.no_batched:
-            try:
-                gen_b, dt_b, steps_b, fed_b = run_batched(0, 1, lambda: None, local, 3)
-                batched = {"metric": BATCHED_METRIC, "value": round(gen_b / dt_b, 1), "unit": "tok/s",
-                           "ms_per_step": round(1000 * dt_b / max(steps_b, 1), 3), "steps": steps_b,
-                           "config": "smollm2-135m-batched (BASELINE configs[4]) on 1 GPU"}
-            except Exception as e:
-                batched = {"error": str(e)}
         mv = None
         if not args.no_matvec:
             try:
@@ -608,7 +651,10 @@ def main():
                        "parallelism": f"replicas x{world}"},
             "e2e": {"value": round(e2e_value, 2), "unit": "tok/s",
                     "h2d_bytes_per_step": int(statistics.mean(x[0] for x in e2e_io)),
-                    "d2h_bytes_per_step": int(statistics.mean(x[1] for x in e2e_io))},
+                    "d2h_bytes_per_step": int(statistics.mean(x[1] for x in e2e_io)),
+                    "note": "generateLlamaWgsl wall time; its 256 ids take 255 device steps (the first id "
+                            "is the one the prompt's last step produced, reused as the reference does), so "
+                            "e2e can come within a step of value or pass it"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic, "traffic_note": traffic_note,
                          "peak_source": peak_kind,
@@ -619,13 +665,18 @@ def main():
             "prefill": prefill,
             "clocks": clk.summary(),
             "gpu_launches": int(launches_per_token * gen * args.steps),
-            "decode_ids_head": ids0[:2],
+            "decode_ids_head": ids0[:8],
+            "decode_ids_check": check,
         }
         print(json.dumps(out), flush=True)
     loaded.engine.dispose()
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
+    if check is not None and check.get("match") is False:
+        log("[bench] PARITY FAILURE: the decoded ids differ from the CPU oracle's "
+            f"(tests/golden/bench_decode_ids.json): got {check['got']}, expected {check['expected']}")
+        sys.exit(3)
 
 
 if __name__ == "__main__":

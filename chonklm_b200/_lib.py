@@ -97,6 +97,7 @@ def lib():
             L.ck_global_error.restype = ctypes.c_char_p
             L.ck_set_stream.argtypes = [P, P]
             L.ck_set_mode.argtypes = [P, I]
+            L.ck_set_sampler.argtypes = [P, I]
             L.ck_set_prefill_gemm.argtypes = [P, I, I]
             L.ck_enqueue_decode_steps.argtypes = [P, I]
             L.ck_sync.argtypes = [P]
@@ -224,6 +225,11 @@ class Engine:
 
     def set_stream(self, stream_handle: int) -> None:
         _check(self._L.ck_set_stream(self.h, ctypes.c_void_p(stream_handle)), self.h)
+
+    def set_sampler(self, exact: bool) -> None:
+        """ck_set_sampler: the reference's chunk-maxima candidates (False) or
+        the exact top-K over the whole vocabulary (True)."""
+        _check(self._L.ck_set_sampler(self.h, 1 if exact else 0), self.h)
 
     def set_mode(self, mode: int) -> None:
         _check(self._L.ck_set_mode(self.h, int(mode)), self.h)

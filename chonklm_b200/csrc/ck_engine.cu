@@ -52,6 +52,9 @@ size_t elem_kv(const ck_model_cfg& c) { return c.kv_dtype == CK_KV_F32 ? 4 : 2; 
 
 struct ck_prefill_state;   // tensor-core prefill buffers (ck_prefill.cuh)
 
+// Weights (device layout) up to this size are kept in the 126 MB L2 across tokens.
+#define CK_L2_RESIDENT_BYTES (112.0 * 1024 * 1024)
+
 struct ck_engine {
   ck_model_cfg cfg;
   int device = 0;
@@ -104,6 +107,7 @@ struct ck_engine {
   // tokens per pass (0: the largest)
   ck_prefill_state* pf = nullptr;
   int pf_min = 64, pf_chunk = 0;
+  int sampler_exact = 0;      // ck_set_sampler
 
   int fail(int code, const char* fmt, ...) {
     char buf[512];
@@ -613,7 +617,10 @@ int enqueue_phases(ck_engine* h, bool logits, int mode, cudaStream_t s) {
   int nph = (int)ph.size();
   void* args[] = {(void*)&dph, (void*)&nph, (void*)&h->Dlaunch};
   size_t dyn = CK_DYN_PHASES + ph.size() * sizeof(Phase);
-  CKC(h, cudaLaunchCooperativeKernel((const void*)k_mega, dim3(h->mega_grid), dim3(CK_THREADS), args, dyn, s));
+  // k_mega<1> carries the exact sampler; the default instantiation leaves it
+  // out so the greedy / chunk-sampler step keeps its registers and stack.
+  const void* fn = (logits && h->sampler_exact) ? (const void*)k_mega<1> : (const void*)k_mega<0>;
+  CKC(h, cudaLaunchCooperativeKernel(fn, dim3(h->mega_grid), dim3(CK_THREADS), args, dyn, s));
   return CK_OK;
 }
 
@@ -621,7 +628,10 @@ int capture(ck_engine* h, bool logits, int mode, cudaGraphExec_t* out) {
   cudaStream_t s = h->own;
   cudaGraph_t g = nullptr;
   CKC(h, cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+  const int exact = h->sampler_exact;
+  h->sampler_exact = 0;  // graphs always hold the default k_mega<0>
   int rc = enqueue_phases(h, logits, mode, s);
+  h->sampler_exact = exact;
   cudaError_t e = cudaStreamEndCapture(s, &g);
   if (rc) { if (g) cudaGraphDestroy(g); return rc; }
   if (e != cudaSuccess) return h->fail(CK_ECUDA, "graph capture: %s", cudaGetErrorString(e));
@@ -651,7 +661,8 @@ int launch_step(ck_engine* h, bool logits) {
   }
   h->epoch_steps++;
   cudaGraphExec_t gx = logits ? h->gx_logits[h->mode] : h->gx_prefill[h->mode];
-  if (gx) {
+  // the mode-0 graph holds k_mega<0>: an exact-sampler step launches directly
+  if (gx && !(logits && h->mode == 0 && h->sampler_exact)) {
     CKC(h, cudaGraphLaunch(gx, h->stream));
     return CK_OK;
   }
@@ -672,6 +683,7 @@ int set_params(ck_engine* h, const ck_sampling* s, int chain, uint64_t draw_over
   p.sampling = (temp > 0.0 || top_p < 1.0 || p.top_k > 0) ? 1 : 0;
   p.chain = chain;
   p.seed = s ? s->philox_seed : 0ull;
+  p.exact = h->sampler_exact;
   p.draw = use_override ? (uint32_t)draw_override : (s ? (uint32_t)s->philox_offset : 0u);
   p.abort_flag = 0;
   p.bar = 0;
@@ -866,6 +878,11 @@ int ck_finalize(ck_engine* h) {
   int groups = (c.vocab + 255) / 256;
   if ((rc = dalloc(h, &h->D.cand_val, (size_t)groups * 4))) return rc;
   if ((rc = dalloc(h, &h->D.cand_idx, (size_t)groups * 4))) return rc;
+  // exact sampler: per-CTA candidate lists for the widest stage-1 grid
+  h->D.xgrid = h->sms * 4;
+  if ((rc = dalloc(h, &h->D.xval, (size_t)h->D.xgrid * CK_SAMPLE_MAX * 4))) return rc;
+  if ((rc = dalloc(h, &h->D.xidx, (size_t)h->D.xgrid * CK_SAMPLE_MAX * 4))) return rc;
+  if ((rc = dalloc(h, &h->D.xcnt, (size_t)h->D.xgrid * 4))) return rc;
   CKC(h, cudaMemset(h->D.tokens, 0, (size_t)c.context_length * 4));
   CKC(h, cudaMemset(h->D.pen_mask, 0, (size_t)((c.vocab + 31) / 32) * 4));
   // tagged activations: 8 bytes per element, cleared so no tag matches a step
@@ -892,6 +909,16 @@ int ck_finalize(ck_engine* h) {
   CKC(h, cudaMemset(h->kv, 0, h->kv_bytes));
 
   if ((rc = epoch_restart(h))) return rc;
+  {
+    // every weight read per token (layers + LM head, device layout) fits L2
+    // with room for the KV cache and activations: stream them evict-last so
+    // they stay resident across tokens (CK_L2_KEEP=0/1 overrides)
+    double wb = 0, kb = 0;
+    ck_step_bytes(h, &wb, &kb);
+    h->D.l2_keep = wb <= CK_L2_RESIDENT_BYTES ? 1 : 0;
+    const char* keep = getenv("CK_L2_KEEP");
+    if (keep) h->D.l2_keep = atoi(keep) ? 1 : 0;
+  }
   h->Dlaunch = h->D;
   build_schedule(h, true, h->ph_logits);
   build_schedule(h, false, h->ph_prefill);
@@ -903,10 +930,11 @@ int ck_finalize(ck_engine* h) {
   if (h->ph_logits.size() * sizeof(Phase) > CK_PHASE_SMEM_MAX)
     return h->fail(CK_EINVAL, "%zu decode phases exceed the %d-byte descriptor stage", h->ph_logits.size(),
                    CK_PHASE_SMEM_MAX);
-  CKC(h, cudaFuncSetAttribute(k_mega, cudaFuncAttributeMaxDynamicSharedMemorySize, CK_DYN_SMEM_MAX));
+  CKC(h, cudaFuncSetAttribute(k_mega<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, CK_DYN_SMEM_MAX));
+  CKC(h, cudaFuncSetAttribute(k_mega<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, CK_DYN_SMEM_MAX));
   CKC(h, cudaFuncSetAttribute(k_mv, cudaFuncAttributeMaxDynamicSharedMemorySize, CK_DYN_SMEM_MAX));
   int per_sm = 0;
-  CKC(h, cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_mega, CK_THREADS,
+  CKC(h, cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_mega<1>, CK_THREADS,
                                                        CK_DYN_PHASES + h->ph_logits.size() * sizeof(Phase)));
   int want = 1;
   const char* w = getenv("CK_MEGA_CTAS_PER_SM");
@@ -945,6 +973,12 @@ int ck_finalize(ck_engine* h) {
 int ck_set_stream(ck_engine* h, void* stream) {
   if (!h) return set_global(CK_EINVAL, "null engine");
   h->stream = stream ? (cudaStream_t)stream : h->own;
+  return CK_OK;
+}
+
+int ck_set_sampler(ck_engine* h, int exact) {
+  if (!h) return set_global(CK_EINVAL, "null engine");
+  h->sampler_exact = exact ? 1 : 0;
   return CK_OK;
 }
 

@@ -50,6 +50,8 @@ struct CkState {
   int chain;                // write next_token into tokens[pos+1]
   int pad1;
   unsigned long long seed;  // Philox key
+  int exact;                // sampler over the whole vocabulary (see phase_topk_local)
+  int pad2;
 };
 
 struct CkDev {
@@ -63,6 +65,12 @@ struct CkDev {
   int vocab;
   int ctx;
   unsigned long long* trace;  // optional globaltimer stamps (null = off)
+  int l2_keep;              // 1: the weights fit L2; stream them evict-last so they stay there
+  // exact sampler: per-CTA top-K candidates [cta][CK_SAMPLE_MAX] and counts
+  float* xval;
+  uint32_t* xidx;
+  int* xcnt;
+  int xgrid;                // CTAs the candidate buffers hold
 };
 
 __device__ __forceinline__ unsigned long long gtimer() {
@@ -286,6 +294,13 @@ struct SmemSm {
   uint32_t idx[CK_SAMPLE_MAX];
   double prob[CK_SAMPLE_MAX];
   int n;
+  // exact sampler (radix select): histogram, warp counts, running bases,
+  // per-CTA list offsets
+  int hist[256];
+  int cnt[CK_WARPS];
+  int base, eqbase, rem, total;
+  uint32_t prefix;
+  int off[1024];
 };
 union Smem {
   SmemMv mv;
@@ -513,6 +528,7 @@ struct IssueState {
   Cursor issue;            // next row to copy
   unsigned issued;         // tiles copied so far
   int nph;                 // phases staged for this launch
+  int keep;                // L2 hint of the weight copies (CkDev::l2_keep)
 };
 __device__ __forceinline__ uint8_t* dyn_smem() {
   extern __shared__ __align__(128) uint8_t ck_dyn[];
@@ -625,11 +641,15 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
                "l"(src), "r"(bytes), "r"(smem_u32(bar))
                : "memory");
 }
-// Same, marking the lines evict-first in L2: streamed weights are read once
-// per token and should not push activations, norms or the KV cache out.
-__device__ __forceinline__ void bulk_g2s_stream(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+// Same, with an L2 cache hint for weights.  By default evict-first: weights
+// larger than L2 are read once per token and should not push activations,
+// norms or the KV cache out.  keep = 1 (every weight of the model fits L2):
+// evict-last, so the next token reads them from L2 instead of HBM.
+__device__ __forceinline__ void bulk_g2s_stream(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                                int keep = 0) {
   uint64_t pol;
-  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  if (keep) asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+  else asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
   asm volatile(
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
           smem_u32(dst)),
@@ -658,7 +678,7 @@ __device__ __forceinline__ void ring_issue(int cta) {
         const MvSeg& S = p.mv.seg[sg];
         const uint32_t rb = S.L.row_bytes, bytes = (uint32_t)rows * rb;
         mbar_expect_tx_only(bar, bytes);
-        bulk_g2s_stream(dst + pick3u(i, T.off0, T.off1, T.off2), S.w + (size_t)r0 * rb, bytes, bar);
+        bulk_g2s_stream(dst + pick3u(i, T.off0, T.off1, T.off2), S.w + (size_t)r0 * rb, bytes, bar, is.keep);
       }
       mbar_arrive(bar);
       is.issued++;
@@ -675,7 +695,8 @@ __device__ __forceinline__ void ring_issue(int cta) {
 // memory with one bulk copy (every later descriptor read is a shared-memory
 // read), then put the first two weight tiles in flight.  Returns the staged
 // descriptors, or null when the wait gave up.
-__device__ __forceinline__ const Phase* launch_start(Ring& R, const Phase* gph, int nph, int cta, int* err, int* abort_flag) {
+__device__ __forceinline__ const Phase* launch_start(Ring& R, const Phase* gph, int nph, int cta, int* err, int* abort_flag,
+                                                    int keep) {
   uint8_t* dyn = dyn_smem();
   uint64_t* bars = (uint64_t*)(dyn + CK_DYN_BARS);
   Phase* sph = (Phase*)(dyn + CK_DYN_PHASES);
@@ -693,6 +714,7 @@ __device__ __forceinline__ const Phase* launch_start(Ring& R, const Phase* gph, 
     is.issue.phase = 0; is.issue.seg = 0; is.issue.row = -1;
     is.issued = 0;
     is.nph = nph;
+    is.keep = keep;
   }
   __syncthreads();
   unsigned spins = 0;
@@ -1535,8 +1557,14 @@ __device__ __forceinline__ void block_argmax(float& v, uint32_t& i, float* sv, u
   }
 }
 
+__device__ __noinline__ void phase_topk_local(const CkDev& D, Smem& smu, int cta, int ncta);
+template <int EXACT>
 __device__ __forceinline__ void phase_argmax1(const CkDev& D, Smem& sm, int cta, int ncta) {
   const CkState* st = D.st;
+  if (EXACT && st->exact && st->sampling && D.xval && ncta <= D.xgrid) {
+    phase_topk_local(D, sm, cta, ncta);
+    return;
+  }
   const int groups = (D.vocab + 255) / 256;
   const bool pen = st->pen_d > 1.0;
   const float penalty = (float)st->pen_milli / 1000.0f;
@@ -1594,35 +1622,16 @@ __device__ __forceinline__ double philox_uniform(unsigned long long seed, unsign
   return ((double)(c[0] >> 5) * 67108864.0 + (double)(c[1] >> 6)) / 9007199254740992.0;
 }
 
-// sampleFromCandidateBuffer (sampling.ts:23-76) on the device: re-penalty of
-// seen ids, stable descending sort, top-k, temperature softmax in fp64, top-p
-// cutoff at the first cdf >= topP, draw.  Single CTA.
-__device__ __forceinline__ void phase_sample(const CkDev& D, Smem& smu, int cta) {
+// sampleFromCandidateBuffer (sampling.ts:23-76) on the device over a
+// candidate list staged in s: val = -(value after the re-penalty of seen
+// ids) or +inf (empty slot), idx = id, prob = the stable sort's tie-break
+// (the candidate's place in the reference's list).  Stable descending sort,
+// top-k, temperature softmax in fp64, top-p cutoff at the first cdf >= topP,
+// Philox draw.  One CTA.
+__device__ __forceinline__ void sample_core(const CkDev& D, SmemSm& s) {
   const CkState* st = D.st;
-  if (cta != 0 || !st->sampling) return;
-  SmemSm& s = smu.sm;
   const int tid = threadIdx.x;
-  const int groups = (D.vocab + 255) / 256;
   const int NP = CK_SAMPLE_MAX;
-  const double rp = fmax(st->pen_d, 1e-6);
-  for (int i = tid; i < NP; i += CK_THREADS) {
-    double v = INFINITY;   // sentinel: sorts last
-    uint32_t id = 0xffffffffu;
-    if (i < groups) {
-      float fv = D.cand_val[i];
-      uint32_t ci = D.cand_idx[i];
-      if (isfinite(fv) && ci != 0xffffffffu) {
-        double dv = (double)fv;
-        if (rp != 1.0 && ci < (uint32_t)D.vocab && ((D.pen_mask[ci >> 5] >> (ci & 31)) & 1u))
-          dv = dv > 0 ? dv / rp : dv * rp;
-        v = -dv;        // ascending sort of -value == descending by value
-        id = ci;
-      }
-    }
-    s.val[i] = v;
-    s.idx[i] = id;
-    s.prob[i] = (double)i;   // original order, the stable tie-break
-  }
   __syncthreads();
   // bitonic sort by (val, original order) ascending
   for (int kk = 2; kk <= NP; kk <<= 1) {
@@ -1679,6 +1688,229 @@ __device__ __forceinline__ void phase_sample(const CkDev& D, Smem& smu, int cta)
   }
 }
 
+// One candidate as the sampler takes it: -(value with sampling.ts's
+// re-penalty of seen ids), or +inf when it is dropped (non-finite).
+__device__ __forceinline__ double sample_key(const CkDev& D, float fv, uint32_t ci, double rp) {
+  if (!isfinite(fv) || ci == 0xffffffffu) return INFINITY;
+  double dv = (double)fv;
+  if (rp != 1.0 && ci < (uint32_t)D.vocab && ((D.pen_mask[ci >> 5] >> (ci & 31)) & 1u))
+    dv = dv > 0 ? dv / rp : dv * rp;
+  return -dv;        // ascending sort of -value == descending by value
+}
+
+// The reference's candidate buffer: the per-256 chunk maxima of argmax
+// stage 1 (ARGMAX_STAGE1_WGSL :3645-3726), in chunk order.
+__device__ __forceinline__ void phase_sample(const CkDev& D, Smem& smu, int cta) {
+  const CkState* st = D.st;
+  if (cta != 0 || !st->sampling) return;
+  SmemSm& s = smu.sm;
+  const int groups = (D.vocab + 255) / 256;
+  const double rp = fmax(st->pen_d, 1e-6);
+  for (int i = threadIdx.x; i < CK_SAMPLE_MAX; i += CK_THREADS) {
+    const bool in = i < groups;
+    s.val[i] = in ? sample_key(D, D.cand_val[i], D.cand_idx[i], rp) : INFINITY;
+    s.idx[i] = in && isfinite(s.val[i]) ? D.cand_idx[i] : 0xffffffffu;
+    s.prob[i] = (double)i;   // original order, the stable tie-break
+  }
+  sample_core(D, s);
+}
+
+// ---------------------------------------------------------------------------
+// Exact sampler (CkState::exact): the candidate list is the K largest
+// stage-1 values of the whole vocabulary (K = top-k when 1..1024, else 1024),
+// ties going to the lower id, instead of the per-256 chunk maxima; the
+// sampler then runs on it exactly as on the reference's list (ordered by id).
+// Found by a block-level radix select twice: every CTA selects the top K of
+// its slice of the vocabulary (any of the global top K is in its slice's),
+// then one CTA selects the top K of those candidates.
+//
+// Keys: the float's bits turned order-preserving as unsigned (negative
+// values inverted, positive ones with the sign bit set); NaN maps to 0, the
+// smallest key, as it never wins the reference's argmax.
+__device__ __forceinline__ uint32_t fkey(float v) {
+  if (v != v) return 0u;
+  const uint32_t u = __float_as_uint(v);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ int exact_k(const CkState* st) {
+  return (st->top_k > 0 && st->top_k < CK_SAMPLE_MAX) ? st->top_k : CK_SAMPLE_MAX;
+}
+
+// Radix select over n keys key(i) (MSB first, 8 bits a pass): the K-th
+// largest key T and how many keys equal T must be taken (need) so that the
+// keys > T plus `need` keys == T make K.  Requires n > K.  Every thread gets
+// the result.
+template <typename KeyAt>
+__device__ __forceinline__ void radix_select(int n, int K, KeyAt key, uint32_t& T, int& need, SmemSm& sm) {
+  int* hist = sm.hist;
+  uint32_t& s_prefix = sm.prefix;
+  int& s_rem = sm.rem;
+  const int tid = threadIdx.x;
+  uint32_t prefix = 0u, mask = 0u;
+  int rem = K;
+  for (int pass = 0; pass < 4; pass++) {
+    const int shift = 24 - 8 * pass;
+    for (int b = tid; b < 256; b += CK_THREADS) hist[b] = 0;
+    __syncthreads();
+    for (int i = tid; i < n; i += CK_THREADS) {
+      const uint32_t k = key(i);
+      if ((k & mask) == prefix) atomicAdd(&hist[(k >> shift) & 255u], 1);
+    }
+    __syncthreads();
+    if (tid == 0) {
+      int cum = 0, sel = 0;
+      for (int b = 255; b >= 0; b--) {
+        if (cum + hist[b] >= rem) { sel = b; break; }
+        cum += hist[b];
+      }
+      s_prefix = prefix | ((uint32_t)sel << shift);
+      s_rem = rem - cum;
+    }
+    __syncthreads();
+    prefix = s_prefix;
+    rem = s_rem;
+    mask |= 0xFFu << shift;
+    __syncthreads();
+  }
+  T = prefix;
+  need = rem;
+}
+
+// Write the selected keys of [0, n) in index order: every key > T, then the
+// first `need` keys == T (lowest indices).  emit(i, pos) stores element i at
+// output place pos; returns how many were written (K, or n when n <= K).
+template <typename KeyAt, typename Emit>
+__device__ __forceinline__ int radix_emit(int n, int K, KeyAt key, Emit emit, SmemSm& sm) {
+  int* s_cnt = sm.cnt;
+  int& s_base = sm.base;
+  int& s_eqbase = sm.eqbase;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (n <= K) {
+    for (int i = tid; i < n; i += CK_THREADS) emit(i, i);
+    return n;
+  }
+  uint32_t T;
+  int need;
+  radix_select(n, K, key, T, need, sm);
+  if (tid == 0) { s_base = 0; s_eqbase = 0; }
+  __syncthreads();
+  // chunks of CK_THREADS elements in order; within a chunk a block scan
+  for (int c0 = 0; c0 < n; c0 += CK_THREADS) {
+    const int i = c0 + tid;
+    const uint32_t k = i < n ? key(i) : 0u;
+    const bool gt = i < n && k > T, eq = i < n && k == T;
+    const unsigned bg = __ballot_sync(0xffffffffu, gt), be = __ballot_sync(0xffffffffu, eq);
+    if (lane == 0) s_cnt[warp] = (__popc(bg) << 16) | __popc(be);
+    __syncthreads();
+    int off_g = 0, off_e = 0, tot_g = 0, tot_e = 0;
+    for (int w = 0; w < CK_WARPS; w++) {
+      const int cg = s_cnt[w] >> 16, ce = s_cnt[w] & 0xFFFF;
+      if (w < warp) { off_g += cg; off_e += ce; }
+      tot_g += cg; tot_e += ce;
+    }
+    const unsigned lt = (1u << lane) - 1u;
+    const int rg = s_base + off_g + __popc(bg & lt);
+    if (gt) emit(i, rg);
+    __syncthreads();
+    if (tid == 0) { s_base += tot_g; s_eqbase += tot_e; }
+    __syncthreads();
+    (void)off_e;
+  }
+  // equal keys go after every greater key: their places are known once all
+  // greater keys are counted, so a second sweep emits them
+  const int ngt = s_base;
+  if (tid == 0) s_eqbase = 0;
+  __syncthreads();
+  for (int c0 = 0; c0 < n; c0 += CK_THREADS) {
+    const int i = c0 + tid;
+    const bool eq = i < n && key(i) == T;
+    const unsigned be = __ballot_sync(0xffffffffu, eq);
+    if (lane == 0) s_cnt[warp] = __popc(be);
+    __syncthreads();
+    int off = 0, tot = 0;
+    for (int w = 0; w < CK_WARPS; w++) {
+      if (w < warp) off += s_cnt[w];
+      tot += s_cnt[w];
+    }
+    const int re = s_eqbase + off + __popc(be & ((1u << lane) - 1u));
+    if (eq && re < need) emit(i, ngt + re);
+    __syncthreads();
+    if (tid == 0) s_eqbase += tot;
+    __syncthreads();
+  }
+  return K;
+}
+
+// Stage 1 of the exact sampler on this CTA: the top K of its slice of the
+// penalized logits (the values ARGMAX_STAGE1_WGSL compares).
+// Not inlined (runs only in exact mode): keeps the step kernels' code small.
+__device__ __noinline__ void phase_topk_local(const CkDev& D, Smem& smu, int cta, int ncta) {
+  const CkState* st = D.st;
+  const bool pen = st->pen_d > 1.0;
+  const float penalty = (float)st->pen_milli / 1000.0f;
+  const int lo = (int)((long long)cta * D.vocab / ncta), hi = (int)((long long)(cta + 1) * D.vocab / ncta);
+  const int K = exact_k(st);
+  auto val = [&](int i) {
+    const uint32_t id = (uint32_t)(lo + i);
+    float v = D.logits[id];
+    if (pen && ((D.pen_mask[id >> 5] >> (id & 31)) & 1u)) v = v > 0.f ? v / penalty : v * penalty;
+    return v;
+  };
+  float* ov = D.xval + (size_t)cta * CK_SAMPLE_MAX;
+  uint32_t* oi = D.xidx + (size_t)cta * CK_SAMPLE_MAX;
+  const int cnt = radix_emit(hi - lo, K, [&](int i) { return fkey(val(i)); },
+                             [&](int i, int p) { ov[p] = val(i); oi[p] = (uint32_t)(lo + i); }, smu.sm);
+  if (threadIdx.x == 0) D.xcnt[cta] = cnt;
+}
+
+// Stage 2 (one CTA, after every CTA's stage 1): the top K of all candidates,
+// ordered by id, then the sampler.
+__device__ __noinline__ void phase_sample_exact(const CkDev& D, Smem& smu, int ncta) {
+  const CkState* st = D.st;
+  SmemSm& s = smu.sm;
+  int* s_off = s.off;
+  int& s_total = s.total;
+  const int tid = threadIdx.x;
+  const int K = exact_k(st);
+  // prefix offsets of the CTAs' lists (CTA order = id order)
+  if (tid == 0) {
+    int t = 0;
+    for (int c = 0; c < ncta && c < 1024; c++) { s_off[c] = t; t += D.xcnt[c]; }
+    s_total = t;
+  }
+  __syncthreads();
+  const int M = s_total;
+  auto at = [&](int j, int& c, int& p) {   // j-th candidate overall -> (CTA, place)
+    int lo = 0, hi = ncta - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (s_off[mid] <= j) lo = mid; else hi = mid - 1;
+    }
+    c = lo;
+    p = j - s_off[lo];
+  };
+  // each CTA's list holds its keys > T_local before its keys == T_local, so
+  // the id order within a list is restored by sorting the final list by id
+  for (int i = tid; i < CK_SAMPLE_MAX; i += CK_THREADS) {
+    s.val[i] = INFINITY;
+    s.idx[i] = 0xffffffffu;
+    s.prob[i] = 4294967296.0;
+  }
+  __syncthreads();
+  const double rp = fmax(st->pen_d, 1e-6);
+  radix_emit(M, K,
+             [&](int j) { int c, p; at(j, c, p); return fkey(D.xval[(size_t)c * CK_SAMPLE_MAX + p]); },
+             [&](int j, int pl) {
+               int c, p;
+               at(j, c, p);
+               const float v = D.xval[(size_t)c * CK_SAMPLE_MAX + p];
+               const uint32_t id = D.xidx[(size_t)c * CK_SAMPLE_MAX + p];
+               s.val[pl] = sample_key(D, v, id, rp);
+               s.idx[pl] = isfinite(s.val[pl]) ? id : 0xffffffffu;
+               s.prob[pl] = (double)id;   // the reference's list order: by id
+             }, s);
+  sample_core(D, s);
+}
 // End of step: clear the penalty set, chain the produced id, advance pos.
 __device__ __forceinline__ void phase_finish(int need_logits, const CkDev& D, int cta, uint32_t ep) {
   if (cta != 0) return;
@@ -1703,17 +1935,26 @@ __device__ __forceinline__ void phase_finish(int need_logits, const CkDev& D, in
   }
 }
 
-// argmax stage 2 -> sampling -> end of step, on CTA 0 in one phase.
-__device__ __forceinline__ void phase_select(int need_logits, const CkDev& D, Smem& sm, int cta, uint32_t ep) {
+// argmax stage 2 -> sampling -> end of step, on CTA 0 in one phase.  `ncta`:
+// the CTAs that ran stage 1 (the exact sampler's candidate lists).
+template <int EXACT>
+__device__ __forceinline__ void phase_select(int need_logits, const CkDev& D, Smem& sm, int cta, uint32_t ep,
+                                             int ncta) {
   if (cta != 0) return;
-  phase_argmax2(D, sm, 0);
-  __syncthreads();
-  phase_sample(D, sm, 0);
+  const CkState* st = D.st;
+  if (EXACT && st->exact && st->sampling && D.xval && ncta <= D.xgrid) {
+    phase_sample_exact(D, sm, ncta);
+  } else {
+    phase_argmax2(D, sm, 0);
+    __syncthreads();
+    phase_sample(D, sm, 0);
+  }
   __syncthreads();
   phase_finish(need_logits, D, 0, ep);
 }
 
 // ---------------------------------------------------------------------------
+template <int EXACT>
 __device__ __forceinline__ void run_phase(const Phase* ph, int i, Smem& sm, Ring& R, const CkDev& D, int cta,
                                           int ncta, int pos, uint32_t ep) {
   const Phase& p = ph[i];
@@ -1726,11 +1967,11 @@ __device__ __forceinline__ void run_phase(const Phase* ph, int i, Smem& sm, Ring
     case PH_EMBED: phase_embed(p.em, D, cta, ncta, pos, ep); break;
     case PH_MATVEC: phase_matvec(p.mv, sm, R, cta, &D.st->err, &D.st->abort_flag, tp, ep); break;
     case PH_ATTN: phase_attn(p.at, sm, D, cta, ncta, pos, tp, ep); break;
-    case PH_ARGMAX1: phase_argmax1(D, sm, cta, ncta); break;
+    case PH_ARGMAX1: phase_argmax1<EXACT>(D, sm, cta, ncta); break;
     case PH_ARGMAX2: phase_argmax2(D, sm, cta); break;
     case PH_SAMPLE: phase_sample(D, sm, cta); break;
     case PH_FINISH: phase_finish(p.need_logits, D, cta, ep); break;
-    case PH_SELECT: phase_select(p.need_logits, D, sm, cta, ep); break;
+    case PH_SELECT: phase_select<EXACT>(p.need_logits, D, sm, cta, ep, ncta); break;
   }
 }
 
@@ -1744,7 +1985,7 @@ __global__ void __launch_bounds__(CK_THREADS, 1) k_mv(const Phase* __restrict__ 
                                ? D.trace + CK_TRACE_MV_BASE + blockIdx.x * 8 : nullptr;
   if (tr) tr[0] = gtimer();
   Ring R;
-  const Phase* sph = launch_start(R, ph, 1, blockIdx.x, &D.st->err, &D.st->abort_flag);
+  const Phase* sph = launch_start(R, ph, 1, blockIdx.x, &D.st->err, &D.st->abort_flag, D.l2_keep);
   if (!sph) return;
   if (tr) tr[1] = gtimer();
   unsigned long long* tp = (D.trace && blockIdx.x == 0 && sph->index < 512)
@@ -1764,11 +2005,11 @@ __global__ void __launch_bounds__(CK_THREADS, 1) k_misc(const Phase* __restrict_
   const uint32_t ep = D.st->epoch;
   switch (p.kind) {
     case PH_EMBED: phase_embed(p.em, D, blockIdx.x, gridDim.x, D.st->pos, ep); break;
-    case PH_ARGMAX1: phase_argmax1(D, sm, blockIdx.x, gridDim.x); break;
+    case PH_ARGMAX1: phase_argmax1<1>(D, sm, blockIdx.x, gridDim.x); break;
     case PH_ARGMAX2: phase_argmax2(D, sm, blockIdx.x); break;
     case PH_SAMPLE: phase_sample(D, sm, blockIdx.x); break;
     case PH_FINISH: phase_finish(p.need_logits, D, blockIdx.x, ep); break;
-    case PH_SELECT: phase_select(p.need_logits, D, sm, blockIdx.x, ep); break;
+    case PH_SELECT: phase_select<1>(p.need_logits, D, sm, blockIdx.x, ep, (ph - 1)->grid); break;
   }
 }
 
@@ -1810,12 +2051,13 @@ __device__ __forceinline__ bool grid_sync(CkState* st, unsigned target) {
 // work is done; a grid barrier remains only where a phase is marked
 // barrier_after (the LM head before argmax stage 1, stage 1 before select),
 // whose outputs are plain.
+template <int EXACT>
 __global__ void __launch_bounds__(CK_THREADS, 1) k_mega(const Phase* __restrict__ ph, int nph, CkDev D) {
   __shared__ Smem sm;
   const int pos = D.st->pos;         // constant for the whole step (phase_finish runs last)
   const uint32_t ep = D.st->epoch;   // read before any CTA can reach the step end
   Ring R;
-  const Phase* sph = launch_start(R, ph, nph, blockIdx.x, &D.st->err, &D.st->abort_flag);
+  const Phase* sph = launch_start(R, ph, nph, blockIdx.x, &D.st->err, &D.st->abort_flag, D.l2_keep);
   if (!sph) return;
   unsigned target = 0;
   const bool tr = D.trace && blockIdx.x == 0 && threadIdx.x == 0;
@@ -1825,7 +2067,7 @@ __global__ void __launch_bounds__(CK_THREADS, 1) k_mega(const Phase* __restrict_
 #pragma unroll 1
   for (int i = 0; i < nph; i++) {
     if (tr && 2 * i + 1 < CK_TRACE_MV_BASE) D.trace[2 * i] = gtimer();
-    run_phase(sph, i, sm, R, D, blockIdx.x, gridDim.x, pos, ep);
+    run_phase<EXACT>(sph, i, sm, R, D, blockIdx.x, gridDim.x, pos, ep);
     if (tr && 2 * i + 1 < CK_TRACE_MV_BASE) D.trace[2 * i + 1] = gtimer();
     if (ct && i >= 1 && i <= 4) ct[i - 1] = gtimer();
     if (!R.ok) return;

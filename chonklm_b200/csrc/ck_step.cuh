@@ -239,7 +239,7 @@ __device__ __forceinline__ bool sk_next_tile(const SkMv& m, int cta, int& seg, i
 // Producer: copy one tile into slot ti % SK_NSLOT once the compute warps
 // have released that slot's previous tile.
 __device__ __forceinline__ void sk_issue_tile(const SkMv& m, const TileList& T, unsigned ti, int* err,
-                                              int* abort_flag) {
+                                              int* abort_flag, int keep) {
   const int s = (int)(ti % SK_NSLOT);
   const unsigned use = ti / SK_NSLOT;
   if (use > 0) sk_wait(sk_empty(s), (use - 1) & 1u, err, abort_flag);
@@ -257,7 +257,7 @@ __device__ __forceinline__ void sk_issue_tile(const SkMv& m, const TileList& T, 
     const int rows = (i + 1 < T.n ? pick3(i + 1, 0, T.st1, T.st2) : T.total) - pick3(i, 0, T.st1, T.st2);
     const SkSeg& S = m.seg[sg];
     bulk_g2s_stream(dst + pick3u(i, T.off0, T.off1, T.off2), S.w + (size_t)r0 * S.L.row_bytes,
-                    (uint32_t)rows * S.L.row_bytes, bar);
+                    (uint32_t)rows * S.L.row_bytes, bar, keep);
   }
 }
 
@@ -904,7 +904,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1) k_step(const SkPhase* __restric
         }
         int seg = 0, row = -1;
         TileList T;
-        while (sk_next_tile(p.mv, cta, seg, row, T)) sk_issue_tile(p.mv, T, ti++, err, ab);
+        while (sk_next_tile(p.mv, cta, seg, row, T)) sk_issue_tile(p.mv, T, ti++, err, ab, D.l2_keep);
       }
       // every issued copy lands before this CTA can exit, even after another
       // CTA gave up (copies from valid addresses always complete; bounded)
@@ -953,7 +953,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1) k_step(const SkPhase* __restric
   unsigned target = ncta;
   if (logits) {
     if (!grid_sync(st, target)) return;    // all logits stored
-    phase_argmax1(D, sm.o, cta, ncta);
+    phase_argmax1<1>(D, sm.o, cta, ncta);
     target += ncta;
   }
   __syncthreads();
@@ -964,6 +964,6 @@ __global__ void __launch_bounds__(SK_THREADS, 1) k_step(const SkPhase* __restric
   }
   __syncthreads();
   if (!s_last) return;
-  if (logits) phase_select(1, D, sm.o, 0, ep);
+  if (logits) phase_select<1>(1, D, sm.o, 0, ep, ncta);
   else phase_finish(0, D, 0, ep);
 }

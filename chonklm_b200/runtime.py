@@ -184,6 +184,10 @@ def generateLlamaWgsl(loaded: LoadedLlamaWgslModel, promptIds: Sequence[int],
                 "topK": opts.get("topK", 0) or 0,
                 "repetitionPenalty": rp}
     seed = int(opts.get("seed", 0))
+    # candidate list of the sampler (an extension of the reference's options):
+    # "chunk" (default) = the reference's per-256 chunk maxima, "exact" = the
+    # top-K of the whole vocabulary (ck_set_sampler)
+    loaded.engine.dev.set_sampler(opts.get("sampler", "chunk") == "exact")
     on_token = opts.get("onToken")
     should_stop = opts.get("shouldStop")
     decode_text = getattr(loaded.tokenizer, "decode", None)

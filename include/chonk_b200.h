@@ -127,6 +127,18 @@ const char* ck_global_error(void);
 /* Use the caller's CUDA stream (cudaStream_t passed as void*); NULL = the
  * engine's own stream.  Lets a caller time steps with its own events. */
 int ck_set_stream(ck_engine* h, void* stream);
+/* Candidate list of the sampler.  0 (default): the reference's, the
+ * per-256-logit chunk maxima of ARGMAX_STAGE1_WGSL that
+ * sampleFromCandidateBuffer (sampling.ts:23-76) reads.  1: exact over the
+ * whole vocabulary, the K largest penalized logits (K = top-k when 1..1024,
+ * else 1024; ties to the lower id), found by a block-level radix select on
+ * every CTA's slice of the vocabulary and once more over their candidates;
+ * temperature, top-k, top-p and the Philox draw then run as in the
+ * reference.  Takes effect at the next step call; greedy steps are not
+ * affected.  No counterpart in the reference (its candidates are the chunk
+ * maxima). */
+int ck_set_sampler(ck_engine* h, int exact);
+
 /* Step implementation: 0 = one persistent cooperative kernel per token
  * (default), 1 = per-op kernels replayed from a CUDA graph. */
 int ck_set_mode(ck_engine* h, int mode);

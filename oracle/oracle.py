@@ -235,6 +235,40 @@ def sampler_probabilities(cand_val: np.ndarray, cand_idx: np.ndarray, temperatur
     return out
 
 
+def exact_candidates(logits: np.ndarray, top_k: int = 0, penalty_ids: Sequence[int] = (),
+                     penalty: float = 1.0):
+    """Candidate list of the engine's exact sampler (ck_set_sampler(h, 1)):
+    the K largest stage-1 values over the whole vocabulary -- the logits with
+    ARGMAX_STAGE1_WGSL's milli-fixed-point penalty on penalized ids
+    (llama-wgsl-runtime.ts:1661, :3665-3690) -- K = top_k when 1..1023, else
+    1024, ties to the lower id, NaN never before a number; returned in id
+    order, as the reference's candidate buffer is ordered."""
+    v = np.asarray(logits, dtype=np.float32).copy()
+    if penalty > 1.0 and len(penalty_ids):
+        pen = np.float32(math.floor(penalty * 1000.0 + 0.5) / 1000.0)
+        ids = np.unique(np.asarray([i for i in penalty_ids if 0 <= i < v.size], dtype=np.int64))
+        pv = v[ids]
+        v[ids] = np.where(pv > 0, pv / pen, pv * pen).astype(np.float32)
+    K = top_k if 0 < top_k < 1024 else 1024
+    K = min(K, v.size)
+    # order-preserving key: NaN lowest; sort by (key desc, id asc)
+    bits = v.view(np.uint32).astype(np.uint64)
+    key = np.where(bits & 0x80000000, (~bits) & 0xFFFFFFFF, bits | 0x80000000)
+    key = np.where(np.isnan(v), 0, key)
+    order = np.lexsort((np.arange(v.size), -key.astype(np.int64)))[:K]
+    order.sort()
+    return v[order], order.astype(np.uint32)
+
+
+def sample_exact(logits: np.ndarray, temperature: float = 0.0, top_p: float = 1.0, top_k: int = 0,
+                 repetition_penalty: float = 1.0, seen_ids: Sequence[int] = (), uniform: Optional[float] = None,
+                 penalty_ids: Sequence[int] = ()) -> int:
+    """The exact sampler: sampleFromCandidateBuffer (sampling.ts:23-76) on
+    exact_candidates instead of the chunk maxima."""
+    cv, ci = exact_candidates(logits, top_k, penalty_ids, repetition_penalty)
+    return sample_from_candidates(cv, ci, temperature, top_p, top_k, repetition_penalty, seen_ids, uniform)
+
+
 def needs_sampling_readback(temperature: float = 0.0, top_p: float = 1.0, top_k: int = 0) -> bool:
     """needsSamplingReadback (sampling.ts:9-16)."""
     k = max(0, int(math.floor(top_k))) if top_k is not None and math.isfinite(top_k) else 0

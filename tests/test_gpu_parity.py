@@ -264,3 +264,58 @@ def test_prefix_reuse_eos_and_errors(tiny_dir):
     assert eng.position == 0
     loaded.engine.dispose()
     loaded2.engine.dispose()
+
+
+@pytest.mark.parametrize("mode", [_lib.MODE_MEGAKERNEL, _lib.MODE_GRAPH, _lib.MODE_STREAM])
+@pytest.mark.parametrize("arch", ["gemma3", "qwen3"])
+def test_exact_sampler_matches_oracle(tiny_dir, arch, mode):
+    """ck_set_sampler(h, 1): the sampled id equals the oracle's exact sampler
+    (top-K of the whole vocabulary by radix select, then
+    sampleFromCandidateBuffer) on the device's own logits with the same
+    Philox draw, in every execution mode."""
+    path = tiny_model(tiny_dir, arch, "q4_k_m")
+    V = _vocab(path)
+    loaded = loadLlamaWgslModel(_def(path, V))
+    eng = loaded.engine.dev
+    eng.set_mode(mode)
+    eng.set_sampler(True)
+    rng = np.random.default_rng(31)
+    hist = []
+    settings = [(1.0, 0.95, 64, 1.0), (0.7, 1.0, 0, 1.3), (1.3, 0.5, 5, 1.0), (1.0, 1.0, 1, 1.0), (2.0, 0.9, 1023, 1.2)]
+    for i, t in enumerate(rng.integers(0, V, size=25).tolist()):
+        hist.append(t)
+        T, p, k, rp = settings[i % len(settings)]
+        s, _ = _lib.make_sampling(T, p, k, rp, seed=77, offset=i)
+        got = eng.run_token(t, True, s)
+        want = oracle.sample_exact(eng.logits(), T, p, k, rp, hist, oracle.philox_uniform(77, i), hist)
+        assert got == want, f"step {i}: {got} != {want}"
+    loaded.engine.dispose()
+
+
+def test_exact_sampled_generation(tiny_dir):
+    """generateLlamaWgsl with {"sampler": "exact"}: every sampled id is the
+    exact sampler's choice on that step's logits (checked by replaying the
+    ids one step at a time), and the default sampler is untouched."""
+    path = tiny_model(tiny_dir, "gemma3", "q4_k_m")
+    V = _vocab(path)
+    loaded = loadLlamaWgslModel(_def(path, V))
+    prompt = np.random.default_rng(33).integers(0, V, size=6).tolist()
+    opts = {"maxNewTokens": 24, "temperature": 1.0, "topK": 64, "topP": 0.95, "seed": 5, "sampler": "exact"}
+    res = generateLlamaWgsl(loaded, prompt, opts)
+    eng = loaded.engine.dev
+    eng.reset()
+    eng.set_sampler(True)
+    for t in prompt[:-1]:
+        eng.run_token(t, False)
+    tok = prompt[-1]
+    for i, want_id in enumerate(res["ids"]):
+        s, _ = _lib.make_sampling(1.0, 0.95, 64, 1.0, seed=5, offset=i)
+        got = eng.run_token(tok, True, s)
+        assert got == want_id
+        assert got == oracle.sample_exact(eng.logits(), 1.0, 0.95, 64, 1.0, [], oracle.philox_uniform(5, i))
+        tok = got
+    # the reference sampler is back for calls that do not ask for it
+    res2 = generateLlamaWgsl(loaded, prompt, {k: v for k, v in opts.items() if k != "sampler"})
+    orc = oracle.OracleModel(path, max_context=256)
+    assert res2["ids"] == oracle.generate(orc, prompt, 24, temperature=1.0, top_k=64, top_p=0.95, seed=5)
+    loaded.engine.dispose()
