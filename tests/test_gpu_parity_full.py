@@ -25,7 +25,7 @@ import numpy as np
 import pytest
 
 from chonklm_b200.registry import ModelDef
-from chonklm_b200.runtime import generateLlamaWgsl, loadLlamaWgslModel
+from chonklm_b200.runtime import generateLlamaWgsl, loadLlamaWgslModel, resetLlamaWgslConversation
 from chonklm_b200.synth import SPECS, write_synthetic_gguf
 from oracle import oracle
 
@@ -172,6 +172,9 @@ def test_full_depth_gemma_sampled_64(full_dir):
         assert r < LOGIT_TOL, f"step {i}: candidate values rel err {r}"
         seq.append(got)
         tok = got
+    # the loop above drove the engine directly, so the runtime's token cache
+    # does not describe it: start the runtime from an empty context
+    resetLlamaWgslConversation(loaded)
     res = generateLlamaWgsl(loaded, prompt, {"maxNewTokens": 64, "temperature": T, "topK": K, "topP": P,
                                              "seed": seed})
     assert res["ids"] == seq
