@@ -505,8 +505,15 @@ def main():
     w0, kv0 = eng.step_bytes()
     eng.truncate(prompt_len)
 
+    # L2 (126 MB) is flushed before every step, outside the timed events, by
+    # writing a 256 MB buffer on the step's stream: a model whose weights fit
+    # in L2 (SmolLM2, ~107 MB) starts each step from HBM like the others
+    l2_flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+
     def one_step():
         eng.truncate(prompt_len)
+        with torch.cuda.stream(stream):
+            l2_flush.fill_(1)
         ev0 = torch.cuda.Event(enable_timing=True)
         ev1 = torch.cuda.Event(enable_timing=True)
         ev0.record(stream)
@@ -647,7 +654,9 @@ def main():
             "config": {"workload": args.config, "prompt": prompt_len, "generated": gen,
                        "weights": "N(0,0.02) seed 0, Q4_K_M mixture", "kv_cache": "fp16",
                        "mode": "megakernel" if args.mode == 0 else "graph",
-                       "l2": "inputs larger than L2 (weights %.0f MB per token > 126 MB L2)" % (w0 / 1e6),
+                       "l2": ("L2 flushed before every timed step (256 MB write); weights %.0f MB per token %s "
+                              "126 MB L2, re-read by each of the step's %d tokens"
+                              % (w0 / 1e6, ">" if w0 > 126e6 else "<", gen)),
                        "parallelism": f"replicas x{world}"},
             "e2e": {"value": round(e2e_value, 2), "unit": "tok/s",
                     "h2d_bytes_per_step": int(statistics.mean(x[0] for x in e2e_io)),

@@ -5,8 +5,8 @@
 //
 // One CTA per SM; CTA c owns rows [c*n/grid, (c+1)*n/grid).  Warp 15 copies
 // the CTA's rows, a slot at a time, into a ring of GV_NSLOT shared-memory
-// slots (cp.async.bulk completing on the slot's mbarrier, L2 evict-first, no
-// multicast); warps 0..14 take each slot's rows three at a time per warp.
+// slots (cp.async.bulk into this CTA's own shared memory, completing on the
+// slot's mbarrier, L2 evict-first); warps 0..14 take each slot's rows three at a time per warp.
 // Each kernel instance is compiled for one block type, so a unit's decode is
 // straight-line code, and x (quantized per 32 elements into X = hi * 256 +
 // lo, as XUnit describes) sits in shared memory in 16-byte chunks that the

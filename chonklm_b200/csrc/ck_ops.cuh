@@ -501,8 +501,8 @@ __device__ __forceinline__ void load_xunit(const SmemMv& s, int c, XUnit& x) {
 // Weight streaming: each CTA owns a contiguous row range of every matvec
 // segment (rows are self-contained and 16-byte aligned in the device layout),
 // packed into tiles of at most CK_TILE_BYTES.  One issuer thread copies tiles into a
-// two-buffer shared-memory ring with cp.async.bulk (TMA bulk copy, no
-// multicast) completing on an mbarrier; the ring runs ahead across phases, so
+// two-buffer shared-memory ring with cp.async.bulk (TMA bulk copy into this
+// CTA's own shared memory) completing on an mbarrier; the ring runs ahead across phases, so
 // the next matvec's weights are in flight while this CTA is in a grid barrier
 // or an attention phase.  Consumers read the tile from shared memory.
 #define CK_ISSUER (CK_THREADS - 32)   // lane 0 of the last warp copies tiles

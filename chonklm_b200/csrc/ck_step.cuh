@@ -8,8 +8,8 @@
 //
 // * Weights.  Warp 15 of every CTA is a producer: it walks the phases ahead
 //   of the compute warps and copies the CTA's rows of every matvec into a
-//   ring of SK_NSLOT shared-memory slots (cp.async.bulk, no multicast,
-//   completing on the slot's mbarrier), limited only by free slots, so a
+//   ring of SK_NSLOT shared-memory slots (cp.async.bulk into this CTA's
+//   own shared memory, completing on the slot's mbarrier), limited only by free slots, so a
 //   phase's weights are resident before its input exists.  The compute
 //   warps release a slot through its "empty" mbarrier.
 // * Hand-offs.  Every activation element is a 64-bit word, value low and
