@@ -42,6 +42,7 @@ const lib = dlopen(process.env.CHONK_B200_LIB ?? "libchonk_b200.so", {
     returns: FFIType.i32,
   },
   ck_reset: { args: [FFIType.ptr], returns: FFIType.i32 },
+  ck_set_sampler: { args: [FFIType.ptr, FFIType.i32], returns: FFIType.i32 },
   ck_position: { args: [FFIType.ptr, FFIType.ptr], returns: FFIType.i32 },
   ck_destroy: { args: [FFIType.ptr], returns: FFIType.i32 },
   ck_last_error: { args: [FFIType.ptr], returns: FFIType.cstring },
@@ -164,6 +165,12 @@ export class CudaEngine {
     check(this.h, S.ck_reset(this.h));
   }
 
+  // candidates of the sampler: false = the 256-chunk maxima (the reference's),
+  // true = the top K of the whole vocabulary (device radix select)
+  setExactSampler(exact: boolean): void {
+    check(this.h, S.ck_set_sampler(this.h, exact ? 1 : 0));
+  }
+
   get position(): number {
     const p = new Int32Array(1);
     check(this.h, S.ck_position(this.h, ptr(p)));
@@ -230,6 +237,7 @@ export interface GenerateLlamaCudaOptions {
   topK?: number;
   repetitionPenalty?: number;
   seed?: number;   // Philox key: the draws replace Math.random
+  sampler?: "chunk" | "exact";   // candidate list (an extension; "chunk" is the reference's)
   onToken?: (info: { id: number; text: string; cumulative: string }) => void;
   shouldStop?: () => boolean;
 }
@@ -260,6 +268,7 @@ export async function generateLlamaCuda(
     repetitionPenalty: opts.repetitionPenalty ?? d.defaultRepetitionPenalty ?? 1,
   };
   const sampled = needsSamplingReadback(sampling);
+  eng.setExactSampler(opts.sampler === "exact");
   let draws = 0;
   const mk = () => packSampling({ ...sampling, seed: opts.seed ?? 0 }, draws);
   const decodeText = (ids: number[]) => (loaded.tokenizer ? loaded.tokenizer.decode(ids) : "");
