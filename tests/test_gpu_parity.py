@@ -66,11 +66,13 @@ def test_dequant_bit_exact(t, kind):
         f"{np.count_nonzero(gpu.view(np.uint32) != ref.view(np.uint32))} weights differ"
 
 
-@pytest.mark.parametrize("t", QTYPES)
-@pytest.mark.parametrize("k,n", [(256, 7), (576, 130), (1024, 1000), (1536, 77), (2048, 333), (3072, 1024)])
+MV_SHAPES = [(256, 7), (576, 130), (1024, 1000), (1536, 77), (2048, 333), (3072, 1024)]
+_KQUANTS = (GGML_TYPE.Q4_K, GGML_TYPE.Q6_K)
+
+
+@pytest.mark.parametrize("t,k,n", [(t, k, n) for t in QTYPES for k, n in MV_SHAPES
+                                   if not (t in _KQUANTS and k % 256)])
 def test_matvec(t, k, n):
-    if t in (GGML_TYPE.Q4_K, GGML_TYPE.Q6_K) and k % 256:
-        pytest.skip("K-quants need k % 256 == 0")
     data = _blocks(t, k, n, k + n)
     rng = np.random.default_rng(k * n)
     x = rng.standard_normal(k).astype(np.float32)
@@ -78,6 +80,15 @@ def test_matvec(t, k, n):
     ref = oracle.matvec(t, np.frombuffer(data, np.uint8), k, n, x, oracle.MODE_F64)
     err = np.abs(y - ref).max() / np.abs(ref).max()
     assert err < 1e-4, err
+
+
+@pytest.mark.parametrize("t", _KQUANTS)
+def test_matvec_rejects_partial_super_blocks(t):
+    """A K-quant row is whole 256-weight super-blocks (the reference's
+    Q4_K / Q6_K shaders index them so): k = 576 is refused with an error,
+    not computed."""
+    with pytest.raises(_lib.CkError, match="requires 256-element rows"):
+        _lib.matvec(t, bytes(130 * 3 * 210), 576, 130, np.ones(576, np.float32))
 
 
 def _def(path, vocab, kv="float16", ctx=256, eos=()):
