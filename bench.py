@@ -269,6 +269,31 @@ def matvec_report(path, peak):
     return out
 
 
+def phase_profile(eng, layers: int) -> dict:
+    """CTA 0's view of one megakernel decode step (ck_trace globaltimer stamps
+    around each phase, read after four traced steps): the mean duration of
+    each phase kind over the layers.  A phase's time includes its wait for
+    the previous phase's slowest producer."""
+    import numpy as np
+    eng.trace(True)
+    eng.enqueue_decode_steps(4)
+    eng.sync()
+    tr = eng.trace_read(4096).astype(np.int64)
+    eng.trace(False)
+    n = 0
+    while n < 2048 and tr[2 * n] != 0:
+        n += 1
+    dur = (tr[1:2 * n:2] - tr[0:2 * n:2]) / 1000.0
+    kinds = ["qkv", "attn", "o", "gate_up", "down"]
+    if n != 1 + 5 * layers + 3:
+        return {"phases": n, "total_us": round(float(dur.sum()), 1)}
+    per = {k: round(float(np.mean(dur[1 + j:1 + 5 * layers:5])), 2) for j, k in enumerate(kinds)}
+    return {"phases": n, "total_us": round(float((tr[2 * n - 1] - tr[0]) / 1000.0), 1),
+            "per_layer_mean_us": per, "embed_us": round(float(dur[0]), 2),
+            "lm_head_us": round(float(dur[n - 3]), 2), "argmax1_us": round(float(dur[n - 2]), 2),
+            "select_us": round(float(dur[n - 1]), 2)}
+
+
 def run_gemma_text(args, rank: int, world: int, barrier, local: int, dist) -> None:
     """Config 4's model through the text API (gemma-runtime.ts interface,
     chonklm_b200.gemma_runtime): a fixed user message, 256 sampled ids
@@ -384,6 +409,9 @@ def main():
     ap.add_argument("--prefill-profile", type=int, default=0, metavar="N",
                     help="profiling run for ncu: N tensor-core prefills of the config's prompt (the first one "
                          "formats the operand tiles), then exit")
+    ap.add_argument("--matvec-profile", type=int, default=0, metavar="N",
+                    help="profiling run for ncu: N launches of the streaming matvec kernel on the config's LM "
+                         "head (copies rotated past L2), then exit")
     ap.add_argument("--profile", type=int, default=0, metavar="N",
                     help="profiling run for ncu: prefill the prompt (megakernel), decode N tokens in --mode, "
                          "print nothing else")
@@ -489,6 +517,17 @@ def main():
                           "next_id": int(nid)}), flush=True)
         loaded.engine.dispose()
         return
+    if args.matvec_profile:
+        from chonklm_b200.gguf import ByteSource, fetch_gguf_header
+        src = ByteSource(path)
+        g = fetch_gguf_header(src)
+        t = g.tensor_map.get("output.weight") or g.tensor_map.get("token_embd.weight")
+        us = _lib.bench_matvec(t.type, src.read(g.data_offset + t.offset, t.n_bytes), t.shape[0], t.shape[1],
+                               reps=args.matvec_profile)
+        print(json.dumps({"matvec_profile": args.config, "type": t.type, "k": t.shape[0], "n": t.shape[1],
+                          "launches": args.matvec_profile, "us": round(us, 2)}), flush=True)
+        loaded.engine.dispose()
+        return
     if args.profile:
         eng.set_mode(0)
         nid = eng.prefill(prompt, True, samp)
@@ -540,6 +579,8 @@ def main():
     eng.truncate(prompt_len + gen - 1)
     w1, kv1 = eng.step_bytes()
     bytes_per_token = w0 + 0.5 * (kv0 + kv1)
+
+    phases = phase_profile(eng, S.layers) if (rank == 0 and args.mode == 0) else None
 
     # ---- e2e through generateLlamaWgsl -------------------------------------
     e2e_times = []
@@ -672,6 +713,7 @@ def main():
             "matvec": mv,
             "batched": batched,
             "prefill": prefill,
+            "phases": phases,
             "clocks": clk.summary(),
             "gpu_launches": int(launches_per_token * gen * args.steps),
             "decode_ids_head": ids0[:8],

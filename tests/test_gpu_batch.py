@@ -102,6 +102,28 @@ def test_batch_matches_oracle_greedy(tiny_dir, arch, kw):
     loaded.engine.dispose()
 
 
+@pytest.mark.parametrize("arch,kw", [("llama", {}), ("llama", {"heads": 6, "kv_heads": 2}),
+                                     ("qwen3", {"head_dim": 128})])
+def test_batch_long_sequences(tiny_dir, arch, kw):
+    """Sequences past 128 positions (prompt + generated up to 240): the
+    attention kernels' multi-round position loop (128 positions per round in
+    the grouped-heads kernel) and the merge across rounds, against the
+    oracle's greedy ids."""
+    from chonklm_b200 import _lib
+    path = tiny_model(tiny_dir, arch, "q4_k_m", **kw)
+    loaded, V = _engine(path)
+    rng = np.random.default_rng(11)
+    pending = [(rng.integers(0, V, size=n).tolist(), m, ()) for n, m in ((150, 90), (129, 40), (200, 40), (60, 120))]
+    batch = _lib.Batch(loaded.engine.dev, max_seqs=3)
+    got = _run(batch, pending)
+    orc = oracle.OracleModel(path, max_context=256)
+    for (prompt, max_new, _), ids in zip(pending, got):
+        orc.reset()
+        assert ids == oracle.generate(orc, prompt, max_new), (len(prompt), max_new)
+    batch.close()
+    loaded.engine.dispose()
+
+
 def test_batch_eos_and_limits(tiny_dir):
     from chonklm_b200 import _lib
     path = tiny_model(tiny_dir, "llama", "q4_k_m")
