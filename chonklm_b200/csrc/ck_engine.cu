@@ -108,6 +108,7 @@ struct ck_engine {
   ck_prefill_state* pf = nullptr;
   int pf_min = 64, pf_chunk = 0;
   int sampler_exact = 0;      // ck_set_sampler
+  const void* mega_fn = nullptr;   // the k_mega instantiation for this model (mega_kernel)
 
   int fail(int code, const char* fmt, ...) {
     char buf[512];
@@ -591,6 +592,46 @@ int sk_setup(ck_engine* h) {
   return CK_OK;
 }
 
+// A k_mega instantiation compiled for the headline model family (Qwen3
+// Q4_K_M: Q4_K and Q6_K weights, head_dim 128, fp16 cache): it only leaves
+// out code for the types and head sizes the model does not have, so its
+// results are the generic kernel's bit for bit, and it decodes ~2 % faster
+// (906 vs 922 us per token).  Compiled the same way, the SmolLM2, Gemma-3
+// and Q8_0 families measured 0.5-4 % slower than the generic kernel, so they
+// run the generic one.
+#define CK_TM_KQ (CK_TM(GT_Q4_K) | CK_TM(GT_Q6_K))
+struct MegaVariant {
+  unsigned tm;
+  int ae;
+  const void* fn;
+};
+const MegaVariant kMegaVariants[] = {
+    {CK_TM_KQ, 4, (const void*)k_mega<0, CK_TM_KQ, 4>},
+};
+const void* const kMegaGeneric = (const void*)k_mega<0, CK_TM_ALL, 0>;
+const void* const kMegaExact = (const void*)k_mega<1, CK_TM_ALL, 0>;
+
+unsigned model_type_mask(const ck_engine* h) {
+  unsigned m = CK_TM(h->head.L.type);
+  for (int i = 0; i < h->cfg.layers; i++) {
+    const LayerW& W = h->L[i];
+    for (const Weight* w : {&W.q, &W.k, &W.v, &W.o, &W.gate, &W.up, &W.down})
+      if (w->present) m |= CK_TM(w->L.type);
+  }
+  return m;
+}
+
+const void* mega_kernel(const ck_engine* h) {
+  const char* g = getenv("CK_MEGA_GENERIC");
+  if (g && atoi(g) != 0) return kMegaGeneric;
+  const ck_model_cfg& c = h->cfg;
+  const int ae = c.kv_dtype != CK_KV_F16 ? 0 : c.head_dim == 64 ? 2 : c.head_dim == 128 ? 4 : c.head_dim == 256 ? 8 : 0;
+  const unsigned m = model_type_mask(h);
+  for (const MegaVariant& v : kMegaVariants)
+    if (v.ae == ae && (m & ~v.tm) == 0) return v.fn;
+  return kMegaGeneric;
+}
+
 int enqueue_phases(ck_engine* h, bool logits, int mode, cudaStream_t s) {
   const std::vector<Phase>& ph = logits ? h->ph_logits : h->ph_prefill;
   if (mode == 2) {
@@ -619,7 +660,7 @@ int enqueue_phases(ck_engine* h, bool logits, int mode, cudaStream_t s) {
   size_t dyn = CK_DYN_PHASES + ph.size() * sizeof(Phase);
   // k_mega<1> carries the exact sampler; the default instantiation leaves it
   // out so the greedy / chunk-sampler step keeps its registers and stack.
-  const void* fn = (logits && h->sampler_exact) ? (const void*)k_mega<1> : (const void*)k_mega<0>;
+  const void* fn = (logits && h->sampler_exact) ? kMegaExact : h->mega_fn;
   CKC(h, cudaLaunchCooperativeKernel(fn, dim3(h->mega_grid), dim3(CK_THREADS), args, dyn, s));
   return CK_OK;
 }
@@ -930,11 +971,13 @@ int ck_finalize(ck_engine* h) {
   if (h->ph_logits.size() * sizeof(Phase) > CK_PHASE_SMEM_MAX)
     return h->fail(CK_EINVAL, "%zu decode phases exceed the %d-byte descriptor stage", h->ph_logits.size(),
                    CK_PHASE_SMEM_MAX);
-  CKC(h, cudaFuncSetAttribute(k_mega<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, CK_DYN_SMEM_MAX));
-  CKC(h, cudaFuncSetAttribute(k_mega<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, CK_DYN_SMEM_MAX));
+  CKC(h, cudaFuncSetAttribute(kMegaGeneric, cudaFuncAttributeMaxDynamicSharedMemorySize, CK_DYN_SMEM_MAX));
+  CKC(h, cudaFuncSetAttribute(kMegaExact, cudaFuncAttributeMaxDynamicSharedMemorySize, CK_DYN_SMEM_MAX));
+  for (const MegaVariant& v : kMegaVariants)
+    CKC(h, cudaFuncSetAttribute(v.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, CK_DYN_SMEM_MAX));
   CKC(h, cudaFuncSetAttribute(k_mv, cudaFuncAttributeMaxDynamicSharedMemorySize, CK_DYN_SMEM_MAX));
   int per_sm = 0;
-  CKC(h, cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_mega<1>, CK_THREADS,
+  CKC(h, cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kMegaExact, CK_THREADS,
                                                        CK_DYN_PHASES + h->ph_logits.size() * sizeof(Phase)));
   int want = 1;
   const char* w = getenv("CK_MEGA_CTAS_PER_SM");
@@ -942,6 +985,7 @@ int ck_finalize(ck_engine* h) {
   if (want < 1) want = 1;
   if (per_sm < 1) return h->fail(CK_ECUDA, "megakernel does not fit on an SM");
   h->mega_grid = h->sms * (want < per_sm ? want : per_sm);
+  h->mega_fn = mega_kernel(h);
   for (int l = 0; l < 2; l++) {
     std::vector<Phase> mp = l ? h->ph_logits : h->ph_prefill;
     for (Phase& p : mp) set_partition(p, h->mega_grid);

@@ -290,7 +290,7 @@ __global__ void __launch_bounds__(GV_THREADS, 1) k_gemv(const uint8_t* __restric
   if (tid == 0) {
     for (int i = 0; i < GV_NSLOT; i++) {
       mbar_init(full + i, 1);
-      mbar_init(empty + i, 1);
+      mbar_init(empty + i, GV_NCW);   // one arrival per compute warp
     }
     mbar_fence_init();
   }
@@ -328,8 +328,11 @@ __global__ void __launch_bounds__(GV_THREADS, 1) k_gemv(const uint8_t* __restric
     const int r = lo + t * tile_rows;
     if (pairs) gv_tile_q4k_pairs(dyn + (size_t)sl * GV_SLOT_BYTES, L, min(tile_rows, hi - r), r, x0, x1, y);
     else gv_tile<TYPE>(dyn + (size_t)sl * GV_SLOT_BYTES, L, min(tile_rows, hi - r), r, s, x0, y);
-    gv_bar();   // every compute thread is done with the slot
-    if (tid == 0) mbar_arrive(empty + sl);
+    // this warp is done with the slot (its loads have been consumed): it
+    // hands it back on its own and moves on; the copy warp refills the slot
+    // once all 15 have arrived
+    __syncwarp();
+    if (lane == 0) mbar_arrive(empty + sl);
   }
 }
 

@@ -322,9 +322,30 @@ struct U8 {
 
 __device__ __forceinline__ float h2f_u16(uint32_t b) { return __half2float(__ushort_as_half((unsigned short)(b & 0xFFFFu))); }
 
-template <bool G>
+// Sets of block types as bit masks (bit t = GGML type t).  A kernel compiled
+// for a set only decodes the types in it: ck_fold_type maps a type to itself
+// when it is in the set and to the set's first type otherwise (the host
+// picks such a kernel only for models whose types are all in the set), so
+// the compiler keeps only the set's arms of a switch over the result.
+#define CK_TM(t) (1u << (t))
+#define CK_TM_ALL (CK_TM(GT_Q4_K) | CK_TM(GT_Q6_K) | CK_TM(GT_Q8_0) | CK_TM(GT_Q5_0) | CK_TM(GT_Q5_1))
+template <unsigned TM>
+__device__ __forceinline__ int ck_fold_type(int type) {
+  if (TM == CK_TM_ALL) return type;
+  int r = (TM & CK_TM(GT_Q4_K)) ? GT_Q4_K
+        : (TM & CK_TM(GT_Q6_K)) ? GT_Q6_K
+        : (TM & CK_TM(GT_Q8_0)) ? GT_Q8_0
+        : (TM & CK_TM(GT_Q5_0)) ? GT_Q5_0 : GT_Q5_1;
+  if ((TM & CK_TM(GT_Q6_K)) && type == GT_Q6_K) r = GT_Q6_K;
+  if ((TM & CK_TM(GT_Q8_0)) && type == GT_Q8_0) r = GT_Q8_0;
+  if ((TM & CK_TM(GT_Q5_0)) && type == GT_Q5_0) r = GT_Q5_0;
+  if ((TM & CK_TM(GT_Q5_1)) && type == GT_Q5_1) r = GT_Q5_1;
+  return r;
+}
+
+template <bool G, unsigned TM = CK_TM_ALL>
 __device__ __forceinline__ void unpack_unit(int type, const uint8_t* row, const Lay& L, int c, U8& u) {
-  switch (type) {  // folds away when `type` is a compile-time constant
+  switch (ck_fold_type<TM>(type)) {  // folds away when `type` is a compile-time constant
     case GT_Q4_K: {
       uint4 w = ld16<G>(row + L.off_q + 16 * c);
       uint4 hd = ld16<G>(row + L.off_sc + 16 * (c >> 3));

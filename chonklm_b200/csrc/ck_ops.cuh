@@ -777,7 +777,7 @@ struct MvStep {
   int sg[R], orow[R];
 };
 
-template <bool ONE>
+template <bool ONE, unsigned TM>
 __device__ __forceinline__ void step_unpack(const MvPhase& P, const uint8_t* tb, const TileList& T, int t,
                                             MvStep<ONE>& w) {
   const int lane = threadIdx.x & 31;
@@ -796,7 +796,7 @@ __device__ __forceinline__ void step_unpack(const MvPhase& P, const uint8_t* tb,
 #pragma unroll
       for (int j = 0; j < MvStep<ONE>::UPL; j++) {
         const int c = lane + 32 * j;
-        if (c < U) unpack_unit<false>(type, row, S.L, c, w.u[i][j]);
+        if (c < U) unpack_unit<false, TM>(type, row, S.L, c, w.u[i][j]);
       }
     }
   }
@@ -859,7 +859,7 @@ __device__ __forceinline__ void step_dot(const MvPhase& P, const TileList& T, in
 // Warp steps t0, t0 + R*CK_WARPS, ... of a tile.  With 2-3 units per lane
 // each unit is unpacked and dotted in turn (its x unit read from shared
 // memory), which keeps a single unpacked unit live.
-template <bool ONE>
+template <bool ONE, unsigned TM>
 __device__ __forceinline__ void mv_tile(const MvPhase& P, const uint8_t* tb, const TileList& T, int t0,
                                         SmemMv& s, const XUnit& x0, float xscale, int cta, uint32_t ep, int* err,
                                         int* abort_flag) {
@@ -867,7 +867,7 @@ __device__ __forceinline__ void mv_tile(const MvPhase& P, const uint8_t* tb, con
   if (ONE) {
     for (int t = t0; t < T.total; t += R * CK_WARPS) {
       MvStep<true> w;
-      step_unpack<true>(P, tb, T, t, w);
+      step_unpack<true, TM>(P, tb, T, t, w);
       step_dot<true>(P, T, t, w, s, x0, xscale, cta, ep, err, abort_flag);
     }
     return;
@@ -888,7 +888,7 @@ __device__ __forceinline__ void mv_tile(const MvPhase& P, const uint8_t* tb, con
       const int c = lane + 32 * j;
       if (c < U) {
         U8 u;
-        unpack_unit<false>(type, row, S.L, c, u);
+        unpack_unit<false, TM>(type, row, S.L, c, u);
         XUnit xj;
         load_xunit(s, c, xj);
         acc += unit_dot8(u, xj);
@@ -992,7 +992,7 @@ __device__ float prologue_quant(const Pro& p, int k, const float (&va)[GPW], con
 
 // One matvec phase on this CTA.  GPW = 32-groups of x per warp (k <= 512 *
 // GPW); ONE (k <= 1024) keeps the lane's x unit in registers.
-template <int GPW>
+template <int GPW, unsigned TM>
 __device__ __forceinline__ void mv_run_t(const MvPhase& P, SmemMv& s, Ring& R, int cta, int* err, int* abort_flag,
                                          unsigned long long* tp, uint32_t ep) {
   constexpr bool ONE = GPW <= 2;
@@ -1019,7 +1019,7 @@ __device__ __forceinline__ void mv_run_t(const MvPhase& P, SmemMv& s, Ring& R, i
   do {
     if (!ring_wait(R, err, abort_flag)) { R.ok = 0; return; }
     if (first) stage_mark(tp, 2);
-    mv_tile<ONE>(P, ring_buf(R.consumed), T, warp, s, x0, xscale, cta, ep, err, abort_flag);
+    mv_tile<ONE, TM>(P, ring_buf(R.consumed), T, warp, s, x0, xscale, cta, ep, err, abort_flag);
     if (first) stage_mark(tp, 3);
     first = false;
     ring_release(R, cta);
@@ -1037,17 +1037,19 @@ __device__ __forceinline__ void mv_run_t(const MvPhase& P, SmemMv& s, Ring& R, i
   stage_mark(tp, 4);
 }
 
+template <unsigned TM>
 __device__ __forceinline__ void mv_run(const MvPhase& P, SmemMv& s, Ring& R, int cta, int* err, int* abort_flag,
                                        unsigned long long* tp, uint32_t ep) {
   const int U = P.k >> 5;
-  if (U <= 2 * CK_WARPS) mv_run_t<2>(P, s, R, cta, err, abort_flag, tp, ep);
-  else if (U <= 4 * CK_WARPS) mv_run_t<4>(P, s, R, cta, err, abort_flag, tp, ep);
-  else mv_run_t<CK_KMAX / 32 / CK_WARPS>(P, s, R, cta, err, abort_flag, tp, ep);
+  if (U <= 2 * CK_WARPS) mv_run_t<2, TM>(P, s, R, cta, err, abort_flag, tp, ep);
+  else if (U <= 4 * CK_WARPS) mv_run_t<4, TM>(P, s, R, cta, err, abort_flag, tp, ep);
+  else mv_run_t<CK_KMAX / 32 / CK_WARPS, TM>(P, s, R, cta, err, abort_flag, tp, ep);
 }
 
+template <unsigned TM = CK_TM_ALL>
 __device__ __forceinline__ void phase_matvec(const MvPhase& P, Smem& sm, Ring& R, int cta, int* err,
                                              int* abort_flag, unsigned long long* tp, uint32_t ep) {
-  mv_run(P, sm.mv, R, cta, err, abort_flag, tp, ep);
+  mv_run<TM>(P, sm.mv, R, cta, err, abort_flag, tp, ep);
 }
 
 // ---------------------------------------------------------------------------
@@ -1508,6 +1510,9 @@ __device__ __forceinline__ void attn_prefetch(const AttnPhase& P, int cta, int n
   }
 }
 
+// AE: 0 = head_dim and cache type dispatched at run time; 2 / 4 / 8 = only
+// head_dim 32 * AE with an fp16 cache (the host guarantees it).
+template <int AE = 0>
 __device__ __forceinline__ void phase_attn(const AttnPhase& P, Smem& sm, const CkDev& D, int cta, int ncta, int pos,
                                            unsigned long long* tp, uint32_t ep) {
   int* err = &D.st->err;
@@ -1518,7 +1523,9 @@ __device__ __forceinline__ void phase_attn(const AttnPhase& P, Smem& sm, const C
   for (int u = cta; u < units; u += ncta) {
     int kvh = u % P.kvh, split = u / P.kvh;
     unsigned long long* up = (tp && u == cta) ? tp : nullptr;
-    if (P.kv_f32) {
+    if constexpr (AE != 0) {
+      attn_unit<(AE ? AE : 2), false>(P, sm.at, kvh, split, pos, up, ep, err, ab);
+    } else if (P.kv_f32) {
       if (P.hd == 64) attn_unit<2, true>(P, sm.at, kvh, split, pos, up, ep, err, ab);
       else if (P.hd == 128) attn_unit<4, true>(P, sm.at, kvh, split, pos, up, ep, err, ab);
       else attn_unit<8, true>(P, sm.at, kvh, split, pos, up, ep, err, ab);
@@ -1954,7 +1961,7 @@ __device__ __forceinline__ void phase_select(int need_logits, const CkDev& D, Sm
 }
 
 // ---------------------------------------------------------------------------
-template <int EXACT>
+template <int EXACT, unsigned TM, int AE>
 __device__ __forceinline__ void run_phase(const Phase* ph, int i, Smem& sm, Ring& R, const CkDev& D, int cta,
                                           int ncta, int pos, uint32_t ep) {
   const Phase& p = ph[i];
@@ -1965,8 +1972,8 @@ __device__ __forceinline__ void run_phase(const Phase* ph, int i, Smem& sm, Ring
   if (p.kind == PH_MATVEC && ph[i + 1].kind == PH_ATTN) attn_prefetch(ph[i + 1].at, cta, ncta, pos);
   switch (p.kind) {
     case PH_EMBED: phase_embed(p.em, D, cta, ncta, pos, ep); break;
-    case PH_MATVEC: phase_matvec(p.mv, sm, R, cta, &D.st->err, &D.st->abort_flag, tp, ep); break;
-    case PH_ATTN: phase_attn(p.at, sm, D, cta, ncta, pos, tp, ep); break;
+    case PH_MATVEC: phase_matvec<TM>(p.mv, sm, R, cta, &D.st->err, &D.st->abort_flag, tp, ep); break;
+    case PH_ATTN: phase_attn<AE>(p.at, sm, D, cta, ncta, pos, tp, ep); break;
     case PH_ARGMAX1: phase_argmax1<EXACT>(D, sm, cta, ncta); break;
     case PH_ARGMAX2: phase_argmax2(D, sm, cta); break;
     case PH_SAMPLE: phase_sample(D, sm, cta); break;
@@ -2051,7 +2058,10 @@ __device__ __forceinline__ bool grid_sync(CkState* st, unsigned target) {
 // work is done; a grid barrier remains only where a phase is marked
 // barrier_after (the LM head before argmax stage 1, stage 1 before select),
 // whose outputs are plain.
-template <int EXACT>
+// EXACT: the whole-vocabulary sampler is compiled in; TM / AE: the block
+// types and the attention shape compiled in (CK_TM_ALL / 0: all, chosen at
+// run time), see mega_kernel on the host.
+template <int EXACT, unsigned TM, int AE>
 __global__ void __launch_bounds__(CK_THREADS, 1) k_mega(const Phase* __restrict__ ph, int nph, CkDev D) {
   __shared__ Smem sm;
   const int pos = D.st->pos;         // constant for the whole step (phase_finish runs last)
@@ -2067,7 +2077,7 @@ __global__ void __launch_bounds__(CK_THREADS, 1) k_mega(const Phase* __restrict_
 #pragma unroll 1
   for (int i = 0; i < nph; i++) {
     if (tr && 2 * i + 1 < CK_TRACE_MV_BASE) D.trace[2 * i] = gtimer();
-    run_phase<EXACT>(sph, i, sm, R, D, blockIdx.x, gridDim.x, pos, ep);
+    run_phase<EXACT, TM, AE>(sph, i, sm, R, D, blockIdx.x, gridDim.x, pos, ep);
     if (tr && 2 * i + 1 < CK_TRACE_MV_BASE) D.trace[2 * i + 1] = gtimer();
     if (ct && i >= 1 && i <= 4) ct[i - 1] = gtimer();
     if (!R.ok) return;

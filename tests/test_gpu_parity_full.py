@@ -110,6 +110,31 @@ def test_full_width_teacher_forced_logits(full_dir, case):
     loaded.engine.dispose()
 
 
+@pytest.mark.parametrize("spec_name", ["qwen3-0.6b"])
+def test_specialised_megakernel_bitwise(full_dir, spec_name, monkeypatch):
+    """The Qwen3 Q4_K_M family runs a megakernel compiled for its block
+    types and head size; it leaves out code only, so its logits and ids are
+    the generic kernel's (CK_MEGA_GENERIC=1) bit for bit."""
+    path = _model(full_dir, spec_name, layers=2)
+    V = SPECS[spec_name].vocab
+    toks = np.random.default_rng(31).integers(0, V, size=12).tolist()
+    outs = []
+    for generic in ("0", "1"):
+        monkeypatch.setenv("CK_MEGA_GENERIC", generic)   # read when the engine is finalized
+        loaded = _load(path, spec_name, 256)
+        eng = loaded.engine.dev
+        eng.set_mode(0)
+        ids, lgs = [], []
+        for t in toks:
+            ids.append(eng.run_token(t, True))
+            lgs.append(eng.logits().copy())
+        ids += eng.decode(ids[-1], 16)
+        outs.append((ids, np.stack(lgs)))
+        loaded.engine.dispose()
+    assert outs[0][0] == outs[1][0]
+    assert np.array_equal(outs[0][1].view(np.uint32), outs[1][1].view(np.uint32))
+
+
 DEPTH_CASES = ["smollm2-135m", "qwen3-0.6b", "gemma3-270m"]
 
 
