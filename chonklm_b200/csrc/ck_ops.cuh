@@ -1575,26 +1575,38 @@ __device__ __forceinline__ void phase_argmax1(const CkDev& D, Smem& sm, int cta,
   const int groups = (D.vocab + 255) / 256;
   const bool pen = st->pen_d > 1.0;
   const float penalty = (float)st->pen_milli / 1000.0f;
-  float* sv = sm.mv.red;
-  uint32_t* si = (uint32_t*)(sm.mv.red + CK_WARPS);
-  for (int g = cta; g < groups; g += ncta) {
-    uint32_t i = (uint32_t)g * 256u + threadIdx.x;
-    float v;
-    uint32_t idx;
-    if (threadIdx.x < 256 && i < (uint32_t)D.vocab) {
-      v = D.logits[i];
-      if (pen && ((D.pen_mask[i >> 5] >> (i & 31)) & 1u)) v = v > 0.f ? v / penalty : v * penalty;
-      idx = i;
-    } else {
-      v = -3.402823e38f;
-      idx = 0xffffffffu;
+  // one warp per 256-logit chunk, 8 logits per lane, every load issued
+  // before the first comparison; the chunk's winner over its logits and
+  // the sentinel (-3.402823e38, 0xffffffff) under `better`, a strict total
+  // order, so the comparison order does not change the result
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int g = cta + warp * ncta; g < groups; g += ncta * CK_WARPS) {
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      const uint32_t i = (uint32_t)g * 256u + 32u * j + lane;
+      v[j] = i < (uint32_t)D.vocab ? D.logits[i] : 0.f;
     }
-    block_argmax(v, idx, sv, si);
-    if (threadIdx.x == 0) {
-      D.cand_val[g] = v;
-      D.cand_idx[g] = idx;
+    float bv = -3.402823e38f;
+    uint32_t bi = 0xffffffffu;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      const uint32_t i = (uint32_t)g * 256u + 32u * j + lane;
+      if (i >= (uint32_t)D.vocab) continue;
+      float x = v[j];
+      if (pen && ((D.pen_mask[i >> 5] >> (i & 31)) & 1u)) x = x > 0.f ? x / penalty : x * penalty;
+      if (better(x, i, bv, bi)) { bv = x; bi = i; }
     }
-    __syncthreads();
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
+    }
+    if (lane == 0) {
+      D.cand_val[g] = bv;
+      D.cand_idx[g] = bi;
+    }
   }
 }
 
