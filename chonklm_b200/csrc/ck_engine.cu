@@ -296,7 +296,7 @@ void assign_tags(ck_engine* h, std::vector<Phase>& ph) {
     const int me = (int)i + 1;
     if (p.kind == PH_EMBED) {
       p.em.tout = wr(p.em.out, me);
-    } else if (p.kind == PH_MATVEC) {
+    } else if (p.kind == PH_MATVEC || p.kind == PH_FNORM) {
       Pro& r = p.mv.pro;
       r.ta = rd(r.a);
       r.tb = (r.kind == PRO_SILU || r.kind == PRO_GELU) ? rd(r.b) : 0;
@@ -383,8 +383,19 @@ void build_schedule(ck_engine* h, bool logits, std::vector<Phase>& out) {
   if (logits) {
     Pro pf = !gemma ? pro_norm(cur, h->final_norm, c.norm_eps)
                     : pro_gemma(h->tmp, h->L[c.layers - 1].post_ffn, cur, other, h->final_norm, c.norm_eps);
-    out.push_back(mk_mv(h, pf, H, {seg(h->head, h->D.logits, nullptr)}));
-    out.back().barrier_after = 1;   // argmax stage 1 reads all logits (plain floats)
+    // the final norm on one CTA, then the LM head as its own launch of the
+    // streaming matvec kernel (k_gemv: dedicated copy warp, 96 KB slots,
+    // block type fixed at compile time), plain floats in and out
+    Phase fn = mk_mv(h, pf, H, {seg(h->head, h->D.logits, nullptr)});
+    fn.kind = PH_FNORM;
+    fn.mv.nseg = 0;
+    fn.grid = 1;
+    out.push_back(fn);
+    Phase hp;
+    memset(&hp, 0, sizeof hp);
+    hp.kind = PH_HEAD;
+    hp.grid = h->sms;
+    out.push_back(hp);
     Phase a1;
     memset(&a1, 0, sizeof a1);
     a1.kind = PH_ARGMAX1;
@@ -609,7 +620,6 @@ const MegaVariant kMegaVariants[] = {
     {CK_TM_KQ, 4, (const void*)k_mega<0, CK_TM_KQ, 4>},
 };
 const void* const kMegaGeneric = (const void*)k_mega<0, CK_TM_ALL, 0>;
-const void* const kMegaExact = (const void*)k_mega<1, CK_TM_ALL, 0>;
 
 unsigned model_type_mask(const ck_engine* h) {
   unsigned m = CK_TM(h->head.L.type);
@@ -632,6 +642,12 @@ const void* mega_kernel(const ck_engine* h) {
   return kMegaGeneric;
 }
 
+// The LM head of a logits step: D.xhead (the final norm's output) -> D.logits.
+void head_launch(ck_engine* h, cudaStream_t s) {
+  const Weight& w = h->head;
+  gv_kernel(w.L.type)<<<h->sms, GV_THREADS, GV_DYN_BYTES, s>>>(w.dev, w.L, w.n, h->D.xhead, h->D.logits, &h->st->err);
+}
+
 int enqueue_phases(ck_engine* h, bool logits, int mode, cudaStream_t s) {
   const std::vector<Phase>& ph = logits ? h->ph_logits : h->ph_prefill;
   if (mode == 2) {
@@ -646,7 +662,8 @@ int enqueue_phases(ck_engine* h, bool logits, int mode, cudaStream_t s) {
   if (mode == 1) {
     const Phase* dph = logits ? h->d_logits : h->d_prefill;
     for (size_t i = 0; i < ph.size(); i++) {
-      if (ph[i].kind == PH_MATVEC) k_mv<<<ph[i].grid, CK_THREADS, CK_DYN_PHASES + sizeof(Phase), s>>>(dph + i, h->Dlaunch);
+      if (ph[i].kind == PH_HEAD) head_launch(h, s);
+      else if (ph[i].kind == PH_MATVEC) k_mv<<<ph[i].grid, CK_THREADS, CK_DYN_PHASES + sizeof(Phase), s>>>(dph + i, h->Dlaunch);
       else if (ph[i].kind == PH_ATTN) k_attn<<<ph[i].grid, CK_THREADS, 0, s>>>(dph + i, h->Dlaunch);
       else k_misc<<<ph[i].grid, CK_THREADS, 0, s>>>(dph + i, h->Dlaunch);
     }
@@ -654,14 +671,20 @@ int enqueue_phases(ck_engine* h, bool logits, int mode, cudaStream_t s) {
     return CK_OK;
   }
   CKC(h, cudaMemsetAsync(&h->st->bar, 0, sizeof(uint32_t), s));
+  // the megakernel runs every phase up to the LM head; the head (k_gemv),
+  // argmax stage 1 and select follow as their own launches
   const Phase* dph = logits ? h->dm_logits : h->dm_prefill;
   int nph = (int)ph.size();
+  for (int i = 0; i < (int)ph.size(); i++)
+    if (ph[i].kind == PH_HEAD) { nph = i; break; }
   void* args[] = {(void*)&dph, (void*)&nph, (void*)&h->Dlaunch};
-  size_t dyn = CK_DYN_PHASES + ph.size() * sizeof(Phase);
-  // k_mega<1> carries the exact sampler; the default instantiation leaves it
-  // out so the greedy / chunk-sampler step keeps its registers and stack.
-  const void* fn = (logits && h->sampler_exact) ? kMegaExact : h->mega_fn;
-  CKC(h, cudaLaunchCooperativeKernel(fn, dim3(h->mega_grid), dim3(CK_THREADS), args, dyn, s));
+  size_t dyn = CK_DYN_PHASES + (size_t)nph * sizeof(Phase);
+  CKC(h, cudaLaunchCooperativeKernel(h->mega_fn, dim3(h->mega_grid), dim3(CK_THREADS), args, dyn, s));
+  for (size_t i = nph; i < ph.size(); i++) {
+    if (ph[i].kind == PH_HEAD) head_launch(h, s);
+    else k_misc<<<ph[i].grid, CK_THREADS, 0, s>>>(dph + i, h->Dlaunch);
+  }
+  CKC(h, cudaGetLastError());
   return CK_OK;
 }
 
@@ -669,10 +692,7 @@ int capture(ck_engine* h, bool logits, int mode, cudaGraphExec_t* out) {
   cudaStream_t s = h->own;
   cudaGraph_t g = nullptr;
   CKC(h, cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
-  const int exact = h->sampler_exact;
-  h->sampler_exact = 0;  // graphs always hold the default k_mega<0>
   int rc = enqueue_phases(h, logits, mode, s);
-  h->sampler_exact = exact;
   cudaError_t e = cudaStreamEndCapture(s, &g);
   if (rc) { if (g) cudaGraphDestroy(g); return rc; }
   if (e != cudaSuccess) return h->fail(CK_ECUDA, "graph capture: %s", cudaGetErrorString(e));
@@ -702,8 +722,7 @@ int launch_step(ck_engine* h, bool logits) {
   }
   h->epoch_steps++;
   cudaGraphExec_t gx = logits ? h->gx_logits[h->mode] : h->gx_prefill[h->mode];
-  // the mode-0 graph holds k_mega<0>: an exact-sampler step launches directly
-  if (gx && !(logits && h->mode == 0 && h->sampler_exact)) {
+  if (gx) {
     CKC(h, cudaGraphLaunch(gx, h->stream));
     return CK_OK;
   }
@@ -916,6 +935,7 @@ int ck_finalize(ck_engine* h) {
   if ((rc = dalloc(h, &h->D.pen_list, (size_t)c.context_length * 4))) return rc;
   if ((rc = dalloc(h, &h->D.pen_mask, (size_t)((c.vocab + 31) / 32) * 4))) return rc;
   if ((rc = dalloc(h, &h->D.logits, (size_t)c.vocab * 4))) return rc;
+  if ((rc = dalloc(h, &h->D.xhead, (size_t)c.hidden * 4))) return rc;
   int groups = (c.vocab + 255) / 256;
   if ((rc = dalloc(h, &h->D.cand_val, (size_t)groups * 4))) return rc;
   if ((rc = dalloc(h, &h->D.cand_idx, (size_t)groups * 4))) return rc;
@@ -972,12 +992,14 @@ int ck_finalize(ck_engine* h) {
     return h->fail(CK_EINVAL, "%zu decode phases exceed the %d-byte descriptor stage", h->ph_logits.size(),
                    CK_PHASE_SMEM_MAX);
   CKC(h, cudaFuncSetAttribute(kMegaGeneric, cudaFuncAttributeMaxDynamicSharedMemorySize, CK_DYN_SMEM_MAX));
-  CKC(h, cudaFuncSetAttribute(kMegaExact, cudaFuncAttributeMaxDynamicSharedMemorySize, CK_DYN_SMEM_MAX));
+  if (!gv_kernel(h->head.L.type)) return h->fail(CK_EINVAL, "LM head block type %d unsupported", h->head.L.type);
+  CKC(h, cudaFuncSetAttribute((const void*)gv_kernel(h->head.L.type), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              GV_DYN_BYTES));
   for (const MegaVariant& v : kMegaVariants)
     CKC(h, cudaFuncSetAttribute(v.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, CK_DYN_SMEM_MAX));
   CKC(h, cudaFuncSetAttribute(k_mv, cudaFuncAttributeMaxDynamicSharedMemorySize, CK_DYN_SMEM_MAX));
   int per_sm = 0;
-  CKC(h, cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kMegaExact, CK_THREADS,
+  CKC(h, cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kMegaGeneric, CK_THREADS,
                                                        CK_DYN_PHASES + h->ph_logits.size() * sizeof(Phase)));
   int want = 1;
   const char* w = getenv("CK_MEGA_CTAS_PER_SM");

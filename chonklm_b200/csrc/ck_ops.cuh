@@ -67,6 +67,7 @@ struct CkDev {
   unsigned long long* trace;  // optional globaltimer stamps (null = off)
   int l2_keep;              // 1: the weights fit L2; stream them evict-last so they stay there
   // exact sampler: per-CTA top-K candidates [cta][CK_SAMPLE_MAX] and counts
+  float* xhead;             // the LM head's input, written by PH_FNORM
   float* xval;
   uint32_t* xidx;
   int* xcnt;
@@ -167,7 +168,10 @@ __device__ __forceinline__ float word_float(unsigned long long w) { return __uin
 
 enum { PRO_COPY = 0, PRO_NORM = 1, PRO_SILU = 2, PRO_GELU = 3, PRO_GEMMA = 4 };
 enum { PH_EMBED = 0, PH_MATVEC = 1, PH_ATTN = 2, PH_ARGMAX1 = 3, PH_ARGMAX2 = 4, PH_SAMPLE = 5, PH_FINISH = 6,
-       PH_SELECT = 7 };
+       PH_SELECT = 7, PH_FNORM = 8, PH_HEAD = 9 };
+// PH_FNORM: the LM head's prologue (final norm) on CTA 0, as plain floats in
+// CkDev::xhead.  PH_HEAD: the LM head itself, xhead -> logits, run by the
+// streaming matvec kernel (k_gemv) as its own launch, never by a phase kernel.
 
 struct Pro {
   int kind;
@@ -1972,6 +1976,15 @@ __device__ __forceinline__ void phase_select(int need_logits, const CkDev& D, Sm
   phase_finish(need_logits, D, 0, ep);
 }
 
+// The LM head's prologue (RMS_NORM_WGSL over the last residual, or Gemma's
+// post-FFN norm + residual add + final norm) on CTA 0, written as plain
+// floats for the streaming head kernel.
+__device__ __forceinline__ void phase_fnorm(const MvPhase& P, SmemMv& s, const CkDev& D, int cta, uint32_t ep) {
+  if (cta != 0) return;
+  build_x(P.pro, P.k, s, cta, ep, &D.st->err, &D.st->abort_flag);
+  for (int i = threadIdx.x; i < P.k; i += CK_THREADS) D.xhead[i] = s.xf[i];
+}
+
 // ---------------------------------------------------------------------------
 template <int EXACT, unsigned TM, int AE>
 __device__ __forceinline__ void run_phase(const Phase* ph, int i, Smem& sm, Ring& R, const CkDev& D, int cta,
@@ -1991,6 +2004,7 @@ __device__ __forceinline__ void run_phase(const Phase* ph, int i, Smem& sm, Ring
     case PH_SAMPLE: phase_sample(D, sm, cta); break;
     case PH_FINISH: phase_finish(p.need_logits, D, cta, ep); break;
     case PH_SELECT: phase_select<EXACT>(p.need_logits, D, sm, cta, ep, ncta); break;
+    case PH_FNORM: phase_fnorm(p.mv, sm.mv, D, cta, ep); break;
   }
 }
 
@@ -2029,6 +2043,7 @@ __global__ void __launch_bounds__(CK_THREADS, 1) k_misc(const Phase* __restrict_
     case PH_SAMPLE: phase_sample(D, sm, blockIdx.x); break;
     case PH_FINISH: phase_finish(p.need_logits, D, blockIdx.x, ep); break;
     case PH_SELECT: phase_select<1>(p.need_logits, D, sm, blockIdx.x, ep, (ph - 1)->grid); break;
+    case PH_FNORM: phase_fnorm(p.mv, sm.mv, D, blockIdx.x, ep); break;
   }
 }
 
