@@ -924,6 +924,18 @@ int ck_finalize(ck_engine* h) {
   // would finish last and hold up the merge
   h->smax = h->sms / c.kv_heads;
   if (h->smax > 64) h->smax = 64;
+  {
+    // The split holding pos merges the splits' partials with 8 loads in
+    // flight per lane and Pw lanes per output element: when one pass covers
+    // every element, up to 8 * Pw splits cost one round trip and more cost
+    // two, so the split count stops there (Qwen3: 16 instead of 18).
+    const int NE = (c.heads / c.kv_heads) * c.head_dim;
+    int pw = 1;
+    while (pw < 32 && 2 * pw * NE <= CK_THREADS) pw *= 2;
+    if (pw * NE <= CK_THREADS && h->smax > 8 * pw) h->smax = 8 * pw;
+    const char* se = getenv("CK_SMAX");
+    if (se && atoi(se) > 0) h->smax = atoi(se);
+  }
   if (h->smax < 1) h->smax = 1;
   if ((rc = dalloc(h, &h->st, sizeof(CkState)))) return rc;
   CKC(h, cudaMemset(h->st, 0, sizeof(CkState)));

@@ -1242,6 +1242,14 @@ __device__ __forceinline__ void attn_merge(const AttnPhase& P, SmemAt& s, int kv
     sm_m[i] = word_float(ml[0]);
     sm_l[i] = word_float(ml[1]);
   }
+  {   // the first accumulators settle in the same wait as the (m, l) pairs
+    const int e = tid / Pw;
+    const int gg = e < NE ? e / hd : 0, d = e % hd;
+    const uint32_t w8[8] = {want, want, want, want, want, want, want, want};
+    settle(x, w8, [&](int j) {
+      return ld_word(pk, ((size_t)(part + j * Pw) * G + gg) * (hd + 2) + 2 + d, P.tout);
+    }, err, abort_flag);
+  }
   __syncthreads();
   for (int gg = warp; gg < G; gg += CK_WARPS) {
     float M = -INFINITY;
@@ -1270,10 +1278,12 @@ __device__ __forceinline__ void attn_merge(const AttnPhase& P, SmemAt& s, int kv
           x[j] = (ok && sp < S) ? ld_word(pk, ((size_t)sp * G + gg) * (hd + 2) + 2 + d, P.tout) : none;
         }
       }
-      const uint32_t w8[8] = {want, want, want, want, want, want, want, want};
-      settle(x, w8, [&](int j) {
-        return ld_word(pk, ((size_t)(sp0 + j * Pw) * G + gg) * (hd + 2) + 2 + d, P.tout);
-      }, err, abort_flag);
+      if (ps > 0 || sp0 != part) {   // the first group settled with the (m, l) pairs
+        const uint32_t w8[8] = {want, want, want, want, want, want, want, want};
+        settle(x, w8, [&](int j) {
+          return ld_word(pk, ((size_t)(sp0 + j * Pw) * G + gg) * (hd + 2) + 2 + d, P.tout);
+        }, err, abort_flag);
+      }
 #pragma unroll
       for (int j = 0; j < 8; j++) {
         const int sp = sp0 + j * Pw;
