@@ -269,13 +269,14 @@ def matvec_report(path, peak):
     return out
 
 
-def phase_profile(eng, layers: int) -> dict:
+def phase_profile(eng, layers: int, start: int) -> dict:
     """CTA 0's view of one megakernel launch of a decode step (ck_trace
     globaltimer stamps around each phase, read after four traced steps): the
     mean duration of each phase kind over the layers.  A phase's time
     includes its wait for the previous phase's slowest producer.  The LM head,
     argmax stage 1 and select run as their own launches after the megakernel."""
     import numpy as np
+    eng.truncate(start)              # the traced steps decode from the prompt end
     eng.trace(True)
     eng.enqueue_decode_steps(4)
     eng.sync()
@@ -580,7 +581,7 @@ def main():
     w1, kv1 = eng.step_bytes()
     bytes_per_token = w0 + 0.5 * (kv0 + kv1)
 
-    phases = phase_profile(eng, S.layers) if (rank == 0 and args.mode == 0) else None
+    phases = phase_profile(eng, S.layers, prompt_len) if (rank == 0 and args.mode == 0) else None
 
     # ---- e2e through generateLlamaWgsl -------------------------------------
     e2e_times = []
@@ -671,7 +672,8 @@ def main():
                 t = json.load(f).get(args.config)
             if t and args.mode == 0:
                 traffic = t["bytes_per_launch"]
-                traffic_note = f"ncu dram__bytes_read+write of one {t['kernel']} launch at position {t['position']}"
+                traffic_note = (f"ncu dram__bytes_read+write of one decode step ({t['kernel']}, the step's "
+                                f"weight- and KV-streaming launches) at position {t['position']}")
         except Exception:
             traffic = None
         cpu = None
