@@ -100,6 +100,7 @@ def lib():
             L.ck_set_sampler.argtypes = [P, I]
             L.ck_set_prefill_gemm.argtypes = [P, I, I]
             L.ck_enqueue_decode_steps.argtypes = [P, I]
+            L.ck_enqueue_decode_steps_sampled.argtypes = [P, I, pp(ck_sampling)]
             L.ck_sync.argtypes = [P]
             L.ck_step_bytes.argtypes = [P, pp(D), pp(D)]
             L.ck_dequant.argtypes = [I, P, S, I, I, P, I]
@@ -239,8 +240,13 @@ class Engine:
         tensor cores, chunk ids per pass (0: the largest)."""
         _check(self._L.ck_set_prefill_gemm(self.h, int(min_tokens), int(chunk)), self.h)
 
-    def enqueue_decode_steps(self, n: int) -> None:
-        _check(self._L.ck_enqueue_decode_steps(self.h, int(n)), self.h)
+    def enqueue_decode_steps(self, n: int, sampling=None) -> None:
+        """n chained decode steps, not synchronised: greedy, or sampling with
+        `sampling` (a ck_sampling from make_sampling)."""
+        if sampling is None:
+            _check(self._L.ck_enqueue_decode_steps(self.h, int(n)), self.h)
+        else:
+            _check(self._L.ck_enqueue_decode_steps_sampled(self.h, int(n), ctypes.byref(sampling)), self.h)
 
     def sync(self) -> None:
         _check(self._L.ck_sync(self.h), self.h)

@@ -1199,6 +1199,19 @@ int ck_enqueue_decode_steps(ck_engine* h, int n) {
   return CK_OK;
 }
 
+int ck_enqueue_decode_steps_sampled(ck_engine* h, int n, const ck_sampling* s) {
+  int rc = pre_step(h);
+  if (rc) return rc;
+  if (h->pos + n > h->cfg.context_length) return h->fail(CK_ECONTEXT, "context exhausted");
+  // chained like ck_decode: each step samples with `s` (draws from its
+  // philox_offset on) and feeds its id to the next step
+  if ((rc = set_params(h, s, 1, s ? s->philox_offset : 0, true))) return rc;
+  for (int i = 0; i < n; i++)
+    if ((rc = launch_step(h, true))) return rc;
+  h->pos += n;
+  return CK_OK;
+}
+
 int ck_sync(ck_engine* h) {
   if (!h) return set_global(CK_EINVAL, "null engine");
   return check_device(h);

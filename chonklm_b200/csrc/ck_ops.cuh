@@ -1686,19 +1686,25 @@ __device__ __forceinline__ void sample_core(const CkDev& D, SmemSm& s) {
       __syncthreads();
     }
   }
+  // n: the finite candidates (they sort before the +inf sentinels), counted
+  // by all threads; the k exponentials are independent, so every thread
+  // takes some (same expression, same values); the fp64 sums, cdf and draw
+  // below stay sequential in the reference's order
+  static_assert(CK_SAMPLE_MAX == 2 * CK_THREADS, "two candidates per thread");
+  const int n = __syncthreads_count(s.val[tid] != INFINITY) + __syncthreads_count(s.val[tid + CK_THREADS] != INFINITY);
+  const int k = st->top_k > 0 ? min(st->top_k, n) : n;
+  const bool draw = st->temperature > 0.0 && k > 0;
+  if (draw) {
+    const double T = st->temperature;
+    const double maxv = -s.val[0];
+    for (int i = tid; i < k; i += CK_THREADS) s.prob[i] = exp((-s.val[i] - maxv) / T);
+  }
+  __syncthreads();
   if (tid == 0) {
-    int n = 0;
-    while (n < NP && s.val[n] != INFINITY) n++;
-    int k = st->top_k > 0 ? min(st->top_k, n) : n;
     uint32_t choice = n > 0 ? s.idx[0] : 0u;
-    if (st->temperature > 0.0 && k > 0) {
-      double T = st->temperature;
-      double maxv = -s.val[0];
+    if (draw) {
       double total = 0.0;
-      for (int i = 0; i < k; i++) {
-        s.prob[i] = exp((-s.val[i] - maxv) / T);
-        total += s.prob[i];
-      }
+      for (int i = 0; i < k; i++) total += s.prob[i];
       double tp = fmin(fmax(st->top_p, 0.0), 1.0);
       int cutoff = k;
       if (tp < 1.0 && total > 0.0) {

@@ -155,6 +155,10 @@ int ck_set_prefill_gemm(ck_engine* h, int min_tokens, int chunk);
  * (benchmark/profiling use).  The first step reads the token already stored
  * at the current position; each step's argmax feeds the next. */
 int ck_enqueue_decode_steps(ck_engine* h, int n);
+/* Same, each step sampling with `s` (null = greedy), the draws numbered from
+ * s->philox_offset as ck_decode numbers them: the sampled configurations'
+ * timed steps (benchmark/profiling use; no reference counterpart). */
+int ck_enqueue_decode_steps_sampled(ck_engine* h, int n, const ck_sampling* s);
 int ck_sync(ck_engine* h);
 /* Host<->device bytes copied so far by the step calls (run_token, prefill,
  * decode, reset, truncate): the e2e transfer count. */

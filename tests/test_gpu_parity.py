@@ -186,6 +186,29 @@ def test_modes_and_prefill_bitwise(tiny_dir, arch):
 
 
 @pytest.mark.parametrize("arch", ["gemma3", "qwen3"])
+def test_enqueued_sampled_steps_match_decode(tiny_dir, arch):
+    """ck_enqueue_decode_steps_sampled (the bench's timed steps) samples and
+    chains exactly as ck_decode (generateLlamaWgsl's device loop): the same
+    draws give the same ids, so the last step's logits are bit-identical."""
+    path = tiny_model(tiny_dir, arch, "q4_k_m")
+    V = _vocab(path)
+    loaded = loadLlamaWgslModel(_def(path, V))
+    eng = loaded.engine.dev
+    prompt = np.random.default_rng(9).integers(0, V, size=10).tolist()
+    s, _ = _lib.make_sampling(1.0, 0.9, 20, 1.0, seed=3, offset=0)
+    first = eng.prefill(prompt, True, s)
+    ids = eng.decode(first, 17, s)
+    lg_decode = eng.logits().copy()
+    eng.truncate(len(prompt))       # the first id stays stored at this position
+    eng.enqueue_decode_steps(16, s)
+    eng.sync()
+    assert eng.position == len(prompt) + 16
+    assert np.array_equal(eng.logits().view(np.uint32), lg_decode.view(np.uint32))
+    assert len(set(ids)) > 1        # the draws did vary
+    loaded.engine.dispose()
+
+
+@pytest.mark.parametrize("arch", ["gemma3", "qwen3"])
 def test_sampling_matches_reference_sampler(tiny_dir, arch):
     """Given the device's own candidate list and the same Philox draw, the
     device sampler picks what sampleFromCandidateBuffer picks."""
