@@ -701,7 +701,9 @@ def main():
                        "l2": ("L2 flushed before every timed step (256 MB write); weights %.0f MB per token %s "
                               "126 MB L2, re-read by each of the step's %d tokens"
                               % (w0 / 1e6, ">" if w0 > 126e6 else "<", gen)),
-                       "parallelism": f"replicas x{world}"},
+                       "parallelism": f"replicas x{world}",
+                       "sampling": (dict(sampling, sampler="chunk maxima (sampleFromCandidateBuffer)")
+                                    if sampling else "greedy")},
             "e2e": {"value": round(e2e_value, 2), "unit": "tok/s",
                     "h2d_bytes_per_step": int(statistics.mean(x[0] for x in e2e_io)),
                     "d2h_bytes_per_step": int(statistics.mean(x[1] for x in e2e_io)),
