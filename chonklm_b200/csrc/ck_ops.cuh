@@ -297,6 +297,7 @@ struct SmemSm {
   double val[CK_SAMPLE_MAX];
   uint32_t idx[CK_SAMPLE_MAX];
   double prob[CK_SAMPLE_MAX];
+  double dtotal;                   // the sampler's fp64 sum of the k weights
   int n;
   // exact sampler (radix select): histogram, warp counts, running bases,
   // per-CTA list offsets
@@ -1700,17 +1701,28 @@ __device__ __forceinline__ void sample_core(const CkDev& D, SmemSm& s) {
     for (int i = tid; i < k; i += CK_THREADS) s.prob[i] = exp((-s.val[i] - maxv) / T);
   }
   __syncthreads();
+  const double tp = fmin(fmax(st->top_p, 0.0), 1.0);
+  if (tid == 0 && draw) {
+    double total = 0.0;
+    for (int i = 0; i < k; i++) total += s.prob[i];
+    s.dtotal = total;
+  }
+  if (draw && tp < 1.0) {   // block-uniform: the cdf terms prob[i] / total, on every thread
+    __syncthreads();
+    const double total = s.dtotal;
+    if (total > 0.0)
+      for (int i = tid; i < k; i += CK_THREADS) s.val[i] = s.prob[i] / total;   // the sorted keys are done with
+    __syncthreads();
+  }
   if (tid == 0) {
     uint32_t choice = n > 0 ? s.idx[0] : 0u;
     if (draw) {
-      double total = 0.0;
-      for (int i = 0; i < k; i++) total += s.prob[i];
-      double tp = fmin(fmax(st->top_p, 0.0), 1.0);
+      const double total = s.dtotal;
       int cutoff = k;
       if (tp < 1.0 && total > 0.0) {
         double cdf = 0.0;
         for (int i = 0; i < k; i++) {
-          cdf += s.prob[i] / total;
+          cdf += s.val[i];
           if (cdf >= tp) { cutoff = i + 1; break; }
         }
       }
