@@ -1667,26 +1667,67 @@ __device__ __forceinline__ void sample_core(const CkDev& D, SmemSm& s) {
   const int tid = threadIdx.x;
   const int NP = CK_SAMPLE_MAX;
   __syncthreads();
-  // bitonic sort by (val, original order) ascending
+  // Bitonic sort by (val, original order) ascending.  Warp w holds elements
+  // e0 = 64 w + lane and e1 = e0 + 32 in registers: compare partners at
+  // distance j <= 32 are in the same warp (j = 32: the same lane), so those
+  // steps exchange by shuffles; each merge level's steps at j >= 64 come
+  // first and go through shared memory, grouped between two barriers
+  // (14 barriers instead of 55).  Pair (lower, upper) ends ascending when
+  // (lower & kk) == 0, descending otherwise.
+  const int lane = tid & 31, warp = tid >> 5;
+  const int e0 = 64 * warp + lane, e1 = e0 + 32;
+  double v0 = s.val[e0], v1 = s.val[e1], o0 = s.prob[e0], o1 = s.prob[e1];
+  uint32_t x0 = s.idx[e0], x1 = s.idx[e1];
+  auto cmpx = [&](double& v, double& o, uint32_t& x, int e, int j, int kk) {
+    const double pv = __shfl_xor_sync(0xffffffffu, v, j), po = __shfl_xor_sync(0xffffffffu, o, j);
+    const uint32_t px = __shfl_xor_sync(0xffffffffu, x, j);
+    const bool mine_less = v < pv || (v == pv && o < po);
+    const bool lower = (e & j) == 0, up = (e & kk) == 0;
+    if (mine_less != (lower == up)) { v = pv; o = po; x = px; }
+  };
   for (int kk = 2; kk <= NP; kk <<= 1) {
-    for (int j = kk >> 1; j > 0; j >>= 1) {
-      for (int i = tid; i < NP; i += CK_THREADS) {
-        int p = i ^ j;
-        if (p > i) {
-          bool up = (i & kk) == 0;
-          double a = s.val[i], b = s.val[p];
-          double oa = s.prob[i], ob = s.prob[p];
-          bool gt = (a > b) || (a == b && oa > ob);
-          if (gt == up) {
-            s.val[i] = b; s.val[p] = a;
-            s.prob[i] = ob; s.prob[p] = oa;
-            uint32_t t = s.idx[i]; s.idx[i] = s.idx[p]; s.idx[p] = t;
+    int j = kk >> 1;
+    if (j >= 64) {
+      s.val[e0] = v0; s.val[e1] = v1; s.prob[e0] = o0; s.prob[e1] = o1; s.idx[e0] = x0; s.idx[e1] = x1;
+      __syncthreads();
+      for (; j >= 64; j >>= 1) {
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+          const int i = h ? e1 : e0, p = i ^ j;
+          if (p > i) {
+            const bool up = (i & kk) == 0;
+            const double a = s.val[i], b = s.val[p];
+            const double oa = s.prob[i], ob = s.prob[p];
+            const bool gt = (a > b) || (a == b && oa > ob);
+            if (gt == up) {
+              s.val[i] = b; s.val[p] = a;
+              s.prob[i] = ob; s.prob[p] = oa;
+              const uint32_t t = s.idx[i]; s.idx[i] = s.idx[p]; s.idx[p] = t;
+            }
           }
         }
+        __syncthreads();
       }
-      __syncthreads();
+      v0 = s.val[e0]; v1 = s.val[e1]; o0 = s.prob[e0]; o1 = s.prob[e1]; x0 = s.idx[e0]; x1 = s.idx[e1];
+    }
+    for (; j > 0; j >>= 1) {
+      if (j == 32) {   // e0 (lower) and e1 in this lane
+        const bool up = (e0 & kk) == 0;
+        const bool gt = v0 > v1 || (v0 == v1 && o0 > o1);
+        if (gt == up) {
+          const double tv = v0, to = o0;
+          const uint32_t tx = x0;
+          v0 = v1; o0 = o1; x0 = x1;
+          v1 = tv; o1 = to; x1 = tx;
+        }
+      } else {
+        cmpx(v0, o0, x0, e0, j, kk);
+        cmpx(v1, o1, x1, e1, j, kk);
+      }
     }
   }
+  s.val[e0] = v0; s.val[e1] = v1; s.prob[e0] = o0; s.prob[e1] = o1; s.idx[e0] = x0; s.idx[e1] = x1;
+  __syncthreads();
   // n: the finite candidates (they sort before the +inf sentinels), counted
   // by all threads; the k exponentials are independent, so every thread
   // takes some (same expression, same values); the fp64 sums, cdf and draw
