@@ -85,6 +85,14 @@ def lib():
             L.or_vcache.argtypes = [P, I]
             L.or_vcache.restype = P
             L.or_destroy.argtypes = [P]
+            L.or_rms_norm.argtypes = [P, P, P, I, F]
+            L.or_add_rms_norm.argtypes = [P, P, P, P, I, F]
+            L.or_rope_store.argtypes = [P, P, P, P, P, I, I, I, I, I, U, I]
+            L.or_qk_norm_rope_store.argtypes = [P, P, P, P, P, P, P, P, I, I, I, I, I, U, F, I]
+            L.or_attention.argtypes = [P, P, P, P, P, I, I, I, I, I, I, F, I]
+            L.or_silu_mul.argtypes = [P, P, P, I]
+            L.or_gelu_tanh_mul.argtypes = [P, P, P, I]
+            L.or_add.argtypes = [P, P, I, I]
             L.or_argmax_stage1.argtypes = [P, I, P, I, U, P, P]
             L.or_argmax_stage2.argtypes = [P, P, I]
             L.or_argmax_stage2.restype = U
