@@ -11,9 +11,15 @@
  *
  * Pinning: the dequantizers are pinned bit-for-bit against gguf-py 0.19.0
  * (llama.cpp's own Python reader of these block formats, whose numpy decode
- * uses the same fp32 operation order) by tests/test_oracle_golden.py.  The
- * rest of the forward pass is parity unpinned: the reference ships no golden
- * vectors and its WebGPU runtime cannot execute on these machines.
+ * uses the same fp32 operation order) by tests/test_oracle_golden.py.  Every
+ * kernel of runToken (matvecs, embeddings, norms, RoPE stores, attention,
+ * activations, residual adds, argmax stages) is pinned against the
+ * reference's own WGSL text, run on the CPU by the oracle/wgsl.py
+ * interpreter (tests/golden/wgsl_golden.npz, tests/test_wgsl_golden.py):
+ * bit for bit where the shader's arithmetic is specified, within a few ulps
+ * through pow / cos / sin / exp / tanh / inverseSqrt.  The graph order of
+ * runToken (:1039-1124) is restated from the TypeScript, which cannot run
+ * here (no JavaScript runtime).
  *
  * Two accumulation modes for matvec / attention dot products:
  *   OR_MODE_WGSL  : 128 per-thread strided partial sums + tree reduction,

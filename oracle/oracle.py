@@ -13,8 +13,10 @@ path (chonklm_b200) never imports it.
   taken from a Philox4x32-10 stream instead of Math.random (:70);
 * restates generateLlamaWgsl (llama-wgsl-runtime.ts:242-314) minus text decode.
 
-Parity status: dequant pinned against gguf-py 0.19.0; forward pass unpinned
-(no reference golden vectors exist; the WebGPU runtime cannot run here).
+Parity status: dequant pinned against gguf-py 0.19.0; every runToken kernel
+pinned against the reference's own WGSL text run by oracle/wgsl.py
+(tests/test_wgsl_golden.py); the graph order and the sampler are restated
+from the TypeScript (no JavaScript runtime here).
 """
 from __future__ import annotations
 
