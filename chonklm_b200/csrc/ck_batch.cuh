@@ -640,22 +640,23 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_bgemm_tc(BGemm G, BStep st, B
 // block table to shared memory, QK-norm + RoPE of the G query heads (into
 // s.qs) and of the new K row (s.kst), and the K/V rows stored into the
 // entry's block at its position.
-template <int E>
+template <int E, int NT = CK_THREADS>
 __device__ __forceinline__ void battn_prologue(const BAttn& P, const BStep& st, SmemAt& s, int* sbt, int t, int kvh,
                                                int pos) {
   constexpr int hd = 32 * E;
+  constexpr int NW = NT / 32;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int G = P.heads / P.kvh, qd = P.heads * hd, kvd = P.kvh * hd;
   const int* bt = st.btab + (size_t)st.slot[t] * st.max_blocks;
-  for (int i = tid; i <= (pos >> 4) && i < 256; i += CK_THREADS) sbt[i] = bt[i];
-  for (int d = tid; d < (hd >> 1); d += CK_THREADS) {
+  for (int i = tid; i <= (pos >> 4) && i < 256; i += NT) sbt[i] = bt[i];
+  for (int d = tid; d < (hd >> 1); d += NT) {
     float sn, cn;
     sincosf((float)pos * P.inv_freq[d], &sn, &cn);
     s.cs[d] = make_float2(cn, sn);
   }
   const float* qsrc = P.q + (size_t)t * qd + (size_t)kvh * G * hd;
-  for (int i = tid; i < G * hd; i += CK_THREADS) s.raw[i] = qsrc[i];
-  for (int d = tid; d < hd; d += CK_THREADS) {
+  for (int i = tid; i < G * hd; i += NT) s.raw[i] = qsrc[i];
+  for (int d = tid; d < hd; d += NT) {
     s.kvw[0][d] = P.k[(size_t)t * kvd + (size_t)kvh * hd + d];
     s.kvw[1][d] = P.v[(size_t)t * kvd + (size_t)kvh * hd + d];
     if (P.kw) s.kvw[3][d] = P.kw[d];
@@ -663,7 +664,7 @@ __device__ __forceinline__ void battn_prologue(const BAttn& P, const BStep& st, 
   }
   __syncthreads();
   if (P.qw) {
-    for (int gg = warp; gg < G + 1; gg += CK_WARPS) {
+    for (int gg = warp; gg < G + 1; gg += NW) {
       const float* src = gg < G ? s.raw + gg * hd : s.kvw[0];
       float ss = 0.f;
       for (int d = lane; d < hd; d += 32) ss += src[d] * src[d];
@@ -674,12 +675,12 @@ __device__ __forceinline__ void battn_prologue(const BAttn& P, const BStep& st, 
   }
   for (int gg = 0; gg < G; gg++)
     rope_head(s.raw + gg * hd, P.qw ? s.kvw[2] : nullptr, P.qw ? s.inv[gg] : 1.f, s.qs + gg * hd, hd, P.interleaved,
-              s.cs, tid, CK_THREADS);
+              s.cs, tid, NT);
   rope_head(s.kvw[0], P.kw ? s.kvw[3] : nullptr, P.kw ? s.inv[G] : 1.f, s.kst, hd, P.interleaved, s.cs, tid,
-            CK_THREADS);
+            NT);
   __syncthreads();
   const size_t cb = (((size_t)sbt[pos >> 4] * P.kvh + kvh) * CK_BLK + (pos & (CK_BLK - 1))) * hd;
-  for (int d = tid; d < hd; d += CK_THREADS) {
+  for (int d = tid; d < hd; d += NT) {
     P.kc[cb + d] = __float2half_rn(s.kst[d]);
     P.vc[cb + d] = __float2half_rn(s.kvw[1][d]);
   }
@@ -787,8 +788,9 @@ __global__ void __launch_bounds__(CK_THREADS, 1) k_battn(BAttn P, BStep st) {
 // flight per round across the CTA), keeping one online softmax per head; the
 // warps' partials are then merged per head.  Same prologue and output as
 // k_battn.  Used for head_dim 64 (E = 2), where it fits two CTAs per SM.
-template <int E, int G>
-__global__ void __launch_bounds__(CK_THREADS, 2) k_battn_g(BAttn P, BStep st) {
+template <int E, int G, int NT = CK_THREADS>
+__global__ void __launch_bounds__(NT, 2 * CK_THREADS / NT) k_battn_g(BAttn P, BStep st) {
+  constexpr int NW = NT / 32;
   constexpr int hd = 32 * E;
   static_assert(G * hd <= CK_HDMAX, "the warps' partials live in SmemAt::wacc");
   const int t = blockIdx.x / P.kvh, kvh = blockIdx.x % P.kvh;
@@ -797,12 +799,12 @@ __global__ void __launch_bounds__(CK_THREADS, 2) k_battn_g(BAttn P, BStep st) {
   pdl_launch();
   __shared__ SmemAt s;
   __shared__ int sbt[256];
-  __shared__ float wm[CK_WARPS * G], wl[CK_WARPS * G], wf[CK_WARPS * G], hl[G];
+  __shared__ float wm[NW * G], wl[NW * G], wf[NW * G], hl[G];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int qd = P.heads * hd;
   const int pos = st.pos[t];
   const int start = (P.window != 0 && pos + 1 > P.window) ? pos + 1 - P.window : 0;
-  battn_prologue<E>(P, st, s, sbt, t, kvh, pos);
+  battn_prologue<E, NT>(P, st, s, sbt, t, kvh, pos);
   float q[G][E], acc[G][E], m[G], l[G];
 #pragma unroll
   for (int g = 0; g < G; g++) {
@@ -818,18 +820,18 @@ __global__ void __launch_bounds__(CK_THREADS, 2) k_battn_g(BAttn P, BStep st) {
     return (((size_t)sbt[p >> 4] * P.kvh + kvh) * CK_BLK + (p & (CK_BLK - 1))) * hd + lane * E;
   };
   constexpr int CH = E <= 4 ? 8 : 4;   // positions of a warp per round
-  for (int p0 = start + warp; p0 < pos; p0 += CH * CK_WARPS) {
+  for (int p0 = start + warp; p0 < pos; p0 += CH * NW) {
     KvRow<E, false> kr[CH], vr[CH];
 #pragma unroll
     for (int j = 0; j < CH; j++) {
-      const int p = p0 + j * CK_WARPS;
+      const int p = p0 + j * NW;
       kv_zero(kr[j]); kv_zero(vr[j]);
       if (p < pos) { kv_load(P.kc, off(p), kr[j]); kv_load(P.vc, off(p), vr[j]); }
     }
 #pragma unroll
     for (int j = 0; j < CH; j += 2) {   // positions grow with j: a pair past pos ends the round
-      if (p0 + j * CK_WARPS < pos) {
-        const bool has1 = p0 + (j + 1) * CK_WARPS < pos;
+      if (p0 + j * NW < pos) {
+        const bool has1 = p0 + (j + 1) * NW < pos;
 #pragma unroll
         for (int g = 0; g < G; g++)
           softmax_pair<E, false>(q[g], kr[j], vr[j], kr[j + 1], vr[j + 1], has1, P.scale, m[g], l[g], acc[g]);
@@ -863,9 +865,9 @@ __global__ void __launch_bounds__(CK_THREADS, 2) k_battn_g(BAttn P, BStep st) {
   __syncthreads();
   if (tid < G) {   // per head: the warps' weights exp(m_w - M) and the merged sum
     float M = -INFINITY;
-    for (int w = 0; w < CK_WARPS; w++) M = fmaxf(M, wm[w * G + tid]);
+    for (int w = 0; w < NW; w++) M = fmaxf(M, wm[w * G + tid]);
     float L = 0.f;
-    for (int w = 0; w < CK_WARPS; w++) {
+    for (int w = 0; w < NW; w++) {
       const float f = wm[w * G + tid] == -INFINITY ? 0.f : expf(wm[w * G + tid] - M);
       wf[w * G + tid] = f;
       L += wl[w * G + tid] * f;
@@ -874,10 +876,10 @@ __global__ void __launch_bounds__(CK_THREADS, 2) k_battn_g(BAttn P, BStep st) {
   }
   __syncthreads();
   const int nch = tc_nch(qd);
-  for (int i = tid; i < G * hd; i += CK_THREADS) {
+  for (int i = tid; i < G * hd; i += NT) {
     const int gg = i / hd, d = i % hd;
     float A = 0.f;
-    for (int w = 0; w < CK_WARPS; w++) A += s.wacc[w * (G * hd) + gg * hd + d] * wf[w * G + gg];
+    for (int w = 0; w < NW; w++) A += s.wacc[w * (G * hd) + gg * hd + d] * wf[w * G + gg];
     const float o = A / hl[gg];
     const int col = (kvh * G + gg) * hd + d;
     const __half h = __float2half_rn(o);
@@ -921,6 +923,7 @@ struct BSeq {
 struct ck_batch {
   ck_engine* h = nullptr;
   int max_seqs = 0, max_blocks = 0, n_blocks = 0;
+  int battn_nt = 256;         // threads of a head_dim-64 attention CTA (CK_BATTN_THREADS=512: the wider form)
   cudaStream_t stream = nullptr;
   std::vector<void*> allocs;
   std::string err;
@@ -1166,7 +1169,11 @@ int batch_enqueue(ck_batch* b, cudaStream_t s) {
     a.eps = c.qk_norm_eps;
     a.scale = (float)(1.0 / sqrt((double)hd));   // ATTN_SCALE (:1711)
     const int grid = b->max_seqs * c.kv_heads, G = c.heads / c.kv_heads;
-    if (hd == 64 && G == 3) CKB(b, launch_pdl(k_battn_g<2, 3>, dim3(grid), dim3(CK_THREADS), s, a, bstep(b)));
+    if (hd == 64 && G == 3 && b->battn_nt == 256)
+      CKB(b, launch_pdl(k_battn_g<2, 3, 256>, dim3(grid), dim3(256), s, a, bstep(b)));
+    else if (hd == 64 && G == 2 && b->battn_nt == 256)
+      CKB(b, launch_pdl(k_battn_g<2, 2, 256>, dim3(grid), dim3(256), s, a, bstep(b)));
+    else if (hd == 64 && G == 3) CKB(b, launch_pdl(k_battn_g<2, 3>, dim3(grid), dim3(CK_THREADS), s, a, bstep(b)));
     else if (hd == 64 && G == 2) CKB(b, launch_pdl(k_battn_g<2, 2>, dim3(grid), dim3(CK_THREADS), s, a, bstep(b)));
     else if (hd == 64) CKB(b, launch_pdl(k_battn<2>, dim3(grid), dim3(CK_THREADS), s, a, bstep(b)));
     else if (hd == 128) CKB(b, launch_pdl(k_battn<4>, dim3(grid), dim3(CK_THREADS), s, a, bstep(b)));
@@ -1215,6 +1222,7 @@ int ck_batch_create(ck_engine* h, int max_seqs, int kv_blocks, ck_batch** out) {
   b->max_seqs = max_seqs;
   b->max_blocks = max_blocks;
   b->n_blocks = kv_blocks > 0 ? kv_blocks : max_seqs * max_blocks;
+  if (const char* e = getenv("CK_BATTN_THREADS")) b->battn_nt = atoi(e) == 512 ? 512 : 256;
   int rc = CK_OK;
   auto bail = [&](int code) {
     std::string m = b->err;
