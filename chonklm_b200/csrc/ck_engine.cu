@@ -620,6 +620,12 @@ const MegaVariant kMegaVariants[] = {
     {CK_TM_KQ, 4, (const void*)k_mega<0, CK_TM_KQ, 4>},
 };
 const void* const kMegaGeneric = (const void*)k_mega<0, CK_TM_ALL, 0>;
+// The generic kernel with the attention's mergers on the top kv_heads CTAs
+// (attn_unit_top) and the phase after the attention on the CTAs below them:
+// for head_dim 64 (the SmolLM2 family), where it decodes 6-10 % faster.  As
+// a run-time switch inside the generic kernel the same code cost the other
+// families 0.5-3 %, so it is an instantiation of its own.
+const void* const kMegaOwnTop = (const void*)k_mega<0, CK_TM_ALL, 0, 1>;
 
 unsigned model_type_mask(const ck_engine* h) {
   unsigned m = CK_TM(h->head.L.type);
@@ -639,6 +645,7 @@ const void* mega_kernel(const ck_engine* h) {
   const unsigned m = model_type_mask(h);
   for (const MegaVariant& v : kMegaVariants)
     if (v.ae == ae && (m & ~v.tm) == 0) return v.fn;
+  if (c.head_dim == 64 && h->mega_grid > 2 * c.kv_heads) return kMegaOwnTop;
   return kMegaGeneric;
 }
 
@@ -1004,6 +1011,7 @@ int ck_finalize(ck_engine* h) {
     return h->fail(CK_EINVAL, "%zu decode phases exceed the %d-byte descriptor stage", h->ph_logits.size(),
                    CK_PHASE_SMEM_MAX);
   CKC(h, cudaFuncSetAttribute(kMegaGeneric, cudaFuncAttributeMaxDynamicSharedMemorySize, CK_DYN_SMEM_MAX));
+  CKC(h, cudaFuncSetAttribute(kMegaOwnTop, cudaFuncAttributeMaxDynamicSharedMemorySize, CK_DYN_SMEM_MAX));
   if (!gv_kernel(h->head.L.type)) return h->fail(CK_EINVAL, "LM head block type %d unsupported", h->head.L.type);
   CKC(h, cudaFuncSetAttribute((const void*)gv_kernel(h->head.L.type), cudaFuncAttributeMaxDynamicSharedMemorySize,
                               GV_DYN_BYTES));
@@ -1022,7 +1030,14 @@ int ck_finalize(ck_engine* h) {
   h->mega_fn = mega_kernel(h);
   for (int l = 0; l < 2; l++) {
     std::vector<Phase> mp = l ? h->ph_logits : h->ph_prefill;
-    for (Phase& p : mp) set_partition(p, h->mega_grid);
+    // kMegaOwnTop: the phase after an attention phase has its rows on the
+    // CTAs below the attention's mergers only
+    const bool own_top = h->mega_fn == kMegaOwnTop && h->cfg.kv_heads * h->smax <= h->mega_grid;
+    for (size_t j = 0; j < mp.size(); j++) {
+      Phase& p = mp[j];
+      const bool below = own_top && j > 0 && mp[j - 1].kind == PH_ATTN;
+      set_partition(p, below ? h->mega_grid - h->cfg.kv_heads : h->mega_grid);
+    }
     Phase** dst = l ? &h->dm_logits : &h->dm_prefill;
     if ((rc = dalloc(h, dst, mp.size() * sizeof(Phase)))) return rc;
     CKC(h, cudaMemcpy(*dst, mp.data(), mp.size() * sizeof(Phase), cudaMemcpyHostToDevice));

@@ -1504,6 +1504,23 @@ __device__ __forceinline__ void prefetch_l2(const void* addr, uint32_t bytes) {
 // Issued one phase early (at the start of the layer's QKV phase): this CTA's
 // attention unit's cache rows [t0, tend) of K and V move into L2 while the
 // projections run, so the unit's first reads do not go to HBM.
+// Megakernel instantiations with OT = 1, when every unit has a CTA of its own: the split holding `pos` (the one that merges, and so
+// finishes last) of kv head h runs on CTA ncta - kvh + h and split s < S - 1
+// on CTA s * kvh + h.  The phase after the attention leaves those top CTAs
+// without rows, so none of its rows waits behind a merge.  False: this CTA
+// has no unit.
+__device__ __forceinline__ bool attn_unit_top(const AttnPhase& P, int S, int cta, int ncta, int& kvh, int& split) {
+  if (cta >= ncta - P.kvh) {
+    kvh = cta - (ncta - P.kvh);
+    split = S - 1;
+    return true;
+  }
+  kvh = cta % P.kvh;
+  split = cta / P.kvh;
+  return split < S - 1;
+}
+
+template <int AE, int OT>
 __device__ __forceinline__ void attn_prefetch(const AttnPhase& P, int cta, int ncta, int pos) {
   if (threadIdx.x != 0) return;
   const int start = (P.window != 0 && pos + 1 > P.window) ? pos + 1 - P.window : 0;
@@ -1512,6 +1529,20 @@ __device__ __forceinline__ void attn_prefetch(const AttnPhase& P, int cta, int n
   if (chunk < CK_MIN_SPLIT) chunk = CK_MIN_SPLIT;
   const int S = (npos + chunk - 1) / chunk;
   const size_t elem = P.kv_f32 ? 4 : 2;
+  if constexpr (OT != 0) {
+    int kvh, split;
+    if (P.kvh * P.smax <= ncta) {
+      if (!attn_unit_top(P, S, cta, ncta, kvh, split)) return;
+      const int t0 = start + split * chunk;
+      const int tend = split == S - 1 ? pos : min(t0 + chunk, pos + 1);
+      if (tend <= t0) return;
+      const size_t off = ((size_t)kvh * P.ctx + t0) * P.hd * elem;
+      const uint32_t bytes = (uint32_t)((size_t)(tend - t0) * P.hd * elem);
+      prefetch_l2((const uint8_t*)P.kc + off, bytes);
+      prefetch_l2((const uint8_t*)P.vc + off, bytes);
+      return;
+    }
+  }
   for (int u = cta; u < P.kvh * P.smax; u += ncta) {
     const int kvh = u % P.kvh, split = u / P.kvh;
     if (split >= S) continue;
@@ -1527,11 +1558,34 @@ __device__ __forceinline__ void attn_prefetch(const AttnPhase& P, int cta, int n
 
 // AE: 0 = head_dim and cache type dispatched at run time; 2 / 4 / 8 = only
 // head_dim 32 * AE with an fp16 cache (the host guarantees it).
-template <int AE = 0>
+template <int AE = 0, int OT = 0>
 __device__ __forceinline__ void phase_attn(const AttnPhase& P, Smem& sm, const CkDev& D, int cta, int ncta, int pos,
                                            unsigned long long* tp, uint32_t ep) {
   int* err = &D.st->err;
   int* ab = &D.st->abort_flag;
+  if constexpr (OT != 0) {
+    if (P.kvh * P.smax <= ncta) {
+      const int start = (P.window != 0 && pos + 1 > P.window) ? pos + 1 - P.window : 0;
+      const int npos = pos - start + 1;
+      int chunk = (npos + P.smax - 1) / P.smax;
+      if (chunk < CK_MIN_SPLIT) chunk = CK_MIN_SPLIT;
+      const int S = (npos + chunk - 1) / chunk;
+      int kvh, split;
+      if (attn_unit_top(P, S, cta, ncta, kvh, split)) {
+        if (P.kv_f32) {
+          if (P.hd == 64) attn_unit<2, true>(P, sm.at, kvh, split, pos, tp, ep, err, ab);
+          else if (P.hd == 128) attn_unit<4, true>(P, sm.at, kvh, split, pos, tp, ep, err, ab);
+          else attn_unit<8, true>(P, sm.at, kvh, split, pos, tp, ep, err, ab);
+        } else {
+          if (P.hd == 64) attn_unit<2, false>(P, sm.at, kvh, split, pos, tp, ep, err, ab);
+          else if (P.hd == 128) attn_unit<4, false>(P, sm.at, kvh, split, pos, tp, ep, err, ab);
+          else attn_unit<8, false>(P, sm.at, kvh, split, pos, tp, ep, err, ab);
+        }
+        __syncthreads();
+      }
+      return;
+    }
+  }
   // split-major: the active split 0 units of every kv head land on
   // different CTAs even when the context needs one split only
   int units = P.kvh * P.smax;
@@ -2055,7 +2109,7 @@ __device__ __forceinline__ void phase_fnorm(const MvPhase& P, SmemMv& s, const C
 }
 
 // ---------------------------------------------------------------------------
-template <int EXACT, unsigned TM, int AE>
+template <int EXACT, unsigned TM, int AE, int OT>
 __device__ __forceinline__ void run_phase(const Phase* ph, int i, Smem& sm, Ring& R, const CkDev& D, int cta,
                                           int ncta, int pos, uint32_t ep) {
   const Phase& p = ph[i];
@@ -2063,11 +2117,11 @@ __device__ __forceinline__ void run_phase(const Phase* ph, int i, Smem& sm, Ring
       !D.trace ? nullptr
       : (i == 2 && cta < 1024) ? D.trace + CK_TRACE_CTA_BASE + cta * 16 + 8
       : (cta == 0 && i < 512) ? D.trace + CK_TRACE_STAGE_BASE + i * 8 : nullptr;
-  if (p.kind == PH_MATVEC && ph[i + 1].kind == PH_ATTN) attn_prefetch(ph[i + 1].at, cta, ncta, pos);
+  if (p.kind == PH_MATVEC && ph[i + 1].kind == PH_ATTN) attn_prefetch<AE, OT>(ph[i + 1].at, cta, ncta, pos);
   switch (p.kind) {
     case PH_EMBED: phase_embed(p.em, D, cta, ncta, pos, ep); break;
     case PH_MATVEC: phase_matvec<TM>(p.mv, sm, R, cta, &D.st->err, &D.st->abort_flag, tp, ep); break;
-    case PH_ATTN: phase_attn<AE>(p.at, sm, D, cta, ncta, pos, tp, ep); break;
+    case PH_ATTN: phase_attn<AE, OT>(p.at, sm, D, cta, ncta, pos, tp, ep); break;
     case PH_ARGMAX1: phase_argmax1<EXACT>(D, sm, cta, ncta); break;
     case PH_ARGMAX2: phase_argmax2(D, sm, cta); break;
     case PH_SAMPLE: phase_sample(D, sm, cta); break;
@@ -2156,8 +2210,9 @@ __device__ __forceinline__ bool grid_sync(CkState* st, unsigned target) {
 // whose outputs are plain.
 // EXACT: the whole-vocabulary sampler is compiled in; TM / AE: the block
 // types and the attention shape compiled in (CK_TM_ALL / 0: all, chosen at
-// run time), see mega_kernel on the host.
-template <int EXACT, unsigned TM, int AE>
+// run time), see mega_kernel on the host; OT: the attention's mergers on the
+// top CTAs (attn_unit_top).
+template <int EXACT, unsigned TM, int AE, int OT = 0>
 __global__ void __launch_bounds__(CK_THREADS, 1) k_mega(const Phase* __restrict__ ph, int nph, CkDev D) {
   __shared__ Smem sm;
   const int pos = D.st->pos;         // constant for the whole step (phase_finish runs last)
@@ -2173,7 +2228,7 @@ __global__ void __launch_bounds__(CK_THREADS, 1) k_mega(const Phase* __restrict_
 #pragma unroll 1
   for (int i = 0; i < nph; i++) {
     if (tr && 2 * i + 1 < CK_TRACE_MV_BASE) D.trace[2 * i] = gtimer();
-    run_phase<EXACT, TM, AE>(sph, i, sm, R, D, blockIdx.x, gridDim.x, pos, ep);
+    run_phase<EXACT, TM, AE, OT>(sph, i, sm, R, D, blockIdx.x, gridDim.x, pos, ep);
     if (tr && 2 * i + 1 < CK_TRACE_MV_BASE) D.trace[2 * i + 1] = gtimer();
     if (ct && i >= 1 && i <= 4) ct[i - 1] = gtimer();
     if (!R.ok) return;
