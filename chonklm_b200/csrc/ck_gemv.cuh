@@ -3,10 +3,13 @@
 // llama-wgsl-runtime.ts:2291-2613, the 151936-row tied head of Qwen3) and
 // any matrix large enough to be bandwidth bound.
 //
-// One CTA per SM; CTA c owns rows [c*n/grid, (c+1)*n/grid).  Warp 15 copies
-// the CTA's rows, a slot at a time, into a ring of GV_NSLOT shared-memory
-// slots (cp.async.bulk into this CTA's own shared memory, completing on the
-// slot's mbarrier, L2 evict-first); warps 0..14 take each slot's rows three at a time per warp.
+// One CTA of 20 warps per SM; CTA c owns rows [c*n/grid, (c+1)*n/grid).
+// The last warp copies the CTA's rows, a slot at a time, into a ring of
+// GV_NSLOT shared-memory slots (cp.async.bulk into this CTA's own shared
+// memory, completing on the slot's mbarrier, L2 evict-first); the other 19
+// warps take each slot's rows GV_RB at a time per warp (20 warps measured
+// 2-5 % faster than 16; a third 64 KB slot in place of two 96 KB ones was
+// slower).
 // Each kernel instance is compiled for one block type, so a unit's decode is
 // straight-line code, and x (quantized per 32 elements into X = hi * 256 +
 // lo, as XUnit describes) sits in shared memory in 16-byte chunks that the
@@ -14,8 +17,10 @@
 #pragma once
 #include "ck_ops.cuh"
 
-#define GV_THREADS 512
-#define GV_NCW 15                 // compute warps
+#ifndef GV_THREADS
+#define GV_THREADS 640
+#endif
+#define GV_NCW (GV_THREADS / 32 - 1)   // compute warps (the last warp copies)
 #define GV_NCT (GV_NCW * 32)
 #ifndef GV_SLOT_BYTES
 #define GV_SLOT_BYTES (96 * 1024)
@@ -330,7 +335,7 @@ __global__ void __launch_bounds__(GV_THREADS, 1) k_gemv(const uint8_t* __restric
     else gv_tile<TYPE>(dyn + (size_t)sl * GV_SLOT_BYTES, L, min(tile_rows, hi - r), r, s, x0, y);
     // this warp is done with the slot (its loads have been consumed): it
     // hands it back on its own and moves on; the copy warp refills the slot
-    // once all 15 have arrived
+    // once every compute warp has arrived
     __syncwarp();
     if (lane == 0) mbar_arrive(empty + sl);
   }
