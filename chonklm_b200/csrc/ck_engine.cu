@@ -400,8 +400,10 @@ void build_schedule(ck_engine* h, bool logits, std::vector<Phase>& out) {
     memset(&a1, 0, sizeof a1);
     a1.kind = PH_ARGMAX1;
     a1.barrier_after = 1;           // select reads every chunk's candidate
+    // one CTA per SM, one warp per 256-logit chunk: a CTA of its own per
+    // chunk kept 15 of its 16 warps idle and took several waves
     a1.grid = (c.vocab + 255) / 256;
-    if (a1.grid > h->sms * 4) a1.grid = h->sms * 4;
+    if (a1.grid > h->sms) a1.grid = h->sms;
     out.push_back(a1);
   }
   Phase f;
